@@ -1,0 +1,491 @@
+"""Benchmark of the MOSS v2 hot path on B200 (one JSON line on rank 0).
+
+Headline workload: the 32-stage residual vector quantizer (encode + decode)
+over 8192 codec frames x 64 dims with 32 codebooks of 1024 x 64, FP32.  One
+step = one pass of the quantizer over one 8192-frame batch per GPU (weak
+scaling: every rank quantizes its own batch, no collective on the data
+path).  The metric is audio seconds per second: each frame is 80 ms of
+48 kHz audio (3840 samples), so one 8192-frame batch is 655.36 s of audio.
+
+  value      device time of the encode kernel only (inputs resident in HBM),
+             L2 flushed between timed steps; max over ranks.
+  e2e        the same metric through the public API with host buffers: every
+             step copies the frames in from pinned host memory and the codes
+             and reconstruction back out.
+  roofline   FP32 FFMA roofline of the encode kernel (algorithmic FLOPs per
+             launch / CUDA-event launch time vs SMs x 128 lanes x 2 x max
+             clock); DRAM traffic from the committed ncu summary.
+  kernels    the other hot-path kernels (residual+LayerNorm, RoPE, SiLU
+             gate, LFQ decode) at their workload sizes vs the measured HBM
+             copy bandwidth, inputs rotated through > L2-sized sets.
+  cpu_baseline  the CPU oracle port of the same quantizer on the host
+             cores (bounded sample).
+
+`--impl reference` times the CPU implementation of the path instead (the
+oracle port, all host threads) on rank 0.
+"""
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(REPO, "fast-moss-tokenizer_b200")
+for _p in (REPO, PKG_DIR):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+FRAMES = 8192
+DIM = 64
+STAGES = 32
+CODES = 1024
+FRAME_SEC = 3840 / 48000  # 80 ms of audio per codec frame
+FLOP_PER_FRAME = STAGES * CODES * DIM * 2  # dot-product multiply-adds
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--no-kernels", action="store_true", help="skip the per-kernel HBM lines")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    return p.parse_args()
+
+
+def rank_info():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def workload(seed=1):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((FRAMES, DIM)).astype(np.float32)
+    books = (rng.standard_normal((STAGES, CODES, DIM)) / 8).astype(np.float32)
+    return x, books
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "sm_max_mhz": 1965.0}, "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary, if one exists."""
+    path = os.path.join(REPO, "profiles", f"{name}.txt")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self, t0, t1):
+        window = [s for t, s in self.samples if t0 <= t <= t1]
+        rows = window if window else [s for _, s in self.samples]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(rows[0][2]), "reasons": sorted(reasons),
+                "samples": len(rows), "in_window": bool(window)}
+
+
+# ---------------------------------------------------------------- CPU oracle
+def cpu_rvq_rate(x, books, seconds=10.0):
+    """Frames per second of the oracle port on all host threads, on a sample
+    sized to about `seconds` of work."""
+    from oracle import oracle as O
+
+    threads = O.max_threads()
+    rows = 64
+    t = time.perf_counter()
+    O.rvq_encode(x[:rows], books, nthreads=threads)
+    dt = time.perf_counter() - t
+    rows = int(min(FRAMES, max(rows, rows * seconds / max(dt, 1e-6))))
+    t = time.perf_counter()
+    O.rvq_encode(x[:rows], books, nthreads=threads)
+    dt = time.perf_counter() - t
+    return rows / dt, threads, rows, dt
+
+
+def run_reference(args):
+    rank, _, world = rank_info()
+    if rank != 0:
+        return
+    x, books = workload()
+    from oracle import oracle as O
+
+    threads = O.max_threads()
+    # size one step to about 5 s of host work
+    rate, _, _, _ = cpu_rvq_rate(x, books, seconds=2.0)
+    rows = int(min(FRAMES, max(64, rate * 5.0)))
+    for _ in range(args.warmup):
+        O.rvq_encode(x[:rows], books, nthreads=threads)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        O.rvq_encode(x[:rows], books, nthreads=threads)
+    dt = time.perf_counter() - t
+    value = rows * args.steps / dt * FRAME_SEC
+    line = {
+        "impl": "reference",
+        "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
+        "value": value, "unit": "audio-sec/sec", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) frames, N(0,1)/8 codebooks",
+        "config": {"workload": f"rvq{STAGES}_encode_decode: {FRAMES} frames x {DIM}, "
+                               f"{STAGES} codebooks x {CODES} x {DIM}, FP32",
+                   "sample_rows_per_step": rows},
+        "cpu_baseline": {"value": value, "unit": "audio-sec/sec", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{rows} of {FRAMES} frames x {STAGES} stages per step"},
+        "e2e": {"value": value, "unit": "audio-sec/sec", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arms
+def time_launches(torch, fn, sets, iters, stream):
+    """Average device time of fn(set) over `iters` launches cycling through
+    `sets` (total size > L2), bracketed by CUDA events on `stream`."""
+    for i in range(3):
+        fn(sets[i % len(sets)])
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(iters):
+        fn(sets[i % len(sets)])
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / iters * 1e-3
+
+
+def kernel_lines(torch, fm, dev, hbm_peak):
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    # config 1: residual + layer scale + LayerNorm, [1,4096,1024] FP32
+    n, rows = 1024, 4096
+    sets = []
+    for _ in range(4):
+        sets.append((torch.randn(1, rows, n, device=dev, generator=g),
+                     torch.randn(1, rows, n, device=dev, generator=g),
+                     torch.empty(1, rows, n, device=dev), torch.empty(1, rows, n, device=dev)))
+    gamma = 1 + 0.1 * torch.randn(n, device=dev, generator=g)
+    beta = 0.1 * torch.randn(n, device=dev, generator=g)
+    ls = 0.01 * torch.randn(n, device=dev, generator=g)
+    from fast_moss_b200 import _lib
+
+    lib = _lib.load()
+    sh = stream.cuda_stream
+
+    def ln(s):
+        _lib.check(lib.moss_residual_layer_norm(
+            s[0].data_ptr(), 0, s[1].data_ptr(), 0, ls.data_ptr(), gamma.data_ptr(),
+            beta.data_ptr(), 1e-5, rows, n, s[2].data_ptr(), s[3].data_ptr(), None, None, sh),
+            "moss_residual_layer_norm")
+
+    t = time_launches(torch, ln, sets, 200, stream)
+    nbytes = 4 * rows * n * 4 + 3 * n * 4
+    out["residual_layer_norm"] = {
+        "shape": [1, rows, n], "us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9,
+        "frac": nbytes / t / 1e9 / hbm_peak, "traffic": profile_traffic("residual_layer_norm")}
+    del sets
+
+    # config 3a: RoPE on q, k [4,16,2048,64] bf16 (phase in-kernel)
+    b, h, tt, d = 4, 16, 2048, 64
+    sets = []
+    for _ in range(4):
+        q = torch.randn(b, h, tt, d, device=dev, generator=g).to(torch.bfloat16)
+        k = torch.randn(b, h, tt, d, device=dev, generator=g).to(torch.bfloat16)
+        sets.append((q, k, torch.empty_like(q), torch.empty_like(k)))
+    offset = torch.zeros(b, dtype=torch.long, device=dev)
+    st = _lib.strides(sets[0][0].stride())
+    import math
+
+    coef = -math.log(10000.0) * 2 / d
+
+    def rope(s):
+        _lib.check(lib.moss_rope(s[0].data_ptr(), s[1].data_ptr(), 1, offset.data_ptr(), 0, coef,
+                                 s[2].data_ptr(), s[3].data_ptr(), b, h, tt, d, st, st, sh),
+                   "moss_rope")
+
+    t = time_launches(torch, rope, sets, 200, stream)
+    nbytes = 4 * b * h * tt * d * 2
+    out["rope"] = {"shape": [b, h, tt, d], "us": t * 1e6, "bytes": nbytes,
+                   "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
+                   "traffic": profile_traffic("rope")}
+    del sets
+
+    # config 3b: SiLU gate + bias, [4,2048,4096] bf16 -> [4,2048,2048]
+    rows, width = 4 * 2048, 4096
+    sets = []
+    for _ in range(3):
+        x = torch.randn(rows, width, device=dev, generator=g).to(torch.bfloat16)
+        sets.append((x, torch.empty(rows, width // 2, device=dev, dtype=torch.bfloat16)))
+    bias = (0.02 * torch.randn(width, device=dev, generator=g)).to(torch.bfloat16)
+
+    def silu(s):
+        _lib.check(lib.moss_gated_act(s[0].data_ptr(), bias.data_ptr(), s[1].data_ptr(), 1, rows,
+                                      width, 0, 1, sh), "moss_gated_act")
+
+    t = time_launches(torch, silu, sets, 200, stream)
+    nbytes = rows * width * 2 + width * 2 + rows * width // 2 * 2
+    out["silu_gate"] = {"shape": [4, 2048, 4096], "us": t * 1e6, "bytes": nbytes,
+                        "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
+                        "traffic": profile_traffic("silu_gate")}
+    del sets
+    torch.cuda.synchronize()
+    return out
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    rank, local_rank, world = rank_info()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    import fast_moss_b200 as fm
+    from fast_moss_b200 import _lib
+
+    lib = _lib.load()
+    peaks, peak_src = measured_peaks()
+    x_np, books_np = workload(seed=1 + rank)
+    books = torch.from_numpy(books_np).to(dev)
+    rvq = fm.ResidualVectorQuantizer(books)
+    x = torch.from_numpy(x_np).to(dev)
+    codes = torch.empty((STAGES, FRAMES), dtype=torch.int32, device=dev)
+    recon = torch.empty((FRAMES, DIM), device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def step():
+        st = lib.moss_rvq_encode(x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(),
+                                 rvq.packed.data_ptr(), rvq.code_norm.data_ptr(),
+                                 rvq.stats.data_ptr(), STAGES, CODES, codes.data_ptr(),
+                                 recon.data_ptr(), None, sh)
+        if st:
+            _lib.check(st, "moss_rvq_encode")
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    for i in range(args.steps):
+        flush.fill_(float(i))  # evict the previous step's data from L2 (untimed)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t1 = time.time()
+    kernel_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
+    # correctness guard on the timed outputs: decode(codes) must equal recon
+    ok = bool(torch.equal(rvq.decode(codes), recon))
+    _lib.check(lib.moss_check_device_error(sh), "device error word")
+
+    # e2e through the public API with host buffers
+    x_host = torch.from_numpy(x_np).pin_memory()
+    codes_host = torch.empty((STAGES, FRAMES), dtype=torch.int32).pin_memory()
+    recon_host = torch.empty((FRAMES, DIM)).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        rvq.encode(x_dev, codes=codes, recon=recon)
+        codes_host.copy_(codes, non_blocking=True)
+        recon_host.copy_(recon, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_steps = max(1, min(args.steps, 200))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    es = torch.cuda.Event(enable_timing=True)
+    ee = torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    ee.synchronize()
+    e2e_s = es.elapsed_time(ee) * 1e-3
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+
+    times = torch.tensor([kernel_s, e2e_s, 0.0 if ok else 1.0], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    kernel_s, e2e_s, bad = times.tolist()
+
+    kernels = None
+    if rank == 0 and not args.no_kernels:
+        kernels = kernel_lines(torch, fm, dev, peaks["hbm_gbs"])
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rate, threads, rows, dt = cpu_rvq_rate(x_np, books_np, seconds=10.0)
+        cpu = {"value": rate * FRAME_SEC, "unit": "audio-sec/sec", "cores": threads,
+               "kind": "port",
+               "sample": f"{rows} of {FRAMES} frames x {STAGES} stages ({dt:.1f} s, oracle "
+                         f"C port, OpenMP)"}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    per_launch = kernel_s / args.steps
+    value = world * FRAMES * args.steps / kernel_s * FRAME_SEC
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    fp32_peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
+    achieved = FRAMES * FLOP_PER_FRAME / per_launch / 1e12
+    traffic = profile_traffic("rvq_encode")
+    line = {
+        "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
+        "value": value,
+        "unit": "audio-sec/sec",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_launch * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) frames, N(0,1)/8 codebooks",
+        "config": {
+            "workload": f"rvq{STAGES}_encode_decode: {FRAMES} frames x {DIM} per GPU, "
+                        f"{STAGES} codebooks x {CODES} x {DIM}, FP32, int32 codes",
+            "frames_per_gpu": FRAMES, "audio_sec_per_frame": FRAME_SEC,
+            "l2": "flushed between timed steps (256 MiB write, untimed)",
+            "parallelism": f"dp{world} (independent frame shards, no collective)",
+        },
+        "e2e": {
+            "value": world * FRAMES * e2e_steps / e2e_s * FRAME_SEC,
+            "unit": "audio-sec/sec",
+            "h2d_bytes_per_step": FRAMES * DIM * 4,
+            "d2h_bytes_per_step": STAGES * FRAMES * 4 + FRAMES * DIM * 4,
+            "api": "ResidualVectorQuantizer.encode (C ABI moss_rvq_encode), pinned host buffers",
+        },
+        "roofline": {
+            "bound": "fp32",
+            "kernel": "rvq_encode_kernel",
+            "achieved": achieved,
+            "peak": fp32_peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / fp32_peak,
+            "traffic": traffic,
+            "peak_source": f"derived: {sms} SMs x 128 FP32 lanes x 2 x {max_mhz:.0f} MHz "
+                           f"(max SM clock of {peak_src} peaks file)",
+            "flop_per_launch": FRAMES * FLOP_PER_FRAME,
+        },
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "outputs_verified": not bad,
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    if kernels is not None:
+        line["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src, **kernels}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

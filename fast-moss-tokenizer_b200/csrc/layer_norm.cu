@@ -1,0 +1,406 @@
+// Residual scale-add and LayerNorm kernels.
+//
+// Residual (fast_moss/v2_pointwise.py:92-98): y = x + u*s, product and sum
+// rounded separately.
+//
+// LayerNorm: the reference normalises with stock nn.LayerNorm on CUDA
+// (fast_moss/v2_runtime.py:259).  For float32 rows whose width n is a
+// multiple of 4 (and 16-byte aligned pointers) PyTorch runs its vectorised
+// layer-norm forward, whose arithmetic is reproduced here operation for
+// operation:
+//   * a block of 128 threads (4 warps of 32) per row; thread j (j = lane +
+//     32*warp) reads float4 vectors j, j+128, j+256, ... and pushes their
+//     elements, in order, through a Welford update with a float count:
+//       delta = v - mean; count += 1; mean = fma(delta, 1/count, mean);
+//       m2 = fma(delta, v - mean, m2)
+//   * a shuffle-down tree (offsets 16..1) inside each warp, then a two-level
+//     tree across the warps (warp w merges warp w+2, then warp 0 merges 1),
+//     each merge of (own B, other A) being
+//       count = cA + cB; coef = 1/count; nA = cA*coef; nB = cB*coef;
+//       mean = fma(nA, meanA, nB*meanB);
+//       m2 = fma(delta*delta*cA, nB, m2A + m2B),  delta = meanB - meanA
+//   * var = m2 / n; rstd = rsqrtf(var + eps);
+//     y = fma(gamma, rstd * (x - mean), beta).
+// The 128-thread block is emulated by ONE warp per row: lane L carries the
+// four Welford states of the virtual threads L, L+32, L+64, L+96 and runs the
+// four shuffle trees side by side, so no shared memory and no block barrier
+// is needed and a CTA streams several rows at once.
+#include "common.cuh"
+
+namespace moss {
+
+struct Welford {
+  float mean;
+  float m2;
+  float count;
+};
+
+__device__ __forceinline__ Welford welford_push(Welford w, float v) {
+  const float delta = __fsub_rn(v, w.mean);
+  const float count = __fadd_rn(w.count, 1.0f);
+  const float mean = __fmaf_rn(delta, __frcp_rn(count), w.mean);
+  const float m2 = __fmaf_rn(delta, __fsub_rn(v, mean), w.m2);
+  return {mean, m2, count};
+}
+
+// Merge of the thread's own state b with a partner state a.
+__device__ __forceinline__ Welford welford_merge(Welford b, Welford a) {
+  const float delta = __fsub_rn(b.mean, a.mean);
+  const float count = __fadd_rn(a.count, b.count);
+  if (count > 0.0f) {
+    const float coef = __frcp_rn(count);
+    const float na = __fmul_rn(a.count, coef);
+    const float nb = __fmul_rn(b.count, coef);
+    const float mean = __fmaf_rn(na, a.mean, __fmul_rn(nb, b.mean));
+    const float m2 =
+        __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), a.count), nb, __fadd_rn(a.m2, b.m2));
+    return {mean, m2, count};
+  }
+  return {0.0f, 0.0f, count};
+}
+
+__device__ __forceinline__ Welford shfl_down_welford(const Welford& w, int offset) {
+  Welford o;
+  o.mean = __shfl_down_sync(0xffffffffu, w.mean, offset);
+  o.m2 = __shfl_down_sync(0xffffffffu, w.m2, offset);
+  o.count = __shfl_down_sync(0xffffffffu, w.count, offset);
+  return o;
+}
+
+// Reduces the four virtual-warp states of every lane to the row statistics
+// (mean, m2) exactly as the 4-warp block would, and broadcasts them.
+__device__ __forceinline__ void reduce_row_stats(Welford (&w)[4], float& mean, float& m2) {
+#pragma unroll
+  for (int offset = 16; offset > 0; offset >>= 1) {
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const Welford other = shfl_down_welford(w[v], offset);
+      w[v] = welford_merge(w[v], other);
+    }
+  }
+  // Cross-warp tree of the emulated block (lane 0 holds each warp result).
+  Welford w0 = welford_merge(w[0], w[2]);
+  const Welford w1 = welford_merge(w[1], w[3]);
+  w0 = welford_merge(w0, w1);
+  mean = __shfl_sync(0xffffffffu, w0.mean, 0);
+  m2 = __shfl_sync(0xffffffffu, w0.m2, 0);
+}
+
+template <int DT>
+__device__ __forceinline__ float4 load4(const void* base, int64_t i4, bool vec_ok) {
+  if constexpr (DT == MOSS_F32) {
+    if (vec_ok) return reinterpret_cast<const float4*>(base)[i4];
+    const float* p = static_cast<const float*>(base) + 4 * i4;
+    return make_float4(p[0], p[1], p[2], p[3]);
+  } else {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + 4 * i4;
+    if (vec_ok) {
+      const uint2 v = reinterpret_cast<const uint2*>(base)[i4];
+      return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                         __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+    }
+    return make_float4(bf16_bits_to_f32(p[0]), bf16_bits_to_f32(p[1]), bf16_bits_to_f32(p[2]),
+                       bf16_bits_to_f32(p[3]));
+  }
+}
+
+__device__ __forceinline__ float scale_add1(float x, float u, float s) {
+  return __fadd_rn(x, __fmul_rn(u, s));
+}
+
+// One warp per row; NV = number of float4 vectors each lane holds (row width
+// n <= 128*NV).  HAS_U selects the fused residual form.
+template <int NV, int XDT, int UDT, bool HAS_U>
+__global__ void __launch_bounds__(256) residual_ln_kernel(
+    const void* __restrict__ x, const void* __restrict__ u, const float* __restrict__ scale,
+    const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int64_t rows,
+    int n, float* __restrict__ residual_out, float* __restrict__ normed_out,
+    float* __restrict__ mean_out, float* __restrict__ rstd_out, bool x_vec, bool u_vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = n >> 2;
+  const int64_t base4 = row * nvec;
+
+  float4 val[NV];
+  Welford w[4];
+#pragma unroll
+  for (int v = 0; v < 4; ++v) w[v] = {0.0f, 0.0f, 0.0f};
+
+  // Issue every load of the row before any arithmetic.
+  float4 xu[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = lane + 32 * v;
+    if (i < nvec) {
+      val[v] = load4<XDT>(x, base4 + i, x_vec);
+      if constexpr (HAS_U) xu[v] = load4<UDT>(u, base4 + i, u_vec);
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = lane + 32 * v;
+    if (i < nvec) {
+      if constexpr (HAS_U) {
+        const float4 s = reinterpret_cast<const float4*>(scale)[i];
+        val[v].x = scale_add1(val[v].x, xu[v].x, s.x);
+        val[v].y = scale_add1(val[v].y, xu[v].y, s.y);
+        val[v].z = scale_add1(val[v].z, xu[v].z, s.z);
+        val[v].w = scale_add1(val[v].w, xu[v].w, s.w);
+        if (residual_out != nullptr) reinterpret_cast<float4*>(residual_out)[base4 + i] = val[v];
+      }
+      Welford& ws = w[v & 3];
+      ws = welford_push(ws, val[v].x);
+      ws = welford_push(ws, val[v].y);
+      ws = welford_push(ws, val[v].z);
+      ws = welford_push(ws, val[v].w);
+    }
+  }
+
+  float mean, m2;
+  reduce_row_stats(w, mean, m2);
+  const float var = __fdiv_rn(m2, static_cast<float>(n));
+  const float rstd = rsqrtf(__fadd_rn(var, eps));
+
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = lane + 32 * v;
+    if (i < nvec) {
+      const float4 g = gamma ? reinterpret_cast<const float4*>(gamma)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+      const float4 bt = beta ? reinterpret_cast<const float4*>(beta)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 o;
+      // gamma * (rstd * (x - mean)) + beta with the outer multiply-add
+      // fused; without gamma the product rstd * (x - mean) itself fuses with
+      // the beta add, so each affine combination has its own expression.
+      if (gamma && beta) {
+        o.x = __fmaf_rn(g.x, __fmul_rn(rstd, __fsub_rn(val[v].x, mean)), bt.x);
+        o.y = __fmaf_rn(g.y, __fmul_rn(rstd, __fsub_rn(val[v].y, mean)), bt.y);
+        o.z = __fmaf_rn(g.z, __fmul_rn(rstd, __fsub_rn(val[v].z, mean)), bt.z);
+        o.w = __fmaf_rn(g.w, __fmul_rn(rstd, __fsub_rn(val[v].w, mean)), bt.w);
+      } else if (gamma) {
+        o.x = __fmul_rn(g.x, __fmul_rn(rstd, __fsub_rn(val[v].x, mean)));
+        o.y = __fmul_rn(g.y, __fmul_rn(rstd, __fsub_rn(val[v].y, mean)));
+        o.z = __fmul_rn(g.z, __fmul_rn(rstd, __fsub_rn(val[v].z, mean)));
+        o.w = __fmul_rn(g.w, __fmul_rn(rstd, __fsub_rn(val[v].w, mean)));
+      } else if (beta) {
+        o.x = __fmaf_rn(rstd, __fsub_rn(val[v].x, mean), bt.x);
+        o.y = __fmaf_rn(rstd, __fsub_rn(val[v].y, mean), bt.y);
+        o.z = __fmaf_rn(rstd, __fsub_rn(val[v].z, mean), bt.z);
+        o.w = __fmaf_rn(rstd, __fsub_rn(val[v].w, mean), bt.w);
+      } else {
+        o.x = __fmul_rn(rstd, __fsub_rn(val[v].x, mean));
+        o.y = __fmul_rn(rstd, __fsub_rn(val[v].y, mean));
+        o.z = __fmul_rn(rstd, __fsub_rn(val[v].z, mean));
+        o.w = __fmul_rn(rstd, __fsub_rn(val[v].w, mean));
+      }
+      reinterpret_cast<float4*>(normed_out)[base4 + i] = o;
+    }
+  }
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = rstd;
+  }
+}
+
+// Plain residual update y = x + u*s over n elements, channel count c.
+template <int XDT, int UDT>
+__global__ void __launch_bounds__(256) scale_add_vec_kernel(const void* __restrict__ x,
+                                                            const void* __restrict__ u,
+                                                            const float* __restrict__ scale,
+                                                            float* __restrict__ y, int64_t n4,
+                                                            int64_t c4) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 xv = load4<XDT>(x, i, true);
+    const float4 uv = load4<UDT>(u, i, true);
+    const float4 s = reinterpret_cast<const float4*>(scale)[i % c4];
+    float4 o;
+    o.x = scale_add1(xv.x, uv.x, s.x);
+    o.y = scale_add1(xv.y, uv.y, s.y);
+    o.z = scale_add1(xv.z, uv.z, s.z);
+    o.w = scale_add1(xv.w, uv.w, s.w);
+    reinterpret_cast<float4*>(y)[i] = o;
+  }
+}
+
+template <int XDT, int UDT>
+__global__ void __launch_bounds__(256) scale_add_scalar_kernel(const void* __restrict__ x,
+                                                               const void* __restrict__ u,
+                                                               const float* __restrict__ scale,
+                                                               float* __restrict__ y, int64_t n,
+                                                               int64_t c) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    y[i] = scale_add1(load_as_f32<XDT>(x, i), load_as_f32<UDT>(u, i), scale[i % c]);
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+template <int NV, int XDT, int UDT, bool HAS_U>
+static void launch_ln(const void* x, const void* u, const float* scale, const float* gamma,
+                      const float* beta, float eps, int64_t rows, int n, float* res,
+                      float* normed, float* mean, float* rstd, bool xv, bool uv,
+                      cudaStream_t s) {
+  constexpr int kRowsPerCta = 8;
+  const int64_t grid = (rows + kRowsPerCta - 1) / kRowsPerCta;
+  residual_ln_kernel<NV, XDT, UDT, HAS_U><<<static_cast<unsigned>(grid), 32 * kRowsPerCta, 0, s>>>(
+      x, u, scale, gamma, beta, eps, rows, n, res, normed, mean, rstd, xv, uv);
+}
+
+template <int XDT, int UDT, bool HAS_U>
+static int dispatch_nv(int nv, const void* x, const void* u, const float* scale,
+                       const float* gamma, const float* beta, float eps, int64_t rows, int n,
+                       float* res, float* normed, float* mean, float* rstd, bool xv, bool uv,
+                       cudaStream_t s) {
+#define MOSS_LN_CASE(K)                                                                       \
+  case K:                                                                                     \
+    launch_ln<K, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean, \
+                                  rstd, xv, uv, s);                                           \
+    return MOSS_OK;
+  switch (nv) {
+    MOSS_LN_CASE(1)
+    MOSS_LN_CASE(2)
+    MOSS_LN_CASE(3)
+    MOSS_LN_CASE(4)
+    MOSS_LN_CASE(5)
+    MOSS_LN_CASE(6)
+    MOSS_LN_CASE(7)
+    MOSS_LN_CASE(8)
+    MOSS_LN_CASE(10)
+    MOSS_LN_CASE(12)
+    MOSS_LN_CASE(16)
+    default:
+      return MOSS_ERR_UNSUPPORTED;
+  }
+#undef MOSS_LN_CASE
+}
+
+static int round_nv(int nv) {
+  if (nv <= 8) return nv;
+  if (nv <= 10) return 10;
+  if (nv <= 12) return 12;
+  if (nv <= 16) return 16;
+  return -1;
+}
+
+static int ln_common(const char* name, const void* x, int x_dtype, const void* u, int u_dtype,
+                     const float* scale, const float* gamma, const float* beta, float eps,
+                     int64_t rows, int64_t n, float* residual_out, float* normed_out,
+                     float* mean, float* rstd, void* stream) {
+  if (rows < 0 || n <= 0) return fail(MOSS_ERR_VALUE, "%s: rows must be >= 0 and n > 0", name);
+  if (x == nullptr || normed_out == nullptr)
+    return fail(MOSS_ERR_VALUE, "%s: null input or output pointer", name);
+  if (x_dtype != MOSS_F32 && x_dtype != MOSS_BF16)
+    return fail(MOSS_ERR_VALUE, "%s: x dtype must be float32 or bfloat16", name);
+  if (u != nullptr && u_dtype != MOSS_F32 && u_dtype != MOSS_BF16)
+    return fail(MOSS_ERR_VALUE, "%s: update dtype must be float32 or bfloat16", name);
+  if (u != nullptr && scale == nullptr)
+    return fail(MOSS_ERR_VALUE, "%s: a residual update needs a channel scale", name);
+  if (n % 4 != 0)
+    return fail(MOSS_ERR_UNSUPPORTED,
+                "%s: width %lld is not a multiple of 4 (PyTorch uses its non-vectorised "
+                "layer norm there)",
+                name, static_cast<long long>(n));
+  if (n > (1 << 24)) return fail(MOSS_ERR_UNSUPPORTED, "%s: width above 2^24", name);
+  if ((gamma && !aligned16(gamma)) || (beta && !aligned16(beta)) || !aligned16(normed_out) ||
+      (residual_out && !aligned16(residual_out)) || (scale && !aligned16(scale)))
+    return fail(MOSS_ERR_UNSUPPORTED,
+                "%s: gamma/beta/scale/outputs must be 16-byte aligned (PyTorch uses its "
+                "non-vectorised layer norm otherwise)",
+                name);
+  if (u == nullptr && x_dtype != MOSS_F32)
+    return fail(MOSS_ERR_VALUE, "%s: plain layer norm takes float32 input", name);
+  if (u == nullptr && !aligned16(x))
+    return fail(MOSS_ERR_UNSUPPORTED, "%s: x must be 16-byte aligned", name);
+  const int nv = round_nv(static_cast<int>((n / 4 + 31) / 32));
+  if (nv < 0)
+    return fail(MOSS_ERR_UNSUPPORTED, "%s: width %lld above the 2048 supported", name,
+                static_cast<long long>(n));
+  if (rows == 0) return MOSS_OK;
+  const bool xv = (x_dtype == MOSS_F32) ? aligned16(x) : ((reinterpret_cast<uintptr_t>(x) & 7u) == 0);
+  const bool uv = u == nullptr ? true
+                               : ((u_dtype == MOSS_F32) ? aligned16(u)
+                                                        : ((reinterpret_cast<uintptr_t>(u) & 7u) == 0));
+  cudaStream_t s = as_stream(stream);
+  const int ni = static_cast<int>(n);
+  int st;
+  if (u == nullptr) {
+    st = dispatch_nv<MOSS_F32, MOSS_F32, false>(nv, x, nullptr, nullptr, gamma, beta, eps, rows,
+                                                ni, nullptr, normed_out, mean, rstd, xv, uv, s);
+  } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_F32) {
+    st = dispatch_nv<MOSS_F32, MOSS_F32, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
+                                               residual_out, normed_out, mean, rstd, xv, uv, s);
+  } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_BF16) {
+    st = dispatch_nv<MOSS_F32, MOSS_BF16, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
+                                                residual_out, normed_out, mean, rstd, xv, uv, s);
+  } else if (x_dtype == MOSS_BF16 && u_dtype == MOSS_F32) {
+    st = dispatch_nv<MOSS_BF16, MOSS_F32, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
+                                                residual_out, normed_out, mean, rstd, xv, uv, s);
+  } else {
+    st = dispatch_nv<MOSS_BF16, MOSS_BF16, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
+                                                 residual_out, normed_out, mean, rstd, xv, uv, s);
+  }
+  if (st != MOSS_OK) return fail(st, "%s: unsupported width", name);
+  return launch_status(name);
+}
+
+}  // namespace moss
+
+using namespace moss;
+
+extern "C" int moss_layer_norm(const float* x, const float* gamma, const float* beta, float eps,
+                               int64_t rows, int64_t n, float* y, float* mean, float* rstd,
+                               void* stream) {
+  return ln_common("moss_layer_norm", x, MOSS_F32, nullptr, MOSS_F32, nullptr, gamma, beta, eps,
+                   rows, n, nullptr, y, mean, rstd, stream);
+}
+
+extern "C" int moss_residual_layer_norm(const void* x, int x_dtype, const void* u, int u_dtype,
+                                        const float* scale, const float* gamma,
+                                        const float* beta, float eps, int64_t rows, int64_t n,
+                                        float* residual_out, float* normed_out, float* mean,
+                                        float* rstd, void* stream) {
+  if (u == nullptr) return fail(MOSS_ERR_VALUE, "moss_residual_layer_norm: update is null");
+  return ln_common("moss_residual_layer_norm", x, x_dtype, u, u_dtype, scale, gamma, beta, eps,
+                   rows, n, residual_out, normed_out, mean, rstd, stream);
+}
+
+extern "C" int moss_scale_add(const void* x, int x_dtype, const void* u, int u_dtype,
+                              const float* scale, float* y, int64_t n, int64_t c, void* stream) {
+  const char* name = "moss_scale_add";
+  if (n < 0 || c <= 0) return fail(MOSS_ERR_VALUE, "%s: n must be >= 0 and c > 0", name);
+  if (n % c != 0) return fail(MOSS_ERR_VALUE, "%s: n is not a multiple of the channel count", name);
+  if ((x_dtype != MOSS_F32 && x_dtype != MOSS_BF16) || (u_dtype != MOSS_F32 && u_dtype != MOSS_BF16))
+    return fail(MOSS_ERR_VALUE, "%s: dtypes must be float32 or bfloat16", name);
+  if (n == 0) return MOSS_OK;
+  if (!x || !u || !scale || !y) return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  cudaStream_t s = as_stream(stream);
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x), ua = reinterpret_cast<uintptr_t>(u);
+  const bool vec = (c % 4 == 0) && aligned16(scale) && aligned16(y) &&
+                   ((x_dtype == MOSS_F32) ? (xa & 15u) == 0 : (xa & 7u) == 0) &&
+                   ((u_dtype == MOSS_F32) ? (ua & 15u) == 0 : (ua & 7u) == 0);
+  const int sms = sm_count();
+  if (vec) {
+    const int64_t n4 = n / 4;
+    int64_t grid = (n4 + 255) / 256;
+    if (grid > static_cast<int64_t>(sms) * 16) grid = static_cast<int64_t>(sms) * 16;
+#define MOSS_SA(XD, UD) \
+  scale_add_vec_kernel<XD, UD><<<static_cast<unsigned>(grid), 256, 0, s>>>(x, u, scale, y, n4, c / 4)
+    if (x_dtype == MOSS_F32 && u_dtype == MOSS_F32) MOSS_SA(MOSS_F32, MOSS_F32);
+    else if (x_dtype == MOSS_F32) MOSS_SA(MOSS_F32, MOSS_BF16);
+    else if (u_dtype == MOSS_F32) MOSS_SA(MOSS_BF16, MOSS_F32);
+    else MOSS_SA(MOSS_BF16, MOSS_BF16);
+#undef MOSS_SA
+  } else {
+    int64_t grid = (n + 255) / 256;
+    if (grid > static_cast<int64_t>(sms) * 16) grid = static_cast<int64_t>(sms) * 16;
+#define MOSS_SA(XD, UD) \
+  scale_add_scalar_kernel<XD, UD><<<static_cast<unsigned>(grid), 256, 0, s>>>(x, u, scale, y, n, c)
+    if (x_dtype == MOSS_F32 && u_dtype == MOSS_F32) MOSS_SA(MOSS_F32, MOSS_F32);
+    else if (x_dtype == MOSS_F32) MOSS_SA(MOSS_F32, MOSS_BF16);
+    else if (u_dtype == MOSS_F32) MOSS_SA(MOSS_BF16, MOSS_F32);
+    else MOSS_SA(MOSS_BF16, MOSS_BF16);
+#undef MOSS_SA
+  }
+  return launch_status(name);
+}

@@ -1,0 +1,239 @@
+// LFQ (eight-channel, cosine-normalised codebook) quantizer kernels.
+//
+// prepare (fast_moss/quantizer_prepare.py:16-58): for each latent row x[8]
+//   total = sum x^2 in one of two fixed orders (see sum_squares), denom =
+//   sqrt(total) clamped below at 1e-12 with NaN passing through, e = x/denom,
+//   twice = 2e, norm = sum e^2 (same order family), every op round-to-nearest.
+//   The "transposed" order applies when b == 1 and t > 1: the reference then
+//   follows PyTorch's strided reduction (four cyclic accumulators, FMA);
+//   otherwise the adjacent pairwise tree of a contiguous row.
+// select (fast_moss/quantizer.py:8-49): distance = (norm - dot) + code_norm,
+//   first NaN wins, else first minimum; int64 index; raw codeword gathered.
+// decode (fast_moss/v2_runtime.py:143-181): prepare + dots + select fused,
+//   dots as a sequential FMA over the 8 channels.
+#include "common.cuh"
+
+#include <math_constants.h>
+
+namespace moss {
+
+// Sum of the 8 pre-rounded values v in the reference's two orders.
+__device__ __forceinline__ float sum8(const float* v, bool transposed) {
+  if (transposed) {
+    const float a = __fadd_rn(v[0], v[4]), b = __fadd_rn(v[1], v[5]);
+    const float c = __fadd_rn(v[2], v[6]), d = __fadd_rn(v[3], v[7]);
+    return __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+  }
+  return __fadd_rn(__fadd_rn(__fadd_rn(v[0], v[1]), __fadd_rn(v[2], v[3])),
+                   __fadd_rn(__fadd_rn(v[4], v[5]), __fadd_rn(v[6], v[7])));
+}
+
+// Sum of squares of x: the transposed order folds channels 4..7 into the
+// accumulators of 0..3 with an FMA before the serial combine.
+__device__ __forceinline__ float sum_squares(const float* x, bool transposed) {
+  float sq[8];
+#pragma unroll
+  for (int d = 0; d < 8; ++d) sq[d] = __fmul_rn(x[d], x[d]);
+  if (transposed) {
+    const float a = __fmaf_rn(x[4], x[4], sq[0]);
+    const float b = __fmaf_rn(x[5], x[5], sq[1]);
+    const float c = __fmaf_rn(x[6], x[6], sq[2]);
+    const float d = __fmaf_rn(x[7], x[7], sq[3]);
+    return __fadd_rn(__fadd_rn(__fadd_rn(a, b), c), d);
+  }
+  return sum8(sq, false);
+}
+
+struct Prepared {
+  float e[8];
+  float twice[8];
+  float norm;
+  float denom;
+};
+
+__device__ __forceinline__ Prepared prepare_row(const float* __restrict__ x, int64_t row,
+                                                int64_t t, bool transposed) {
+  float v[8];
+  const int64_t bi = row / t, ti = row - bi * t;
+#pragma unroll
+  for (int d = 0; d < 8; ++d) v[d] = x[bi * 8 * t + d * t + ti];
+  Prepared p;
+  float denom = __fsqrt_rn(sum_squares(v, transposed));
+  denom = denom < 1.0e-12f ? 1.0e-12f : denom;  // a NaN compares false and stays
+  float esq[8];
+#pragma unroll
+  for (int d = 0; d < 8; ++d) {
+    p.e[d] = __fdiv_rn(v[d], denom);
+    p.twice[d] = __fmul_rn(2.0f, p.e[d]);
+    esq[d] = __fmul_rn(p.e[d], p.e[d]);
+  }
+  p.norm = sum8(esq, transposed);
+  p.denom = denom;
+  return p;
+}
+
+__global__ void __launch_bounds__(128) lfq_prepare_kernel(const float* __restrict__ x, int64_t b,
+                                                          int64_t t, float* __restrict__ e,
+                                                          float* __restrict__ norm,
+                                                          float* __restrict__ twice,
+                                                          float* __restrict__ denom) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t rows = b * t;
+  if (row >= rows) return;
+  const bool transposed = (b == 1 && t > 1);
+  const Prepared p = prepare_row(x, row, t, transposed);
+#pragma unroll
+  for (int d = 0; d < 8; ++d) {
+    const int64_t o = transposed ? d * t + row : row * 8 + d;
+    e[o] = p.e[d];
+    twice[o] = p.twice[d];
+  }
+  norm[row] = p.norm;
+  denom[row] = p.denom;
+}
+
+// Running selection state of one lane: first NaN index and first minimum.
+struct Pick {
+  float best;
+  int64_t best_i;
+  int64_t nan_i;
+};
+
+__device__ __forceinline__ void pick_push(Pick& p, float dist, int64_t j) {
+  if (dist != dist) {
+    if (j < p.nan_i) p.nan_i = j;
+  } else if (dist < p.best) {
+    p.best = dist;
+    p.best_i = j;
+  }
+}
+
+// Warp-wide reduction; every lane returns the selected index.
+__device__ __forceinline__ int64_t pick_reduce(Pick p) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, p.best, m);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, p.best_i, m);
+    const int64_t on = __shfl_xor_sync(0xffffffffu, p.nan_i, m);
+    if (ob < p.best || (ob == p.best && oi < p.best_i)) {
+      p.best = ob;
+      p.best_i = oi;
+    }
+    if (on < p.nan_i) p.nan_i = on;
+  }
+  return p.nan_i != INT64_MAX ? p.nan_i : p.best_i;
+}
+
+// One warp per row; lane L visits codes L, L+32, ...  The initial best index
+// of a lane is its own first code, so a row whose distances are all +inf
+// resolves to code 0 like the reference's first-minimum rule.
+__global__ void __launch_bounds__(256) lfq_select_kernel(
+    const float* __restrict__ dots, const float* __restrict__ row_norm,
+    const float* __restrict__ code_norm, const float* __restrict__ book,
+    const float* __restrict__ latents, int64_t ls0, int64_t ls1, int64_t ls2, int64_t b,
+    int64_t dd, int64_t t, int64_t k, int ste, float* __restrict__ out,
+    int64_t* __restrict__ indices) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= b * t) return;
+  const float n = row_norm[row];
+  Pick p{CUDART_INF_F, lane, INT64_MAX};
+  const float* drow = dots + row * k;
+  for (int64_t j = lane; j < k; j += 32) {
+    pick_push(p, __fadd_rn(__fsub_rn(n, drow[j]), code_norm[j]), j);
+  }
+  const int64_t idx = pick_reduce(p);
+  if (lane == 0) indices[row] = idx;
+  const int64_t bi = row / t, ti = row - bi * t;
+  for (int64_t d = lane; d < dd; d += 32) {
+    const float value = book[idx * dd + d];
+    if (ste) {
+      const float latent = latents[bi * ls0 + d * ls1 + ti * ls2];
+      out[bi * dd * t + d * t + ti] = __fadd_rn(latent, __fsub_rn(value, latent));
+    } else {
+      out[row * dd + d] = value;
+    }
+  }
+}
+
+// Fused decode: prepare + sequential-FMA dots + select + gather.
+__global__ void __launch_bounds__(256) lfq_decode_kernel(
+    const float* __restrict__ x, const float* __restrict__ book_normed,
+    const float* __restrict__ code_norm, const float* __restrict__ weight, int64_t b, int64_t t,
+    int64_t k, float* __restrict__ out, int64_t* __restrict__ indices) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= b * t) return;
+  const Prepared p = prepare_row(x, row, t, b == 1 && t > 1);
+  Pick pk{CUDART_INF_F, lane, INT64_MAX};
+  for (int64_t j = lane; j < k; j += 32) {
+    const float4 c0 = reinterpret_cast<const float4*>(book_normed + j * 8)[0];
+    const float4 c1 = reinterpret_cast<const float4*>(book_normed + j * 8)[1];
+    float dot = __fmul_rn(p.twice[0], c0.x);
+    dot = __fmaf_rn(p.twice[1], c0.y, dot);
+    dot = __fmaf_rn(p.twice[2], c0.z, dot);
+    dot = __fmaf_rn(p.twice[3], c0.w, dot);
+    dot = __fmaf_rn(p.twice[4], c1.x, dot);
+    dot = __fmaf_rn(p.twice[5], c1.y, dot);
+    dot = __fmaf_rn(p.twice[6], c1.z, dot);
+    dot = __fmaf_rn(p.twice[7], c1.w, dot);
+    pick_push(pk, __fadd_rn(__fsub_rn(p.norm, dot), code_norm[j]), j);
+  }
+  const int64_t idx = pick_reduce(pk);
+  if (lane == 0) indices[row] = idx;
+  if (lane < 8) out[row * 8 + lane] = weight[idx * 8 + lane];
+}
+
+}  // namespace moss
+
+using namespace moss;
+
+extern "C" int moss_lfq_prepare(const float* x, int64_t b, int64_t t, float* e, float* norm,
+                                float* twice, float* denom, void* stream) {
+  const char* name = "moss_lfq_prepare";
+  if (b < 1 || t < 1) return fail(MOSS_ERR_VALUE, "%s: expected nonempty B,8,T latents", name);
+  if (b * 8 * t > 2147483647LL) return fail(MOSS_ERR_VALUE, "%s: more than 2^31-1 elements", name);
+  if (!x || !e || !norm || !twice || !denom) return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  const int64_t rows = b * t;
+  lfq_prepare_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, as_stream(stream)>>>(
+      x, b, t, e, norm, twice, denom);
+  return launch_status(name);
+}
+
+extern "C" int moss_lfq_select(const float* dots, const float* row_norm, const float* code_norm,
+                               const float* codebook, const float* latents,
+                               const int64_t* latent_strides, int64_t b, int64_t d, int64_t t,
+                               int64_t k, int straight_through, float* out, int64_t* indices,
+                               void* stream) {
+  const char* name = "moss_lfq_select";
+  if (b < 0 || d < 1 || t < 0 || k < 1 || k > 65536)
+    return fail(MOSS_ERR_VALUE, "%s: incompatible quantizer shapes or unsupported codebook size", name);
+  if (b * t == 0) return MOSS_OK;
+  if (!dots || !row_norm || !code_norm || !codebook || !out || !indices)
+    return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  int64_t ls[3] = {0, 0, 0};
+  if (straight_through) {
+    if (!latents || !latent_strides) return fail(MOSS_ERR_VALUE, "%s: STE needs latents", name);
+    for (int i = 0; i < 3; ++i) ls[i] = latent_strides[i];
+  }
+  const int64_t rows = b * t;
+  lfq_select_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, as_stream(stream)>>>(
+      dots, row_norm, code_norm, codebook, latents, ls[0], ls[1], ls[2], b, d, t, k,
+      straight_through, out, indices);
+  return launch_status(name);
+}
+
+extern "C" int moss_lfq_decode(const float* x, const float* book_normed, const float* code_norm,
+                               const float* weight, int64_t b, int64_t t, int64_t k, float* out,
+                               int64_t* indices, void* stream) {
+  const char* name = "moss_lfq_decode";
+  if (b < 1 || t < 1 || k < 1 || k > 65536)
+    return fail(MOSS_ERR_VALUE, "%s: expected nonempty B,8,T latents and 1..65536 codes", name);
+  if (!x || !book_normed || !code_norm || !weight || !out || !indices)
+    return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  if (!aligned16(book_normed)) return fail(MOSS_ERR_VALUE, "%s: normalised book must be 16-byte aligned", name);
+  const int64_t rows = b * t;
+  lfq_decode_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, as_stream(stream)>>>(
+      x, book_normed, code_norm, weight, b, t, k, out, indices);
+  return launch_status(name);
+}

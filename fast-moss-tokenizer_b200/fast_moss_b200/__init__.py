@@ -1,0 +1,40 @@
+"""B200-native hot path of the MOSS Audio Tokenizer v2 codec.
+
+Drop-in for the data-parallel hot path of fast_moss (kadirnar/fast-moss-tokenizer):
+the same kernel-level functions (`rotate`, `scale_add`, `select`, `prepare`)
+backed by hand-written sm_100a CUDA kernels in libfast_moss_b200.so, plus
+the fused forms (residual + LayerNorm, in-kernel RoPE phase, gated
+activation, fused LFQ decode, the whole multi-stage residual VQ in one
+kernel).
+"""
+
+from . import _lib
+from .quantizer import decode_latents, select
+from .quantizer_prepare import prepare
+from .rvq import ResidualVectorQuantizer
+from .v2_pointwise import (
+    gated_activation,
+    layer_norm,
+    residual_layer_norm,
+    rope,
+    rotate,
+    scale_add,
+)
+
+__all__ = [
+    "rotate",
+    "rope",
+    "scale_add",
+    "layer_norm",
+    "residual_layer_norm",
+    "gated_activation",
+    "select",
+    "decode_latents",
+    "prepare",
+    "ResidualVectorQuantizer",
+]
+
+
+def library_path():
+    """Path of the native library that every op of this package calls."""
+    return _lib.LIB_PATH

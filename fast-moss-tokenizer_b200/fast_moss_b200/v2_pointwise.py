@@ -1,0 +1,240 @@
+"""Pointwise hot-path ops on B200: residual, LayerNorm, RoPE, gated activation.
+
+`rotate` and `scale_add` keep the names, argument meaning, validation and
+exception types of fast_moss/v2_pointwise.py (rotate :50-89, scale_add
+:101-122); the remaining functions are the fused forms the optimized
+transformer layer uses.  Every op launches a kernel of libfast_moss_b200 on
+the current CUDA stream; there is no other implementation behind them.
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def rotate(q, k, cos, sin):
+    """Interleaved-pair rotation of q and k by FP32 tables [B,T,D/2].
+
+    Returns contiguous B,H,T,D tensors of q's dtype (reference
+    fast_moss/v2_pointwise.py:50-89).
+    """
+    if q.ndim != 4 or q.shape != k.shape or q.shape[-1] < 2 or q.shape[-1] % 2:
+        raise ValueError("Expected equal B,H,T,even-D rotary inputs")
+    b, h, t, d = q.shape
+    if (
+        q.dtype not in _DTYPES
+        or k.dtype != q.dtype
+        or cos.dtype != torch.float32
+        or sin.dtype != torch.float32
+        or not q.is_cuda
+        or any(x.device != q.device for x in (k, cos, sin))
+        or cos.shape != (b, t, d // 2)
+        or sin.shape != cos.shape
+        or not cos.is_contiguous()
+        or not sin.is_contiguous()
+    ):
+        raise ValueError(
+            "Expected same-device BF16/FP32 Q/K and contiguous FP32 rotary tables"
+        )
+    oq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    ok = torch.empty_like(oq)
+    if q.numel():
+        with torch.cuda.device(q.device):
+            _lib.call(
+                "moss_rotate", q.data_ptr(), k.data_ptr(), _DTYPES[q.dtype], cos.data_ptr(),
+                sin.data_ptr(), oq.data_ptr(), ok.data_ptr(), b, h, t, d,
+                _lib.strides(q.stride()), _lib.strides(k.stride()), _stream(q.device))
+    return oq, ok
+
+
+def rope(q, k, offset, max_period):
+    """Rotary embedding with the phase computed inside the kernel.
+
+    Same result as the reference's patched rotary forward
+    (fast_moss/v2_runtime.py:209-224): freq = exp(arange(d/2) * c) with
+    c = float32(-ln(max_period) * 2 / d), phase = freq * (offset + t),
+    cos/sin of the phase, then `rotate` -- without materialising the tables.
+    offset: [B] integer or float tensor on q's device.
+    """
+    if q.ndim != 4 or q.shape != k.shape or q.shape[-1] < 2 or q.shape[-1] % 2:
+        raise ValueError("Expected equal B,H,T,even-D rotary inputs")
+    b, h, t, d = q.shape
+    if (
+        q.dtype not in _DTYPES
+        or k.dtype != q.dtype
+        or not q.is_cuda
+        or k.device != q.device
+        or offset.device != q.device
+        or offset.numel() != b
+    ):
+        raise ValueError("Expected same-device BF16/FP32 Q/K and a per-batch offset")
+    if offset.dtype == torch.int64:
+        odt = 0
+    elif offset.dtype == torch.int32:
+        odt = 1
+    else:
+        odt = 2
+        offset = offset.float()
+    offset = offset.contiguous()
+    coef = -math.log(max_period) * 2 / d
+    oq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    ok = torch.empty_like(oq)
+    if q.numel():
+        with torch.cuda.device(q.device):
+            _lib.call(
+                "moss_rope", q.data_ptr(), k.data_ptr(), _DTYPES[q.dtype], offset.data_ptr(), odt,
+                coef, oq.data_ptr(), ok.data_ptr(), b, h, t, d, _lib.strides(q.stride()),
+                _lib.strides(k.stride()), _stream(q.device))
+    return oq, ok
+
+
+def scale_add(x, update, scale):
+    """Residual update x + update * scale (FP32 out, no FMA).
+
+    Reference fast_moss/v2_pointwise.py:101-122.  Non-contiguous inputs are
+    made contiguous first (the arithmetic is elementwise, so the result is
+    the same as the reference's eager path for them).
+    """
+    if (
+        x.shape != update.shape
+        or scale.shape != (x.shape[-1],)
+        or x.dtype not in _DTYPES
+        or update.dtype not in _DTYPES
+        or scale.dtype != torch.float32
+        or not x.is_cuda
+        or update.device != x.device
+        or scale.device != x.device
+    ):
+        raise ValueError(
+            "Expected equal BF16/FP32 residuals and same-device FP32 channel scale"
+        )
+    x, update, scale = x.contiguous(), update.contiguous(), scale.contiguous()
+    out = torch.empty(x.shape, device=x.device, dtype=torch.float32)
+    if x.numel():
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "moss_scale_add", x.data_ptr(), _DTYPES[x.dtype], update.data_ptr(),
+                _DTYPES[update.dtype], scale.data_ptr(), out.data_ptr(), x.numel(),
+                x.shape[-1], _stream(x.device))
+    return out
+
+
+def _check_norm_params(x, weight, bias):
+    n = x.shape[-1]
+    for p in (weight, bias):
+        if p is not None and (
+            p.shape != (n,) or p.dtype != torch.float32 or p.device != x.device
+            or not p.is_contiguous()
+        ):
+            raise ValueError("Expected contiguous same-device FP32 LayerNorm parameters")
+
+
+def layer_norm(x, weight, bias, eps=1e-5, *, return_stats=False):
+    """FP32 LayerNorm over the last dim, bit-identical to torch's CUDA op.
+
+    Raises _lib.UnsupportedError for widths PyTorch would not vectorise
+    (n % 4 != 0) or misaligned buffers.
+    """
+    if x.dtype != torch.float32 or not x.is_cuda or x.ndim < 1:
+        raise ValueError("Expected a CUDA FP32 tensor")
+    _check_norm_params(x, weight, bias)
+    x = x.contiguous()
+    n = x.shape[-1]
+    rows = x.numel() // n if n else 0
+    y = torch.empty_like(x)
+    mean = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
+    if x.numel():
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "moss_layer_norm", x.data_ptr(), weight.data_ptr() if weight is not None else None,
+                bias.data_ptr() if bias is not None else None, float(eps), rows, n, y.data_ptr(),
+                mean.data_ptr() if mean is not None else None,
+                rstd.data_ptr() if rstd is not None else None, _stream(x.device))
+    return (y, mean, rstd) if return_stats else y
+
+
+def residual_layer_norm(x, update, scale, weight, bias, eps=1e-5, *, write_residual=True,
+                        return_stats=False):
+    """Fused `r = scale_add(x, update, scale)` and `LayerNorm(r)` in one pass.
+
+    Returns (r, normed) -- r is None when write_residual is False -- plus
+    (mean, rstd) when return_stats.  Same bits as the reference's
+    scale_add followed by torch's CUDA layer norm.
+    """
+    if (
+        x.shape != update.shape
+        or scale.shape != (x.shape[-1],)
+        or x.dtype not in _DTYPES
+        or update.dtype not in _DTYPES
+        or scale.dtype != torch.float32
+        or not x.is_cuda
+        or update.device != x.device
+        or scale.device != x.device
+    ):
+        raise ValueError(
+            "Expected equal BF16/FP32 residuals and same-device FP32 channel scale"
+        )
+    _check_norm_params(x, weight, bias)
+    x, update, scale = x.contiguous(), update.contiguous(), scale.contiguous()
+    n = x.shape[-1]
+    rows = x.numel() // n if n else 0
+    res = torch.empty(x.shape, device=x.device, dtype=torch.float32) if write_residual else None
+    y = torch.empty(x.shape, device=x.device, dtype=torch.float32)
+    mean = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
+    if x.numel():
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "moss_residual_layer_norm", x.data_ptr(), _DTYPES[x.dtype], update.data_ptr(),
+                _DTYPES[update.dtype], scale.data_ptr(),
+                weight.data_ptr() if weight is not None else None,
+                bias.data_ptr() if bias is not None else None, float(eps), rows, n,
+                res.data_ptr() if res is not None else None, y.data_ptr(),
+                mean.data_ptr() if mean is not None else None,
+                rstd.data_ptr() if rstd is not None else None, _stream(x.device))
+    if return_stats:
+        return res, y, mean, rstd
+    return res, y
+
+
+_ACTS = {"silu": _lib.ACT_SILU, "gelu": _lib.ACT_GELU_ERF, "gelu_tanh": _lib.ACT_GELU_TANH}
+
+
+def gated_activation(x, bias=None, activation="silu", gated=True):
+    """Bias + activation (+ gate) with torch's per-op rounding.
+
+    gated: act(x[..., :w] + b[:w]) * (x[..., w:] + b[w:]) with w = width/2;
+    otherwise act(x + b).  x: BF16 or FP32 CUDA tensor, bias of x's dtype.
+    """
+    if activation not in _ACTS:
+        raise ValueError(f"Unknown activation {activation!r}")
+    if x.dtype not in _DTYPES or not x.is_cuda or x.ndim < 1:
+        raise ValueError("Expected a CUDA BF16/FP32 tensor")
+    width = x.shape[-1]
+    if gated and width % 2:
+        raise ValueError("Gated activation needs an even last dimension")
+    if bias is not None and (
+        bias.shape != (width,) or bias.dtype != x.dtype or bias.device != x.device
+    ):
+        raise ValueError("Expected a same-device bias of x's dtype and width")
+    x = x.contiguous()
+    bias = bias.contiguous() if bias is not None else None
+    out_w = width // 2 if gated else width
+    y = torch.empty(x.shape[:-1] + (out_w,), device=x.device, dtype=x.dtype)
+    rows = x.numel() // width if width else 0
+    if x.numel():
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "moss_gated_act", x.data_ptr(), bias.data_ptr() if bias is not None else None,
+                y.data_ptr(), _DTYPES[x.dtype], rows, width, _ACTS[activation], 1 if gated else 0,
+                _stream(x.device))
+    return y

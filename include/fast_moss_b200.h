@@ -1,0 +1,230 @@
+/*
+ * fast_moss_b200.h -- C ABI of the B200 (sm_100a) kernels for the MOSS Audio
+ * Tokenizer v2 data-parallel hot path.
+ *
+ * Conventions shared by every entry point:
+ *   - All tensor pointers are DEVICE pointers owned by the caller; nothing is
+ *     allocated inside a call and nothing is freed.
+ *   - Sizes are int64_t element counts; strides are int64_t element strides.
+ *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
+ *     stream.  Every call is stream-ordered, never synchronises the host and is
+ *     therefore legal inside CUDA-graph capture.
+ *   - Return value: MOSS_OK (0) on success, otherwise a status code below; a
+ *     human-readable message for the calling thread is in moss_last_error().
+ *     The Python host layer maps MOSS_ERR_VALUE -> ValueError and the others
+ *     -> RuntimeError, the same exception classes the reference raises.
+ *   - Calls on distinct streams are independent (no shared mutable state).
+ *
+ * Dtype codes: MOSS_F32 = float32, MOSS_BF16 = bfloat16 (stored as uint16).
+ *
+ * Each declaration names the reference function (path within the reference
+ * project, file:line) whose behaviour it reproduces.
+ */
+#ifndef FAST_MOSS_B200_H
+#define FAST_MOSS_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOSS_API __attribute__((visibility("default")))
+#else
+#define MOSS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOSS_OK 0
+#define MOSS_ERR_VALUE 1       /* bad shape / dtype / stride / alignment  */
+#define MOSS_ERR_UNSUPPORTED 2 /* valid input this kernel does not cover  */
+#define MOSS_ERR_CUDA 3        /* kernel launch or device error           */
+#define MOSS_ERR_TIMEOUT 4     /* a bounded device-side wait ran out      */
+
+#define MOSS_F32 0
+#define MOSS_BF16 1
+
+#define MOSS_ACT_SILU 0
+#define MOSS_ACT_GELU_ERF 1
+#define MOSS_ACT_GELU_TANH 2
+
+/* Library ABI version (major*100 + minor). */
+MOSS_API int moss_version(void);
+
+/* Message describing the last non-OK status returned on this host thread. */
+MOSS_API const char* moss_last_error(void);
+
+/* Reads and clears the device-side error word that bounded waits set when
+ * they give up (MOSS_ERR_TIMEOUT).  Synchronises `stream`; not for use inside
+ * graph capture. */
+MOSS_API int moss_check_device_error(void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Residual update with per-channel layer scale.
+ * Replaces fast_moss/v2_pointwise.py:92-122 (`_scale_add` / `scale_add`):
+ *   y[i] = float(x[i]) + float(u[i]) * scale[i % c]
+ * with the product and the sum rounded separately (no FMA), y float32.
+ * x, u contiguous with n elements, scale contiguous [c], n % c == 0.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_scale_add(const void* x, int x_dtype, const void* u, int u_dtype,
+                   const float* scale, float* y, int64_t n, int64_t c,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------
+ * LayerNorm over the last dimension, float32, identical to the arithmetic of
+ * PyTorch's CUDA vectorised layer-norm forward that the reference calls
+ * through nn.LayerNorm (fast_moss/v2_runtime.py:259, type-checked at :330).
+ * x [rows, n] contiguous, n % 4 == 0, gamma/beta [n] 16-byte aligned (NULL
+ * gamma => 1, NULL beta => 0).  mean/rstd [rows] are optional (NULL = skip).
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_layer_norm(const float* x, const float* gamma, const float* beta,
+                    float eps, int64_t rows, int64_t n, float* y, float* mean,
+                    float* rstd, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused residual + layer scale + LayerNorm: one pass computes
+ *   residual = x + u * scale          (as moss_scale_add)
+ *   normed   = LayerNorm(residual)    (as moss_layer_norm)
+ * Replaces the pair `scale_add(residual, update, scale)` followed by the next
+ * `norm(x)` in the patched transformer layer (fast_moss/v2_runtime.py:254-276).
+ * residual_out may be NULL when only the normalised output is needed.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_residual_layer_norm(const void* x, int x_dtype, const void* u,
+                             int u_dtype, const float* scale,
+                             const float* gamma, const float* beta, float eps,
+                             int64_t rows, int64_t n, float* residual_out,
+                             float* normed_out, float* mean, float* rstd,
+                             void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rotary embedding on q and k with caller-supplied tables.
+ * Replaces fast_moss/v2_pointwise.py:50-89 (`_rotate` / `rotate`):
+ *   o[2p]   = q[2p]*cos - q[2p+1]*sin
+ *   o[2p+1] = q[2p]*sin + q[2p+1]*cos     (float32, no FMA)
+ * q, k: [b,h,t,d] with arbitrary element strides (q_strides/k_strides: 4
+ * int64 each, host memory); cos/sin: contiguous float32 [b,t,d/2];
+ * oq/ok: contiguous [b,h,t,d] of the input dtype (MOSS_F32 or MOSS_BF16).
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rotate(const void* q, const void* k, int dtype, const float* cos_t,
+                const float* sin_t, void* oq, void* ok, int64_t b, int64_t h,
+                int64_t t, int64_t d, const int64_t* q_strides,
+                const int64_t* k_strides, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Rotary embedding with the phase tables computed inside the kernel.
+ * Replaces the patched rotary forward fast_moss/v2_runtime.py:186-224:
+ *   freq[j]  = expf(j * freq_coef)                 (freq_coef = float32 of
+ *                                                   -ln(max_period)*2/d)
+ *   ts       = float(offset[b]) + t
+ *   phase    = freq[j] * ts ; cos = cosf(phase) ; sin = sinf(phase)
+ * followed by the rotation of moss_rotate.  offset: device pointer to b
+ * values of dtype offset_dtype (0 = int64, 1 = int32, 2 = float32).
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rope(const void* q, const void* k, int dtype, const void* offset,
+              int offset_dtype, float freq_coef, void* oq, void* ok, int64_t b,
+              int64_t h, int64_t t, int64_t d, const int64_t* q_strides,
+              const int64_t* k_strides, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Bias + gated activation, bf16 or float32 in and out.
+ * No kernel in the reference (its FFN activation is upstream model code);
+ * this is the eager-PyTorch chain it replaces, one rounding per torch op:
+ *   h = x + bias                      (rounded to dtype)
+ *   gated:   y = act(h[:, :w]) * h[:, w:]   (each op rounded to dtype)
+ *   ungated: y = act(h)
+ * x [rows, width], bias [width] (or NULL), y [rows, width/2] if gated.
+ * act: MOSS_ACT_SILU, MOSS_ACT_GELU_ERF, MOSS_ACT_GELU_TANH.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_gated_act(const void* x, const void* bias, void* y, int dtype,
+                   int64_t rows, int64_t width, int act, int gated,
+                   void* stream);
+
+/* ---------------------------------------------------------------------------
+ * LFQ latent preparation for eight-channel latents x [b,8,t] (contiguous).
+ * Replaces fast_moss/quantizer_prepare.py:111-157 (`prepare`, kernel source
+ * :16-58): denom = max(sqrt(sum x^2), 1e-12) (NaN-propagating), e = x/denom,
+ * twice = 2e, norm = sum e^2, with the reference's summation orders.
+ * Layout of e/twice: [8,t] transposed (column j = row j) when b == 1 and
+ * t > 1, else [b*t, 8].  norm, denom: [b*t].
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_lfq_prepare(const float* x, int64_t b, int64_t t, float* e,
+                     float* norm, float* twice, float* denom, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Nearest-codeword selection from precomputed dot products.
+ * Replaces fast_moss/quantizer.py:52-108 (`_select` / `select`):
+ *   distance = (row_norm - dots) + code_norm ; the first NaN wins, otherwise
+ *   the first minimum ; indices int64 ; out = codebook[index].
+ * dots [b*t, k], row_norm [b*t], code_norm [k], codebook [k, d] contiguous;
+ * latents [b,d,t] with strides latent_strides (3 int64, host) used only when
+ * straight_through != 0, in which case out is [b,d,t] contiguous holding
+ * latents + (codebook[index] - latents); otherwise out is [b*t, d].
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_lfq_select(const float* dots, const float* row_norm,
+                    const float* code_norm, const float* codebook,
+                    const float* latents, const int64_t* latent_strides,
+                    int64_t b, int64_t d, int64_t t, int64_t k,
+                    int straight_through, float* out, int64_t* indices,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused LFQ decode: preparation + dot products + selection in one kernel,
+ * no [b*t, k] dot-product matrix in HBM.
+ * Replaces fast_moss/v2_runtime.py:143-181 (patched `decode_latents`).
+ * x [b,8,t] contiguous float32; book_normed [k,8] (F.normalize of the
+ * weight), code_norm [k] (sum of squares of book_normed rows), weight [k,8]
+ * (raw codebook, gathered into the output).  Dots use a sequential FMA over
+ * the 8 channels.  out [b*t, 8] (the reference returns its B,8,T transpose
+ * view), indices int64 [b*t].
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_lfq_decode(const float* x, const float* book_normed,
+                    const float* code_norm, const float* weight, int64_t b,
+                    int64_t t, int64_t k, float* out, int64_t* indices,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Codebook preparation for the multi-stage residual vector quantizer,
+ * the analogue of the one-off codebook normalisation the reference performs
+ * when its optimisation context is entered (fast_moss/v2_runtime.py:401-403).
+ * books [stages, k, d] float32 contiguous.  Writes
+ *   code_norm [stages, kpad]  sum_d c[d]^2 (sequential FMA; +inf for padding)
+ *   packed    [stages, kpad/256, d, 256]  k-major copy for the search kernel
+ *   stats     [stages, 4]     {max code norm, non-finite flag, 0, 0}
+ * with kpad = k rounded up to a multiple of 256.  Only d == 64 is supported.
+ * ------------------------------------------------------------------------- */
+MOSS_API int64_t moss_rvq_packed_floats(int64_t stages, int64_t k, int64_t d);
+MOSS_API int moss_rvq_prepare_codebooks(const float* books, int64_t stages, int64_t k,
+                               int64_t d, float* code_norm, float* packed,
+                               float* stats, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Multi-stage residual vector quantizer, encode + decode in one kernel.
+ * The stage loop the reference delegates to the upstream quantizer
+ * (fast_moss/v2_codec.py:45), each stage with the selection rule of
+ * fast_moss/quantizer.py:33-39: for every row r (residual kept on chip):
+ *   norm = sum_d r[d]^2, dot_j = sum_d (2 r[d]) c_j[d]  (sequential FMA, d
+ *   ascending), dist_j = (norm - dot_j) + code_norm_j, index = first NaN,
+ *   else first minimum; r -= c_index; recon += c_index.
+ * x [rows, d]; codes int32 [stages, rows]; recon [rows, d];
+ * residual_out [rows, d] optional (NULL = skip).
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rvq_encode(const float* x, int64_t rows, int64_t d,
+                    const float* books, const float* packed,
+                    const float* code_norm, const float* stats,
+                    int64_t stages, int64_t k, int32_t* codes, float* recon,
+                    float* residual_out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Residual-VQ dequantisation: recon[r] = sum_s books[s][codes[s][r]] in
+ * stage order (float32 adds starting from zero).  Codes outside [0, k) are
+ * reported through the device error word and contribute nothing.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rvq_decode(const int32_t* codes, int64_t rows, const float* books,
+                    int64_t stages, int64_t k, int64_t d, float* recon,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FAST_MOSS_B200_H */

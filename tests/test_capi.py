@@ -1,0 +1,92 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and rejects
+bad arguments with the documented status codes before touching the GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "fast_moss_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^MOSS_API\s+[\w\s\*]+?\b(moss_\w+)\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from fast_moss_b200 import _lib
+
+    return _lib.load()
+
+
+def test_header_declares_the_api():
+    syms = declared_symbols()
+    assert len(syms) >= 16
+    assert "moss_rvq_encode" in syms and "moss_residual_layer_norm" in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_python_binding_covers_the_header():
+    from fast_moss_b200 import _lib
+
+    assert sorted(_lib.EXPORTED) == declared_symbols()
+
+
+def test_library_is_sm100a_only():
+    from fast_moss_b200 import _lib
+
+    blob = open(_lib.LIB_PATH, "rb").read()
+    assert b"sm_100a" in blob
+
+
+def test_version(lib):
+    assert lib.moss_version() == 100
+
+
+def test_bad_arguments_map_to_value_errors(lib):
+    from fast_moss_b200 import _lib
+
+    # negative sizes / zero channels are rejected before any CUDA call
+    assert lib.moss_scale_add(None, 0, None, 0, None, None, -1, 4, None) == _lib.ERR_VALUE
+    assert lib.moss_scale_add(None, 0, None, 0, None, None, 8, 0, None) == _lib.ERR_VALUE
+    assert lib.moss_scale_add(None, 7, None, 0, None, None, 8, 4, None) == _lib.ERR_VALUE
+    assert b"dtype" in lib.moss_last_error()
+    # odd head dim
+    s = _lib.strides([0, 0, 0, 1])
+    assert lib.moss_rotate(None, None, 1, None, None, None, None, 1, 1, 1, 3, s, s,
+                           None) == _lib.ERR_VALUE
+    # unsupported widths are distinguished from invalid ones
+    assert lib.moss_layer_norm(ctypes.c_void_p(16), None, None, 1e-5, 4, 6, ctypes.c_void_p(16),
+                               None, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.moss_rvq_encode(None, 8, 32, None, None, None, None, 1, 4, None, None, None,
+                               None) == _lib.ERR_UNSUPPORTED
+    assert lib.moss_lfq_select(None, None, None, None, None, None, 1, 8, 1, 70000, 0, None, None,
+                               None) == _lib.ERR_VALUE
+    # empty inputs are a no-op success
+    assert lib.moss_scale_add(None, 0, None, 0, None, None, 0, 4, None) == _lib.OK
+    assert lib.moss_rvq_packed_floats(32, 1000, 64) == 32 * 1024 * 64
+
+
+def test_python_wrappers_raise_reference_exceptions():
+    import torch
+
+    import fast_moss_b200 as fm
+
+    x = torch.zeros(2, 4, 8)
+    with pytest.raises(ValueError, match="rotary"):
+        fm.rotate(torch.zeros(2, 3), x, x, x)
+    with pytest.raises(ValueError, match="channel scale"):
+        fm.scale_add(x, x, torch.zeros(3))
+    with pytest.raises(ValueError):
+        fm.prepare(torch.zeros(1, 8, 4))  # CPU tensor
+    with pytest.raises(ValueError, match="B,D,T"):
+        fm.select(x, x, x, torch.zeros(3), x)

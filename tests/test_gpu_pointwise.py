@@ -1,0 +1,181 @@
+"""GPU parity: residual scale-add, RoPE (tables and in-kernel phase), gated
+activation.
+
+Bars: scale_add / rotate bit-exact against the reference's kernels (golden
+fixtures) and the oracle; the in-kernel RoPE phase bit-exact against the
+reference's torch table construction on the same device; bf16 pointwise
+within 1 bf16 ulp of the oracle (and bit-exact against torch's eager CUDA
+chain, which uses the same math library).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_ulp_diff, golden, same_bits
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, device, dtype=torch.float32):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device=device, dtype=dtype)
+
+
+def test_scale_add_golden(moss, cuda_device):
+    g = golden("scale_add.npz")
+    for case in g["cases"]:
+        xd = torch.bfloat16 if bool(g[f"{case}_xbf16"]) else torch.float32
+        ud = torch.bfloat16 if bool(g[f"{case}_ubf16"]) else torch.float32
+        y = moss.scale_add(dev(g[f"{case}_x"], cuda_device, xd), dev(g[f"{case}_u"], cuda_device, ud),
+                           dev(g[f"{case}_s"], cuda_device))
+        assert same_bits(y.cpu().numpy(), g[f"{case}_y"]), case
+
+
+def test_scale_add_random_and_strided(moss, cuda_device):
+    g = torch.Generator().manual_seed(11)
+    for shape in [(1, 4096, 1024), (3, 7, 1280), (5, 33), (2, 3, 6)]:
+        x = torch.randn(*shape, generator=g).to(cuda_device)
+        u = torch.randn(*shape, generator=g).to(cuda_device, torch.bfloat16)
+        s = torch.randn(shape[-1], generator=g).to(cuda_device)
+        y = moss.scale_add(x, u, s)
+        ref = O.scale_add(x.cpu().numpy(), u.float().cpu().numpy(), s.cpu().numpy())
+        assert same_bits(y.cpu().numpy(), ref), shape
+    # non-contiguous views give the same values as their contiguous copies
+    x = torch.randn(8, 64, generator=g).to(cuda_device).t()
+    u = torch.randn(8, 64, generator=g).to(cuda_device).t()
+    s = torch.randn(8, generator=g).to(cuda_device)
+    assert torch.equal(moss.scale_add(x, u, s), moss.scale_add(x.contiguous(), u.contiguous(), s))
+
+
+def test_rotate_golden(moss, cuda_device):
+    g = golden("rotate.npz")
+    for case in g["cases"]:
+        bf16 = bool(g[f"{case}_bf16"])
+        dt = torch.bfloat16 if bf16 else torch.float32
+        if case == "bf16_view":
+            qkv = dev(g[f"{case}_qbase"], cuda_device, dt)
+            q, k = qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2)
+        else:
+            q, k = dev(g[f"{case}_q"], cuda_device, dt), dev(g[f"{case}_k"], cuda_device, dt)
+        oq, ok = moss.rotate(q, k, dev(g[f"{case}_cos"], cuda_device), dev(g[f"{case}_sin"], cuda_device))
+        assert oq.is_contiguous() and oq.dtype == dt
+        assert same_bits(oq.float().cpu().numpy(), g[f"{case}_oq"]), case
+        assert same_bits(ok.float().cpu().numpy(), g[f"{case}_ok"]), case
+
+
+def reference_tables(offset, t, d, period, device):
+    """The reference's rotary table construction (fast_moss/v2_runtime.py:214-222)."""
+    b = offset.numel()
+    ds = torch.arange(d // 2, device=device, dtype=torch.float32)
+    freq = torch.exp(ds * (-math.log(period) * 2 / d))
+    ts = offset.float().view(-1, 1) + torch.arange(t, device=device, dtype=torch.float32)
+    phase = freq * ts.view(b, t, 1)
+    return torch.cos(phase), torch.sin(phase)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rope_config3_matches_reference_tables(moss, cuda_device, dtype):
+    b, h, t, d = 4, 16, 2048, 64
+    g = torch.Generator().manual_seed(3)
+    qkv = torch.randn(b, t, 3, h, d, generator=g).to(cuda_device, dtype)
+    q, k = qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2)
+    offset = torch.zeros(b, dtype=torch.long, device=cuda_device)
+    cos, sin = reference_tables(offset, t, d, 10000.0, cuda_device)
+    rq, rk = moss.rotate(q, k, cos, sin)
+    fq, fk = moss.rope(q, k, offset, 10000.0)
+    assert torch.equal(fq.view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
+                       rq.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+    assert torch.equal(fk.view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
+                       rk.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+    # rotation itself against the oracle, on a slice
+    sl = slice(0, 64)
+    oq, ok = O.rotate(q[:, :, sl].float().cpu().numpy(), k[:, :, sl].float().cpu().numpy(),
+                      cos[:, sl].cpu().numpy(), sin[:, sl].cpu().numpy(), dtype == torch.bfloat16)
+    assert same_bits(rq[:, :, sl].float().cpu().numpy(), oq)
+    assert same_bits(rk[:, :, sl].float().cpu().numpy(), ok)
+
+
+def test_rope_phase_tables_bit_exact(moss, cuda_device):
+    """With q = (1, 0) pairs the f32 rotation returns (cos, sin) exactly, which
+    exposes the in-kernel tables for a direct comparison."""
+    b, h, t, d = 3, 1, 700, 128
+    q = torch.zeros(b, h, t, d, device=cuda_device)
+    q[..., 0::2] = 1.0
+    for offset in (torch.tensor([0, 5, 123456], device=cuda_device),
+                   torch.tensor([7, 0, 3], device=cuda_device, dtype=torch.int32),
+                   torch.tensor([0.0, 2.0, 1e5], device=cuda_device)):
+        oq, _ = moss.rope(q, q, offset, 10000.0)
+        cos, sin = reference_tables(offset, t, d, 10000.0, cuda_device)
+        assert torch.equal(oq[:, 0, :, 0::2], cos)
+        assert torch.equal(oq[:, 0, :, 1::2], sin)
+        ocs, osn = O.rope_tables(offset.float().cpu().numpy(), t, d,
+                                 np.float32(-math.log(10000.0) * 2 / d))
+        # CUDA's cosf/sinf/expf vs double libm: a few float ulps at most
+        assert np.max(np.abs(ocs - cos.cpu().numpy())) < 1e-4
+
+
+def test_rope_generic_strides(moss, cuda_device):
+    g = torch.Generator().manual_seed(5)
+    base = torch.randn(2, 6, 5, 4, 10, generator=g).to(cuda_device, torch.bfloat16)
+    q = base[..., 0, :].permute(0, 2, 1, 3)  # [2,5,6,10], innermost stride 1
+    k = base[..., 1, :].permute(0, 2, 1, 3).flip(-1)  # innermost stride -1
+    offset = torch.tensor([3, 0], device=cuda_device)
+    cos, sin = reference_tables(offset, 6, 10, 500.0, cuda_device)
+    oq, ok = moss.rotate(q, k, cos, sin)
+    rq, rk = O.rotate(q.float().cpu().numpy(), k.float().cpu().numpy(), cos.cpu().numpy(),
+                      sin.cpu().numpy(), True)
+    assert same_bits(oq.float().cpu().numpy(), rq)
+    assert same_bits(ok.float().cpu().numpy(), rk)
+    fq, fk = moss.rope(q, k, offset, 500.0)
+    assert torch.equal(fq, oq) and torch.equal(fk, ok)
+
+
+def torch_gated(x, bias, act, gated):
+    h = x + bias
+    if gated:
+        w = x.shape[-1] // 2
+        gate, up = h[..., :w], h[..., w:]
+    else:
+        gate = h
+    if act == "silu":
+        a = torch.nn.functional.silu(gate)
+    elif act == "gelu":
+        a = torch.nn.functional.gelu(gate)
+    else:
+        a = torch.nn.functional.gelu(gate, approximate="tanh")
+    return a * up if gated else a
+
+
+def test_silu_gate_config3(moss, cuda_device):
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(4, 2048, 4096, generator=g).to(cuda_device, torch.bfloat16)
+    bias = (0.02 * torch.randn(4096, generator=g)).to(cuda_device, torch.bfloat16)
+    y = moss.gated_activation(x, bias, "silu", gated=True)
+    ref = torch_gated(x, bias, "silu", True)
+    assert y.shape == (4, 2048, 2048) and y.dtype == torch.bfloat16
+    assert bf16_ulp_diff(y.float().cpu().numpy(), ref.float().cpu().numpy()) == 0
+    sub = slice(0, 64)
+    oy = O.gated_act(x[:, sub].float().cpu().numpy(), bias.float().cpu().numpy(), "silu", True, True)
+    assert bf16_ulp_diff(y[:, sub].float().cpu().numpy(), oy) <= 1
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
+@pytest.mark.parametrize("gated", [True, False])
+def test_activations_match_torch(moss, cuda_device, act, gated):
+    g = torch.Generator().manual_seed(9)
+    x = (3 * torch.randn(37, 96, generator=g)).to(cuda_device, torch.bfloat16)
+    bias = torch.randn(96, generator=g).to(cuda_device, torch.bfloat16)
+    y = moss.gated_activation(x, bias, act, gated=gated)
+    ref = torch_gated(x, bias, act, gated)
+    assert bf16_ulp_diff(y.float().cpu().numpy(), ref.float().cpu().numpy()) <= 1
+    oy = O.gated_act(x.float().cpu().numpy(), bias.float().cpu().numpy(), act, gated, True)
+    assert bf16_ulp_diff(y.float().cpu().numpy(), oy) <= 1
+    # odd width -> scalar path; float32 path
+    x2 = torch.randn(5, 22, generator=g).to(cuda_device)
+    b2 = torch.randn(22, generator=g).to(cuda_device)
+    y2 = moss.gated_activation(x2, b2, act, gated=gated)
+    r2 = torch_gated(x2, b2, act, gated)
+    assert torch.allclose(y2, r2, rtol=1e-6, atol=1e-6)
