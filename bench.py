@@ -180,9 +180,10 @@ def run_reference(args):
     from oracle import oracle as O
 
     threads = O.max_threads()
-    # size one step to about 5 s of host work
+    # size each step so that the whole warm-up + timed run takes ~2 minutes
     rate, _, _, _ = cpu_rvq_rate(x, books, seconds=2.0)
-    rows = int(min(FRAMES, max(64, rate * 5.0)))
+    per_step = min(5.0, 120.0 / max(1, args.steps + args.warmup))
+    rows = int(min(FRAMES, max(16, rate * per_step)))
     for _ in range(args.warmup):
         O.rvq_encode(x[:rows], books, nthreads=threads)
     t = time.perf_counter()
@@ -210,25 +211,41 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- GPU arms
-def time_launches(torch, fn, sets, iters, stream):
-    """Average device time of fn(set) over `iters` launches cycling through
-    `sets` (total size > L2), bracketed by CUDA events on `stream`."""
-    for i in range(3):
-        fn(sets[i % len(sets)])
+def time_launches(torch, fn, sets, launches=40, replays=5):
+    """Device time per launch of fn(set, stream_handle).
+
+    `launches` calls cycling through `sets` (whose total size exceeds L2, so
+    every launch reads cold data) are captured into one CUDA graph; the graph
+    is replayed `replays` times between CUDA events on the replay stream, so
+    no host launch overhead enters the measurement."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for i in range(3):
+            fn(sets[i % len(sets)], side.cuda_stream)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        handle = torch.cuda.current_stream().cuda_stream
+        for i in range(launches):
+            fn(sets[i % len(sets)], handle)
+    graph.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
-    for i in range(iters):
-        fn(sets[i % len(sets)])
+    for _ in range(replays):
+        graph.replay()
     end.record(stream)
     end.synchronize()
-    return start.elapsed_time(end) / iters * 1e-3
+    t = start.elapsed_time(end) * 1e-3 / (launches * replays)
+    del graph
+    return t
 
 
 def kernel_lines(torch, fm, dev, hbm_peak):
     out = {}
-    stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev).manual_seed(0)
 
     # config 1: residual + layer scale + LayerNorm, [1,4096,1024] FP32
@@ -244,15 +261,14 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     from fast_moss_b200 import _lib
 
     lib = _lib.load()
-    sh = stream.cuda_stream
 
-    def ln(s):
+    def ln(s, sh):
         _lib.check(lib.moss_residual_layer_norm(
             s[0].data_ptr(), 0, s[1].data_ptr(), 0, ls.data_ptr(), gamma.data_ptr(),
             beta.data_ptr(), 1e-5, rows, n, s[2].data_ptr(), s[3].data_ptr(), None, None, sh),
             "moss_residual_layer_norm")
 
-    t = time_launches(torch, ln, sets, 200, stream)
+    t = time_launches(torch, ln, sets)
     nbytes = 4 * rows * n * 4 + 3 * n * 4
     out["residual_layer_norm"] = {
         "shape": [1, rows, n], "us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9,
@@ -272,12 +288,12 @@ def kernel_lines(torch, fm, dev, hbm_peak):
 
     coef = -math.log(10000.0) * 2 / d
 
-    def rope(s):
+    def rope(s, sh):
         _lib.check(lib.moss_rope(s[0].data_ptr(), s[1].data_ptr(), 1, offset.data_ptr(), 0, coef,
                                  s[2].data_ptr(), s[3].data_ptr(), b, h, tt, d, st, st, sh),
                    "moss_rope")
 
-    t = time_launches(torch, rope, sets, 200, stream)
+    t = time_launches(torch, rope, sets)
     nbytes = 4 * b * h * tt * d * 2
     out["rope"] = {"shape": [b, h, tt, d], "us": t * 1e6, "bytes": nbytes,
                    "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
@@ -292,11 +308,11 @@ def kernel_lines(torch, fm, dev, hbm_peak):
         sets.append((x, torch.empty(rows, width // 2, device=dev, dtype=torch.bfloat16)))
     bias = (0.02 * torch.randn(width, device=dev, generator=g)).to(torch.bfloat16)
 
-    def silu(s):
+    def silu(s, sh):
         _lib.check(lib.moss_gated_act(s[0].data_ptr(), bias.data_ptr(), s[1].data_ptr(), 1, rows,
                                       width, 0, 1, sh), "moss_gated_act")
 
-    t = time_launches(torch, silu, sets, 200, stream)
+    t = time_launches(torch, silu, sets)
     nbytes = rows * width * 2 + width * 2 + rows * width // 2 * 2
     out["silu_gate"] = {"shape": [4, 2048, 4096], "us": t * 1e6, "bytes": nbytes,
                         "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
@@ -336,7 +352,7 @@ def run_b200(args):
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
 
-    def step():
+    def step():  # tensor-core kernel: one launch per step
         st = lib.moss_rvq_encode(x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(),
                                  rvq.packed.data_ptr(), rvq.code_norm.data_ptr(),
                                  rvq.stats.data_ptr(), STAGES, CODES, codes.data_ptr(),
@@ -398,6 +414,26 @@ def run_b200(args):
     ee.record(stream)
     ee.synchronize()
     e2e_s = es.elapsed_time(ee) * 1e-3
+
+    # the all-FFMA kernel (same codes) for comparison, same flush discipline
+    ffma_steps = max(3, min(args.steps, 50))
+    fs = [torch.cuda.Event(enable_timing=True) for _ in range(ffma_steps)]
+    fe = [torch.cuda.Event(enable_timing=True) for _ in range(ffma_steps)]
+    codes_f = torch.empty_like(codes)
+    recon_f = torch.empty_like(recon)
+    for i in range(ffma_steps + 1):
+        flush.fill_(float(i))
+        if i:
+            fs[i - 1].record(stream)
+        _lib.check(lib.moss_rvq_encode_ffma(
+            x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(), rvq.packed.data_ptr(),
+            rvq.code_norm.data_ptr(), rvq.stats.data_ptr(), STAGES, CODES, codes_f.data_ptr(),
+            recon_f.data_ptr(), None, sh), "moss_rvq_encode_ffma")
+        if i:
+            fe[i - 1].record(stream)
+    torch.cuda.synchronize()
+    ffma_s = sum(a.elapsed_time(b) for a, b in zip(fs, fe)) * 1e-3 / ffma_steps
+    ok = ok and bool(torch.equal(codes_f, codes))
     sampler.stop()
     clocks = sampler.summary(t0, t1)
 
@@ -428,7 +464,8 @@ def run_b200(args):
     max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
     fp32_peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
     achieved = FRAMES * FLOP_PER_FRAME / per_launch / 1e12
-    traffic = profile_traffic("rvq_encode")
+    tf32_peak = float(peaks["bf16_tflops"]) / 2
+    traffic = profile_traffic("rvq_tc")
     line = {
         "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
         "value": value,
@@ -457,16 +494,17 @@ def run_b200(args):
             "api": "ResidualVectorQuantizer.encode (C ABI moss_rvq_encode), pinned host buffers",
         },
         "roofline": {
-            "bound": "fp32",
-            "kernel": "rvq_encode_kernel",
+            "bound": "tensor",
+            "kernel": "rvq_tc_kernel (TF32 tcgen05 screening + exact FP32 rerank)",
             "achieved": achieved,
-            "peak": fp32_peak,
+            "peak": tf32_peak,
             "unit": "TFLOP/s",
-            "frac": achieved / fp32_peak,
+            "frac": achieved / tf32_peak,
             "traffic": traffic,
-            "peak_source": f"derived: {sms} SMs x 128 FP32 lanes x 2 x {max_mhz:.0f} MHz "
-                           f"(max SM clock of {peak_src} peaks file)",
+            "peak_source": f"TF32 dense = 1/2 of the {peak_src} bf16 dense GEMM rate "
+                           f"({peaks['bf16_tflops']} TFLOP/s)",
             "flop_per_launch": FRAMES * FLOP_PER_FRAME,
+            "fp32_ffma_peak": fp32_peak,
         },
         "gpu_launches": args.steps,
         "clocks": clocks,
@@ -474,8 +512,15 @@ def run_b200(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    ffma_tflops = FRAMES * FLOP_PER_FRAME / ffma_s / 1e12
+    ffma = {"kernel": "rvq_encode_kernel (all-FFMA, identical codes)", "ms": ffma_s * 1e3,
+            "achieved_tflops": ffma_tflops, "fp32_peak_tflops": fp32_peak,
+            "frac": ffma_tflops / fp32_peak}
     if kernels is not None:
-        line["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src, **kernels}
+        line["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src,
+                           "rvq_ffma": ffma, **kernels}
+    else:
+        line["kernels"] = {"rvq_ffma": ffma}
     print(json.dumps(line), flush=True)
 
 

@@ -375,33 +375,53 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_encode_kernel(EncodeArgs a) {
   }
 }
 
-// One CTA per stage: code norms, k-major packing, per-stage stats.
+// Byte offset of (code n, dim k) inside one 256-code tensor-core tile image:
+// K-major, 128-byte swizzle (16-byte chunk index XOR n % 8), 8-code groups
+// 1024 bytes apart, the two 32-dim halves 32 KB apart.
+__device__ __forceinline__ uint32_t tc_image_offset(int n, int k) {
+  const int kk = k & 31;
+  return static_cast<uint32_t>(k >> 5) * 32768u + static_cast<uint32_t>(n >> 3) * 1024u +
+         static_cast<uint32_t>(n & 7) * 128u +
+         static_cast<uint32_t>(((kk >> 2) ^ (n & 7)) << 4) + static_cast<uint32_t>(kk & 3) * 4u;
+}
+
+// One CTA per stage: code norms, the k-major copy used by the FFMA kernel,
+// the swizzled tile images used by the tensor-core kernel, per-stage stats.
 __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restrict__ books, int k,
-                                                          int kpad, float* __restrict__ code_norm,
+                                                          int kpad, int stages,
+                                                          float* __restrict__ code_norm,
                                                           float* __restrict__ packed,
                                                           float* __restrict__ stats) {
   __shared__ float red_max[256];
   __shared__ int red_bad[256];
   const int s = blockIdx.x;
   const float* book = books + static_cast<int64_t>(s) * k * kDim;
+  const int nch = kpad / kChunk;
+  unsigned char* image = reinterpret_cast<unsigned char*>(
+      packed + static_cast<int64_t>(stages) * kpad * kDim);
   float mx = 0.0f;
   int bad = 0;
   for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
     const int ch = j / kChunk, i = j % kChunk;
-    float* dst = packed + ((static_cast<int64_t>(s) * (kpad / kChunk) + ch) * kDim) * kChunk + i;
+    float* dst = packed + ((static_cast<int64_t>(s) * nch + ch) * kDim) * kChunk + i;
+    unsigned char* tile = image + (static_cast<int64_t>(s) * nch + ch) * (kChunk * kDim * 4);
     if (j < k) {
       float n = 0.0f;
       for (int d = 0; d < kDim; ++d) {
         const float v = book[static_cast<int64_t>(j) * kDim + d];
         n = __fmaf_rn(v, v, n);
         dst[static_cast<int64_t>(d) * kChunk] = v;
+        *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = v;
         if (!isfinite(v)) bad = 1;
       }
       code_norm[static_cast<int64_t>(s) * kpad + j] = n;
       if (!isfinite(n)) bad = 1;
       else mx = fmaxf(mx, n);
     } else {
-      for (int d = 0; d < kDim; ++d) dst[static_cast<int64_t>(d) * kChunk] = 0.0f;
+      for (int d = 0; d < kDim; ++d) {
+        dst[static_cast<int64_t>(d) * kChunk] = 0.0f;
+        *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = 0.0f;
+      }
       code_norm[static_cast<int64_t>(s) * kpad + j] = CUDART_INF_F;
     }
   }
@@ -454,7 +474,7 @@ using namespace moss;
 extern "C" int64_t moss_rvq_packed_floats(int64_t stages, int64_t k, int64_t d) {
   if (stages < 1 || k < 1 || d < 1) return 0;
   const int64_t kpad = (k + rvq::kChunk - 1) / rvq::kChunk * rvq::kChunk;
-  return stages * kpad * d;
+  return 2 * stages * kpad * d;  // FFMA k-major copy + tensor-core tile images
 }
 
 extern "C" int moss_rvq_prepare_codebooks(const float* books, int64_t stages, int64_t k, int64_t d,
@@ -467,15 +487,16 @@ extern "C" int moss_rvq_prepare_codebooks(const float* books, int64_t stages, in
   if (!books || !code_norm || !packed || !stats) return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
   const int64_t kpad = (k + rvq::kChunk - 1) / rvq::kChunk * rvq::kChunk;
   rvq::rvq_prepare_kernel<<<static_cast<unsigned>(stages), 256, 0, as_stream(stream)>>>(
-      books, static_cast<int>(k), static_cast<int>(kpad), code_norm, packed, stats);
+      books, static_cast<int>(k), static_cast<int>(kpad), static_cast<int>(stages), code_norm,
+      packed, stats);
   return launch_status(name);
 }
 
-extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const float* books,
-                               const float* packed, const float* code_norm, const float* stats,
-                               int64_t stages, int64_t k, int32_t* codes, float* recon,
-                               float* residual_out, void* stream) {
-  const char* name = "moss_rvq_encode";
+extern "C" int moss_rvq_encode_ffma(const float* x, int64_t rows, int64_t d, const float* books,
+                                    const float* packed, const float* code_norm,
+                                    const float* stats, int64_t stages, int64_t k, int32_t* codes,
+                                    float* recon, float* residual_out, void* stream) {
+  const char* name = "moss_rvq_encode_ffma";
   (void)stats;
   if (rows < 0 || stages < 1 || k < 1) return fail(MOSS_ERR_VALUE, "%s: bad shape", name);
   if (d != rvq::kDim) return fail(MOSS_ERR_UNSUPPORTED, "%s: only 64-dim codewords are supported", name);

@@ -4,8 +4,12 @@ The stage loop of the upstream quantizer that the reference calls at
 fast_moss/v2_codec.py:45, every stage selecting with the rule of
 fast_moss/quantizer.py:33-39 (distance = (norm - dot) + code_norm, first
 NaN, else first minimum).  The whole loop runs in ONE kernel with the
-residual kept on chip across stages.  Numerics (the documented order the
-CPU oracle also follows): norm and code norms are sequential FMAs over the
+residual kept on chip across stages.  Two kernels implement it with
+identical results: "tensor_core" screens the codes with TF32 tcgen05 dot
+products under a proven error margin and resolves the survivors exactly
+(the default), "ffma" evaluates every distance with FP32 FMAs.  Numerics
+(the documented order the CPU oracle also follows): norm and code norms
+are sequential FMAs over the
 dimensions in ascending order starting from +0, dot_j = the same over
 (2 r[d]) * c_j[d]; r -= c and recon += c in float32.
 """
@@ -30,7 +34,7 @@ class ResidualVectorQuantizer:
         self.stages, self.codes, self.dim = self.books.shape
         lib = _lib.load()
         floats = lib.moss_rvq_packed_floats(self.stages, self.codes, self.dim)
-        kpad = floats // max(1, self.stages * self.dim)
+        kpad = floats // max(1, 2 * self.stages * self.dim)  # two layouts per code
         dev = self.books.device
         self.code_norm = torch.empty((self.stages, kpad), device=dev, dtype=torch.float32)
         self.packed = torch.empty(floats, device=dev, dtype=torch.float32)
@@ -48,12 +52,18 @@ class ResidualVectorQuantizer:
         ):
             raise ValueError(f"Expected FP32 rows [N, {self.dim}] on {self.books.device}")
 
-    def encode(self, x, *, codes=None, recon=None, residual=None):
+    def encode(self, x, *, codes=None, recon=None, residual=None, algorithm="tensor_core"):
         """Quantizes rows x [N, D]; returns (codes int32 [S, N], recon [N, D]).
 
         Output buffers may be passed in (e.g. static buffers of a CUDA graph);
-        `residual` (optional) receives the final residual.
+        `residual` (optional) receives the final residual.  `algorithm` picks
+        the kernel ("tensor_core" or "ffma"; both give the same bits); books
+        with more than 4096 codes always use "ffma".
         """
+        if algorithm not in ("tensor_core", "ffma"):
+            raise ValueError(f"Unknown algorithm {algorithm!r}")
+        entry = "moss_rvq_encode" if algorithm == "tensor_core" and self.codes <= 4096 \
+            else "moss_rvq_encode_ffma"
         self._check_rows(x)
         x = x.contiguous()
         n = x.shape[0]
@@ -68,7 +78,7 @@ class ResidualVectorQuantizer:
             raise ValueError("recon buffer must be float32 [rows, dim]")
         with torch.cuda.device(dev):
             _lib.call(
-                "moss_rvq_encode", x.data_ptr(), n, self.dim, self.books.data_ptr(),
+                entry, x.data_ptr(), n, self.dim, self.books.data_ptr(),
                 self.packed.data_ptr(), self.code_norm.data_ptr(), self.stats.data_ptr(),
                 self.stages, self.codes, codes.data_ptr(), recon.data_ptr(),
                 residual.data_ptr() if residual is not None else None,

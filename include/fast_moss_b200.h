@@ -188,7 +188,10 @@ MOSS_API int moss_lfq_decode(const float* x, const float* book_normed,
  * when its optimisation context is entered (fast_moss/v2_runtime.py:401-403).
  * books [stages, k, d] float32 contiguous.  Writes
  *   code_norm [stages, kpad]  sum_d c[d]^2 (sequential FMA; +inf for padding)
- *   packed    [stages, kpad/256, d, 256]  k-major copy for the search kernel
+ *   packed    moss_rvq_packed_floats() floats: the k-major copy
+ *             [stages, kpad/256, d, 256] read by moss_rvq_encode_ffma, then
+ *             the 128-byte-swizzled 256-code tile images read by the
+ *             tensor cores in moss_rvq_encode
  *   stats     [stages, 4]     {max code norm, non-finite flag, 0, 0}
  * with kpad = k rounded up to a multiple of 256.  Only d == 64 is supported.
  * ------------------------------------------------------------------------- */
@@ -206,9 +209,20 @@ MOSS_API int moss_rvq_prepare_codebooks(const float* books, int64_t stages, int6
  *   ascending), dist_j = (norm - dot_j) + code_norm_j, index = first NaN,
  *   else first minimum; r -= c_index; recon += c_index.
  * x [rows, d]; codes int32 [stages, rows]; recon [rows, d];
- * residual_out [rows, d] optional (NULL = skip).
+ * residual_out [rows, d] optional (NULL = skip); all 16-byte aligned.
+ *
+ * moss_rvq_encode screens the codes with TF32 tensor-core dot products
+ * (tcgen05, accumulators in tensor memory) under a proven error margin and
+ * resolves the surviving candidates with the exact arithmetic above, so its
+ * codes equal those of moss_rvq_encode_ffma, which evaluates every distance
+ * with FP32 FMAs.  k <= 4096 for the tensor-core path.
  * ------------------------------------------------------------------------- */
 MOSS_API int moss_rvq_encode(const float* x, int64_t rows, int64_t d,
+                    const float* books, const float* packed,
+                    const float* code_norm, const float* stats,
+                    int64_t stages, int64_t k, int32_t* codes, float* recon,
+                    float* residual_out, void* stream);
+MOSS_API int moss_rvq_encode_ffma(const float* x, int64_t rows, int64_t d,
                     const float* books, const float* packed,
                     const float* code_norm, const float* stats,
                     int64_t stages, int64_t k, int32_t* codes, float* recon,

@@ -95,24 +95,32 @@ def rvq_case(rows, k, stages, seed, device):
     return x, books
 
 
-def run_rvq(moss, x, books, device):
+ALGOS = ["tensor_core", "ffma"]
+
+
+def run_rvq(moss, x, books, device, algorithm="tensor_core"):
     q = moss.ResidualVectorQuantizer(dev(books, device))
     res = torch.empty(x.shape, device=device)
-    codes, recon = q.encode(dev(x, device), residual=res)
+    codes, recon = q.encode(dev(x, device), residual=res, algorithm=algorithm)
+    torch.cuda.synchronize()
+    from fast_moss_b200 import _lib
+    _lib.check(_lib.load().moss_check_device_error(None), "device error word")
     return q, codes, recon, res
 
 
-def test_rvq_golden(moss, cuda_device):
+@pytest.mark.parametrize("algorithm", ALGOS)
+def test_rvq_golden(moss, cuda_device, algorithm):
     g = golden("rvq_small.npz")
-    _, codes, recon, res = run_rvq(moss, g["x"], g["books"], cuda_device)
+    _, codes, recon, res = run_rvq(moss, g["x"], g["books"], cuda_device, algorithm)
     assert np.array_equal(codes.cpu().numpy(), g["codes"])
     assert same_bits(recon.cpu().numpy(), g["recon"])
     assert same_bits(res.cpu().numpy(), g["residual"])
 
 
-def test_rvq_config2_bit_exact(moss, cuda_device):
+@pytest.mark.parametrize("algorithm", ALGOS)
+def test_rvq_config2_bit_exact(moss, cuda_device, algorithm):
     x, books = rvq_case(8192, 1024, 32, 1, cuda_device)
-    q, codes, recon, res = run_rvq(moss, x, books, cuda_device)
+    q, codes, recon, res = run_rvq(moss, x, books, cuda_device, algorithm)
     oc, orc, ores = O.rvq_encode(x, books, residual=True)
     assert codes.dtype == torch.int32 and codes.shape == (32, 8192)
     assert np.array_equal(codes.cpu().numpy(), oc)
@@ -121,18 +129,20 @@ def test_rvq_config2_bit_exact(moss, cuda_device):
     assert torch.equal(q.decode(codes), recon)
 
 
+@pytest.mark.parametrize("algorithm", ALGOS)
 @pytest.mark.parametrize("rows,k,stages", [(1, 1024, 4), (57, 1000, 3), (113, 256, 2),
-                                           (300, 37, 5), (56, 2049, 2)])
-def test_rvq_ragged_shapes(moss, cuda_device, rows, k, stages):
+                                           (300, 37, 5), (56, 2049, 2), (129, 4096, 2)])
+def test_rvq_ragged_shapes(moss, cuda_device, rows, k, stages, algorithm):
     x, books = rvq_case(rows, k, stages, rows + k, cuda_device)
-    q, codes, recon, res = run_rvq(moss, x, books, cuda_device)
+    q, codes, recon, res = run_rvq(moss, x, books, cuda_device, algorithm)
     oc, orc, ores = O.rvq_encode(x, books, residual=True)
     assert np.array_equal(codes.cpu().numpy(), oc)
     assert same_bits(recon.cpu().numpy(), orc)
     assert same_bits(res.cpu().numpy(), ores)
 
 
-def test_rvq_ties_nan_inf_overflow(moss, cuda_device):
+@pytest.mark.parametrize("algorithm", ALGOS)
+def test_rvq_ties_nan_inf_overflow(moss, cuda_device, algorithm):
     x, books = rvq_case(120, 300, 4, 77, cuda_device)
     books[0, 10] = books[0, 3]  # exact duplicate codeword: first one wins
     books[2, 7, 5] = np.nan  # a NaN codeword: every row picks it at stage 2
@@ -141,13 +151,36 @@ def test_rvq_ties_nan_inf_overflow(moss, cuda_device):
     x[3, :] = 1.5e19  # finite row whose dot products overflow
     x[4, :] = 0.0  # zero row
     x[5, :] = 1e-42  # subnormal row
-    q, codes, recon, res = run_rvq(moss, x, books, cuda_device)
+    q, codes, recon, res = run_rvq(moss, x, books, cuda_device, algorithm)
     oc, orc, ores = O.rvq_encode(x, books, residual=True)
     assert np.array_equal(codes.cpu().numpy(), oc)
     assert same_bits(recon.cpu().numpy(), orc)
     assert same_bits(res.cpu().numpy(), ores)
     # rows whose residual is still finite take the first NaN distance, code 7
     assert np.all(codes.cpu().numpy()[2, 6:] == 7)
+
+
+def test_rvq_near_ties(moss, cuda_device):
+    """Codewords that differ by one float ulp, duplicated codewords and rows
+    placed exactly between two codewords: the screening margin must keep
+    every tied or nearly tied candidate and the exact rerank must pick the
+    first minimum."""
+    rng = np.random.default_rng(21)
+    k, stages, rows = 512, 3, 256
+    books = (rng.standard_normal((stages, k, 64)) / 8).astype(np.float32)
+    for s in range(stages):
+        books[s, 100] = books[s, 7]
+        books[s, 101] = np.nextafter(books[s, 7], np.float32(np.inf))
+        books[s, 300:310] = books[s, 300]
+    x = rng.standard_normal((rows, 64)).astype(np.float32) * 0.3
+    x[:32] = books[0, 7] + 1e-7 * rng.standard_normal((32, 64)).astype(np.float32)
+    x[32:64] = 0.5 * (books[0, 20] + books[0, 21])
+    for algorithm in ALGOS:
+        _, codes, recon, res = run_rvq(moss, x, books, cuda_device, algorithm)
+        oc, orc, ores = O.rvq_encode(x, books, residual=True)
+        assert np.array_equal(codes.cpu().numpy(), oc), algorithm
+        assert same_bits(recon.cpu().numpy(), orc), algorithm
+        assert same_bits(res.cpu().numpy(), ores), algorithm
 
 
 def test_rvq_decode_and_buffers(moss, cuda_device):
