@@ -375,14 +375,23 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_encode_kernel(EncodeArgs a) {
   }
 }
 
-// Byte offset of (code n, dim k) inside one 256-code tensor-core tile image:
-// K-major, 128-byte swizzle (16-byte chunk index XOR n % 8), 8-code groups
-// 1024 bytes apart, the two 32-dim halves 32 KB apart.
+// Tensor-core tile image of 256 codes (73728 bytes): the 64 dims in a K-major
+// 128-byte-swizzled layout (16-byte chunk index XOR n % 8, 8-code groups 1024
+// bytes apart, the two 32-dim halves 32 KB apart), then an 8-wide K block
+// without swizzle (8-code x 16-byte core matrices, K halves 128 bytes apart,
+// 8-code groups 256 bytes apart) holding {-cnorm, 0 x 7} per code.
+constexpr int kTcMainBytes = kChunk * kDim * 4;
+constexpr int kTcTileBytes = kTcMainBytes + kChunk * 8 * 4;
+
 __device__ __forceinline__ uint32_t tc_image_offset(int n, int k) {
   const int kk = k & 31;
   return static_cast<uint32_t>(k >> 5) * 32768u + static_cast<uint32_t>(n >> 3) * 1024u +
          static_cast<uint32_t>(n & 7) * 128u +
          static_cast<uint32_t>(((kk >> 2) ^ (n & 7)) << 4) + static_cast<uint32_t>(kk & 3) * 4u;
+}
+__device__ __forceinline__ uint32_t tc_extra_offset(int n, int k) {
+  return kTcMainBytes + static_cast<uint32_t>(n >> 3) * 256u + static_cast<uint32_t>(k >> 2) * 128u +
+         static_cast<uint32_t>(n & 7) * 16u + static_cast<uint32_t>(k & 3) * 4u;
 }
 
 // One CTA per stage: code norms, the k-major copy used by the FFMA kernel,
@@ -404,7 +413,7 @@ __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restric
   for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
     const int ch = j / kChunk, i = j % kChunk;
     float* dst = packed + ((static_cast<int64_t>(s) * nch + ch) * kDim) * kChunk + i;
-    unsigned char* tile = image + (static_cast<int64_t>(s) * nch + ch) * (kChunk * kDim * 4);
+    unsigned char* tile = image + (static_cast<int64_t>(s) * nch + ch) * kTcTileBytes;
     if (j < k) {
       float n = 0.0f;
       for (int d = 0; d < kDim; ++d) {
@@ -415,6 +424,8 @@ __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restric
         if (!isfinite(v)) bad = 1;
       }
       code_norm[static_cast<int64_t>(s) * kpad + j] = n;
+      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -n;
+      for (int e = 1; e < 8; ++e) *reinterpret_cast<float*>(tile + tc_extra_offset(i, e)) = 0.0f;
       if (!isfinite(n)) bad = 1;
       else mx = fmaxf(mx, n);
     } else {
@@ -423,6 +434,9 @@ __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restric
         *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = 0.0f;
       }
       code_norm[static_cast<int64_t>(s) * kpad + j] = CUDART_INF_F;
+      // padding codes screen far below every real code
+      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -1.0e38f;
+      for (int e = 1; e < 8; ++e) *reinterpret_cast<float*>(tile + tc_extra_offset(i, e)) = 0.0f;
     }
   }
   red_max[threadIdx.x] = mx;
@@ -474,7 +488,8 @@ using namespace moss;
 extern "C" int64_t moss_rvq_packed_floats(int64_t stages, int64_t k, int64_t d) {
   if (stages < 1 || k < 1 || d < 1) return 0;
   const int64_t kpad = (k + rvq::kChunk - 1) / rvq::kChunk * rvq::kChunk;
-  return 2 * stages * kpad * d;  // FFMA k-major copy + tensor-core tile images
+  // FFMA k-major copy, then the tensor-core tile images
+  return stages * kpad * d + stages * (kpad / rvq::kChunk) * (rvq::kTcTileBytes / 4);
 }
 
 extern "C" int moss_rvq_prepare_codebooks(const float* books, int64_t stages, int64_t k, int64_t d,

@@ -1,30 +1,36 @@
 // Multi-stage residual VQ with tensor-core screening (tcgen05, TF32) and an
-// exact FP32 rerank.  Produces exactly the codes of the FFMA kernel in
-// rvq.cu (same documented arithmetic), typically ~10x faster.
+// exact FP32 resolution.  Produces exactly the codes of the FFMA kernel in
+// rvq.cu (same documented arithmetic).
 //
-// Why the indices stay exact.  For row r and code j let
-//   key_j   = cnorm_j - A_j,  A_j = TF32 tensor-core value of sum_d 2r_d c_jd
-//   exact_j = dist_j - norm   (real-number difference; dist_j in the pinned
-//                              FP32 order of rvq.cu)
-// TF32 keeps 10 fraction bits (relative error < 2^-10 per operand), so
-// |A_j - sum 2r_d c_jd| < 2^-9 sum|2r_d c_jd| (+ accumulation rounding), and
-// the pinned FP32 dot and the two FP32 roundings of dist add < 2^-20 (norm +
-// cnorm_max + |dot|).  With S = |2r| (Euclidean), C = max_j |c_j|:
-//   |key_j - exact_j| <= M = 2^-8 S C + 2^-20 (norm + cnorm_max) + 2^-100
-// (a 2x margin over the TF32 bound).  Every minimiser j* of dist then has
-// key_j* <= min_i key_i + 2M, so the candidates {j : key_j <= min key + 2M}
-// contain all of them; a single candidate is the answer, several are
-// reranked with the exact pinned arithmetic (first minimum wins).  Rows
-// whose preconditions fail (non-finite norm or codebook, S*C >= 2^120, more
-// than kCap candidates) are resolved by an exact NaN-aware scan of all codes.
+// Why the indices stay exact.  For row r and code j the tensor cores compute
+//   acc_j = TF32 sum_d 2r_d c_jd  -  TF32(cnorm_j)      (9th K step: 1 x -cnorm)
+// and key_j = -acc_j approximates exact_j = dist_j - norm (real-number
+// difference; dist_j in the pinned FP32 order of rvq.cu).  TF32 keeps 10
+// fraction bits (relative error < 2^-10 per operand), so the products are
+// within 2^-9 sum|2r_d c_jd| <= 2^-9 S C (S = |2r|, C = max_j |c_j|) and the
+// folded norm within 2^-10 cnorm_max; the pinned FP32 dot and the two FP32
+// roundings of dist add less than 2^-20 (norm + cnorm_max + S C).  Hence
+//   |key_j - exact_j| <= M = 2^-8 S C + 2^-9 cnorm_max + 2^-20 (norm + cnorm_max)
+// (twice the TF32 bound).  Every minimiser j* of dist has key_j* <= min key
+// + 2M, so the candidates {j : acc_j >= max acc - 2M} contain all of them.
+// One candidate is the answer; several are resolved with the exact pinned
+// arithmetic (first minimum wins).  Rows whose preconditions fail
+// (non-finite norm or codebook, S C >= 1e36, candidate records overflow) are
+// resolved by an exact NaN-aware scan of all codes.
 //
-// Structure of one CTA (128 rows = the 128 TMEM lanes, all stages):
-//   warps 0-3  epilogue: thread i owns row i (residual in registers), reads
-//              its TMEM lane, screens, reranks, updates, writes the next
-//              stage's A operand (2r, K-major, 128B swizzle) to shared memory;
-//   warp 4     producer: cp.async.bulk of pre-swizzled 256-code codebook
-//              tiles (64 KB) into a 2-slot ring;
-//   warp 5     TMEM allocator + MMA issuer: per tile, 8 x tcgen05.mma
+// SIMT shape of the screening: per 32-code chunk a thread (one row) takes the
+// chunk maximum, updates its running maximum, and forms a 32-bit mask of the
+// codes inside the window -- all branch-free.  Only a non-empty mask costs a
+// (rare, short) record of {chunk, mask, chunk max} in shared memory; the
+// records are filtered against the final window at the end of the stage.
+//
+// One CTA = 128 rows (the 128 TMEM lanes), all stages:
+//   warps 0-3  epilogue: thread i owns row i (residual in registers), screens
+//              its TMEM lane, resolves, updates, writes the next stage's A
+//              operand (2r, K-major 128B-swizzled) to shared memory;
+//   warp 4     producer: cp.async.bulk of pre-built 256-code codebook tile
+//              images (64 KB swizzled dims + 8 KB norm column) into 2 slots;
+//   warp 5     TMEM allocator + MMA issuer: per tile 9 x tcgen05.mma
 //              (M=128, N=256, K=8) into one of two 256-column accumulators.
 // Every wait is bounded (~2 s) and records MOSS_ERR_TIMEOUT; all roles then
 // meet at the final barrier where the TMEM is released.
@@ -39,25 +45,29 @@ constexpr int kDim = 64;
 constexpr int kRows = 128;
 constexpr int kTileCodes = 256;
 constexpr int kSlots = 2;
-constexpr int kCap = 8;
+constexpr int kRec = 16;     // screening records per row and stage
+constexpr int kMaxCand = 32;  // candidates resolved exactly per row and stage
 constexpr int kEpiThreads = 128;
 constexpr int kThreads = 192;
-constexpr uint32_t kTileBytes = kTileCodes * kDim * 4;  // 65536
+constexpr uint32_t kMainBytes = kTileCodes * kDim * 4;   // 65536: swizzled dims
+constexpr uint32_t kExtraBytes = kTileCodes * 8 * 4;     // 8192: norm column block
+constexpr uint32_t kTileBytes = kMainBytes + kExtraBytes;  // 73728 per tile image
 constexpr uint32_t kTmemCols = 512;
-constexpr int kRStride = 65;
+constexpr int kMaxCodes = 4096;
 
 struct __align__(1024) Smem {
-  float btile[kSlots][kTileCodes * kDim];  // pre-swizzled B images (1024-aligned)
-  float a[kRows * kDim];                   // 2r, K-major SW128 image
-  float recon[kRows * kRStride];
-  float cn[4096];                          // code norms of the current stage (<= 4096 codes)
-  float cand_key[kCap][kRows];
-  int cand_idx[kCap][kRows];
+  float btile[kSlots][kTileBytes / 4];  // tile images (each 1024-aligned)
+  float a[kRows * kDim];                // 2r, K-major SW128 image
+  float a_extra[kRows * 8];             // [1, 0 x 7] per row, no-swizzle K block
+  float cmax[8][kRows];  // chunk maxima of the current tile
+  float rec_max[kRec][kRows];
+  uint32_t rec_mask[kRec][kRows];
+  int cand[kMaxCand][kRows];
+  unsigned char rec_chunk[kRec][kRows];
   float norms[kRows];
   int sel[kRows];
   int slow_list[kRows];
   int slow_count;
-  int abort_flag;
   uint32_t tmem_base;
   alignas(8) unsigned long long b_full[kSlots];
   alignas(8) unsigned long long b_empty[kSlots];
@@ -82,14 +92,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, u
                "r"(bytes)
                : "memory");
 }
+// The waiting thread is suspended (up to ~20 us per attempt) instead of
+// spinning, so waiting roles leave the issue slots to the epilogue warps.
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
       : "memory");
   return ok != 0;
 }
@@ -142,11 +154,17 @@ __device__ __forceinline__ int epi_bar_or(int pred) {
   return out;
 }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), descriptor version 1.
+// Shared-memory matrix descriptors (descriptor version 1).
+//   K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (SBO).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) |
          (1ull << 46) | (2ull << 61);
+}
+//   K-major, no swizzle: 8-row x 16-byte core matrices; the two K halves
+//   128 bytes apart (LBO), 8-row groups 256 bytes apart (SBO).
+__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (8ull << 16) | (16ull << 32) |
+         (1ull << 46);
 }
 // Instruction descriptor: kind::tf32, D f32, A/B tf32 K-major, M=128, N=256.
 constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((256u >> 3) << 17) |
@@ -198,20 +216,25 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
       : "memory");
 }
 
-// Byte offset of element (row, k) in a K-major SW128 image whose 8-row
-// groups are 1024 bytes apart and whose two 32-element K halves are `half`
-// bytes apart.
+// Byte offset of (row, k) in a K-major SW128 image: 8-row groups 1024 bytes
+// apart, 16-byte chunk index XOR row % 8, the two 32-element K halves `half`
+// bytes apart.  The tile images built by rvq.cu use the same formula.
 __device__ __forceinline__ uint32_t sw128_offset(int row, int k, uint32_t half) {
   const int kk = k & 31;
   return static_cast<uint32_t>(k >> 5) * half + static_cast<uint32_t>(row >> 3) * 1024u +
          static_cast<uint32_t>(row & 7) * 128u +
          static_cast<uint32_t>(((kk >> 2) ^ (row & 7)) << 4) + static_cast<uint32_t>(kk & 3) * 4u;
 }
+// Byte offset of (row, k < 8) in the no-swizzle K block.
+__device__ __forceinline__ uint32_t plain_offset(int row, int k) {
+  return static_cast<uint32_t>(row >> 3) * 256u + static_cast<uint32_t>(k >> 2) * 128u +
+         static_cast<uint32_t>(row & 7) * 16u + static_cast<uint32_t>(k & 3) * 4u;
+}
 
 struct Args {
   const float* x;
   const float* books;      // raw [stages][k][64]
-  const float* image;      // [stages][ntiles][64 KB swizzled]
+  const float* image;      // [stages][ntiles][kTileBytes]
   const float* code_norm;  // [stages][kpad]
   const float* stats;      // [stages][4]: max code norm, non-finite flag
   int32_t* codes;
@@ -259,61 +282,67 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
-
-// Keeps the candidates still inside the window; returns their count.
-__device__ __noinline__ int compact_candidates(Smem& sm, int row, float thr) {
+// Keeps the records whose chunk maximum is still inside the window.
+__device__ __noinline__ int compact_records(Smem& sm, int row, float athr) {
   int w = 0;
-  for (int e = 0; e < kCap; ++e) {
-    const float ek = sm.cand_key[e][row];
-    if (ek <= thr) {
-      sm.cand_key[w][row] = ek;
-      sm.cand_idx[w][row] = sm.cand_idx[e][row];
+  for (int e = 0; e < kRec; ++e) {
+    if (sm.rec_max[e][row] >= athr) {
+      sm.rec_max[w][row] = sm.rec_max[e][row];
+      sm.rec_mask[w][row] = sm.rec_mask[e][row];
+      sm.rec_chunk[w][row] = sm.rec_chunk[e][row];
       ++w;
     }
   }
   return w;
 }
 
-// Screens 32 accumulator columns (codes code0..code0+31) of this row:
-// key = cnorm - TF32 dot; keeps the running minimum and appends every code
-// within `window` of it to the row's candidate list (pruning entries that
-// fell out of the window when the list is full).
-__device__ __forceinline__ void screen_chunk(const uint32_t (&acc)[32], int code0, Smem& sm,
-                                             int row, int s, const Args& a, bool slow,
-                                             float window, float& mkey, float& thr, int& cnt,
-                                             bool& overflow) {
-  const float4* cn4 = reinterpret_cast<const float4*>(&sm.cn[code0]);
-  float key[32];
-  float cm = CUDART_INF_F;
-#pragma unroll
-  for (int j4 = 0; j4 < 8; ++j4) {
-    const float4 cv = cn4[j4];
-    key[4 * j4 + 0] = __fsub_rn(cv.x, __uint_as_float(acc[4 * j4 + 0]));
-    key[4 * j4 + 1] = __fsub_rn(cv.y, __uint_as_float(acc[4 * j4 + 1]));
-    key[4 * j4 + 2] = __fsub_rn(cv.z, __uint_as_float(acc[4 * j4 + 2]));
-    key[4 * j4 + 3] = __fsub_rn(cv.w, __uint_as_float(acc[4 * j4 + 3]));
-    cm = fminf(cm, fminf(fminf(key[4 * j4], key[4 * j4 + 1]),
-                         fminf(key[4 * j4 + 2], key[4 * j4 + 3])));
+// Screening record: stores {chunk max, mask, chunk}, prefetches the masked
+// codewords and returns the new record count (kRec + 1 once the records
+// overflowed; compaction of records that left the window is the rare case).
+__device__ __forceinline__ int add_record(Smem& sm, int row, int chunk, uint32_t mask, float cmx,
+                                          float athr, int nrec, const float* book,
+                                          const float* cnorm) {
+  if (nrec >= kRec) {
+    if (nrec > kRec) return nrec;
+    nrec = compact_records(sm, row, athr);
+    if (nrec == kRec) return kRec + 1;
   }
-  if (slow || !(cm <= thr)) return;
-  mkey = fminf(mkey, cm);
-  thr = mkey + window;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (key[j] <= thr) {
-      if (cnt == kCap) cnt = compact_candidates(sm, row, thr);
-      if (cnt == kCap) {
-        overflow = true;
-      } else {
-        sm.cand_key[cnt][row] = key[j];
-        sm.cand_idx[cnt][row] = code0 + j;
-        ++cnt;
-        const float* cw = a.books + (static_cast<int64_t>(s) * a.k + code0 + j) * kDim;
-        prefetch_l1(cw);
-        prefetch_l1(cw + 32);
-      }
-    }
+  sm.rec_max[nrec][row] = cmx;
+  sm.rec_mask[nrec][row] = mask;
+  sm.rec_chunk[nrec][row] = static_cast<unsigned char>(chunk);
+  for (uint32_t m = mask; m; m &= m - 1) {
+    const int j = chunk * 32 + (__ffs(m) - 1);
+    const float* cw = book + static_cast<int64_t>(j) * kDim;
+    prefetch_l1(cw);
+    prefetch_l1(cw + 32);
+    prefetch_l1(cnorm + j);
   }
+  return nrec + 1;
+}
+
+// Maximum of 32 accumulator values as a depth-5 tree (independent pairs).
+__device__ __forceinline__ float max32(const uint32_t (&acc)[32]) {
+  float m[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) m[j] = fmaxf(__uint_as_float(acc[j]), __uint_as_float(acc[j + 16]));
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1) {
+#pragma unroll
+    for (int j = 0; j < w; ++j) m[j] = fmaxf(m[j], m[j + w]);
+  }
+  return m[0];
+}
+
+// Bit j set iff acc[j] >= athr; four independent 8-bit partial masks.
+__device__ __forceinline__ uint32_t mask32(const uint32_t (&acc)[32], float athr) {
+  uint32_t part[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int p = 0; p < 4; ++p)
+      part[p] |= (__uint_as_float(acc[8 * p + j]) >= athr) ? (1u << (8 * p + j)) : 0u;
+  }
+  return (part[0] | part[1]) | (part[2] | part[3]);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
@@ -338,7 +367,6 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     }
     mbar_init(&sm.a_full, kEpiThreads);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    sm.abort_flag = 0;
     sm.slow_count = 0;
   }
   if (warp == 5) {
@@ -358,10 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     if (lane == 0) {
       for (int q = 0; q < total_tiles; ++q) {
         const int slot = q % kSlots;
-        if (!mbar_wait(&sm.b_empty[slot], ((q / kSlots) & 1) ^ 1)) {
-          sm.abort_flag = 1;
-          break;
-        }
+        if (!mbar_wait(&sm.b_empty[slot], ((q / kSlots) & 1) ^ 1)) break;
         mbar_arrive_expect_tx(&sm.b_full[slot], kTileBytes);
         bulk_g2s(&sm.btile[slot][0], a.image + static_cast<int64_t>(q) * (kTileBytes / 4),
                  kTileBytes, &sm.b_full[slot]);
@@ -372,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t a_base = smem_u32(sm.a);
+      const uint64_t a_extra = plain_desc(smem_u32(sm.a_extra));
       int q = 0;
       bool ok = true;
       for (int s = 0; s < a.stages && ok; ++s) {
@@ -393,18 +419,23 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           const uint32_t d_tmem = tmem + static_cast<uint32_t>(abuf * 256);
 #pragma unroll
           for (int kk = 0; kk < kDim / 8; ++kk) {
-            const uint32_t koff = static_cast<uint32_t>(kk >> 2) + 0u;
+            const uint32_t koff = static_cast<uint32_t>(kk >> 2);
             const uint64_t ad =
                 sw128_desc(a_base + koff * (kRows * 128u) + static_cast<uint32_t>(kk & 3) * 32u);
             const uint64_t bd = sw128_desc(b_base + koff * (kTileCodes * 128u) +
                                            static_cast<uint32_t>(kk & 3) * 32u);
             mma_tf32(d_tmem, ad, bd, kk > 0 ? 1u : 0u);
           }
+          // 9th K step: 1 x (-cnorm_j)
+          mma_tf32(d_tmem, a_extra, plain_desc(b_base + kMainBytes), 1u);
           mma_commit(&sm.t_full[abuf]);
           mma_commit(&sm.b_empty[slot]);
         }
       }
-      if (!ok) sm.abort_flag = 1;
+      // Let the final commit arrivals land before the CTA can retire.
+      for (int last = (q > kSlots ? q - kSlots : 0); ok && last < q; ++last) {
+        ok = mbar_wait(&sm.b_empty[last % kSlots], (last / kSlots) & 1);
+      }
     }
     __syncwarp();
   } else {
@@ -424,13 +455,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
 #pragma unroll
       for (int d = 0; d < kDim; ++d) r[d] = 0.0f;
     }
-    for (int d = 0; d < kDim; ++d) sm.recon[row * kRStride + d] = 0.0f;
     unsigned char* a_bytes = reinterpret_cast<unsigned char*>(sm.a);
+    {
+      unsigned char* e = reinterpret_cast<unsigned char*>(sm.a_extra);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        *reinterpret_cast<float*>(e + plain_offset(row, k)) = k == 0 ? 1.0f : 0.0f;
+    }
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
 
     int q = 0;
     bool aborted = false;
     for (int s = 0; s < a.stages; ++s) {
+      const float* book = a.books + static_cast<int64_t>(s) * a.k * kDim;
+      const float* cnorm = a.code_norm + static_cast<int64_t>(s) * a.kpad;
       // norm and the A operand (2r) of this stage
       float norm = 0.0f;
 #pragma unroll
@@ -442,26 +480,19 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
                                __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
         *reinterpret_cast<float4*>(a_bytes + sw128_offset(row, 4 * c, kRows * 128u)) = v;
       }
-      // stage code norms into shared memory
-      const float* cn_g = a.code_norm + static_cast<int64_t>(s) * a.kpad;
-      for (int i = row; i < a.kpad; i += kEpiThreads) sm.cn[i] = cn_g[i];
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      epi_bar();  // cn visible to all epilogue threads
       mbar_arrive(&sm.a_full);
 
-      // screening margin and preconditions
+      // screening window and preconditions
       const float cn_max = a.stats[s * 4 + 0];
       const bool book_ok = a.stats[s * 4 + 1] == 0.0f;
-      const float s2r = __fmul_rn(2.0f, sqrtf(norm));
-      const float cmax = sqrtf(cn_max);
-      const float sc = s2r * cmax;
-      bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
-      const float margin = fmaf(sc, 0.00390625f, (norm + cn_max) * 9.5367431640625e-07f) + 1e-30f;
+      const float sc = __fmul_rn(2.0f, sqrtf(norm)) * sqrtf(cn_max);
+      const bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
+      const float margin = sc * 0.00390625f + cn_max * 0.001953125f +
+                           (norm + cn_max) * 9.5367431640625e-07f + 1e-30f;
       const float window = 2.0f * margin * 1.0001f;
-      float mkey = CUDART_INF_F;
-      float thr = CUDART_INF_F;
-      int cnt = 0;
-      bool overflow = false;
+      float amax = -CUDART_INF_F;
+      int nrec = 0;
 
       for (int t = 0; t < ntiles; ++t, ++q) {
         const int abuf = q & 1;
@@ -472,62 +503,100 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         }
         tc_fence_after();
         const uint32_t tcol = tmem + lane_base + static_cast<uint32_t>(abuf * 256);
+        // Pass 1: the eight chunk maxima of this tile (independent chains),
+        // then one threshold for the whole tile.
         uint32_t va[32], vb[32];
-        tmem_load32(tcol, va);
-        tmem_wait_ld(va);
+        float tmax = -CUDART_INF_F;
 #pragma unroll 1
-        for (int c = 0; c < kTileCodes / 32; c += 2) {
+        for (int c = 0; c < 8; c += 2) {
+          tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
           tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
-          screen_chunk(va, t * kTileCodes + c * 32, sm, row, s, a, slow, window, mkey, thr, cnt,
-                       overflow);
+          tmem_wait_ld(va);
           tmem_wait_ld(vb);
-          if (c + 2 < kTileCodes / 32) tmem_load32(tcol + static_cast<uint32_t>((c + 2) * 32), va);
-          screen_chunk(vb, t * kTileCodes + (c + 1) * 32, sm, row, s, a, slow, window, mkey, thr,
-                       cnt, overflow);
-          if (c + 2 < kTileCodes / 32) tmem_wait_ld(va);
+          const float ca = max32(va), cb = max32(vb);
+          sm.cmax[c][row] = ca;
+          sm.cmax[c + 1][row] = cb;
+          tmax = fmaxf(tmax, fmaxf(ca, cb));
+        }
+        amax = fmaxf(amax, tmax);
+        const float athr = amax - window;
+        // Pass 2: window masks of the chunks that reach the threshold.
+#pragma unroll 1
+        for (int c = 0; c < 8; c += 2) {
+          tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
+          tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
+          tmem_wait_ld(va);
+          tmem_wait_ld(vb);
+          const uint32_t ma = mask32(va, athr);
+          const uint32_t mb = mask32(vb, athr);
+          if (ma) nrec = add_record(sm, row, t * 8 + c, ma, sm.cmax[c][row], athr, nrec, book, cnorm);
+          if (mb)
+            nrec = add_record(sm, row, t * 8 + c + 1, mb, sm.cmax[c + 1][row], athr, nrec, book, cnorm);
         }
         tc_fence_before();
         mbar_arrive(&sm.t_empty[abuf]);
       }
       if (aborted) break;
 
-      // ---- resolve the stage: candidates -> exact winner
+      // ---- resolve the stage: surviving records -> exact winner
       int winner = -1;
-      if (!slow && !overflow) {
-        int best_i = -1;
-        float best_d = 0.0f;
-        int live = 0;
-        for (int e = 0; e < cnt; ++e) {
-          if (sm.cand_key[e][row] <= thr) {
-            ++live;
-            best_i = sm.cand_idx[e][row];
+      if (!slow && nrec <= kRec) {
+        const float athr = amax - window;
+        int ncand = 0;
+        for (int e = 0; e < nrec; ++e) {
+          if (sm.rec_max[e][row] < athr) continue;
+          const int base = sm.rec_chunk[e][row] * 32;
+          for (uint32_t m = sm.rec_mask[e][row]; m; m &= m - 1) {
+            if (ncand < kMaxCand) sm.cand[ncand][row] = base + (__ffs(m) - 1);
+            ++ncand;
           }
         }
-        if (live == 1) {
-          winner = best_i;
-        } else if (live > 1) {
-          best_i = -1;
-          for (int e = 0; e < cnt; ++e) {
-            if (sm.cand_key[e][row] > thr) continue;
-            const int j = sm.cand_idx[e][row];
-            const float4* cw =
-                reinterpret_cast<const float4*>(a.books + (static_cast<int64_t>(s) * a.k + j) * kDim);
-            float dot = 0.0f;
+        if (ncand == 1) {
+          winner = sm.cand[0][row];
+        } else if (ncand > 1 && ncand <= kMaxCand) {
+          // exact distances, two candidates at a time: both codewords are
+          // loaded before the two independent FMA chains run; candidates are
+          // in ascending code order, so the first minimum wins
+          float best_d = 0.0f;
+          for (int b = 0; b < ncand; b += 2) {
+            const int j0 = sm.cand[b][row];
+            const int j1 = sm.cand[b + 1 < ncand ? b + 1 : b][row];
+            const float4* c0 = reinterpret_cast<const float4*>(book + static_cast<int64_t>(j0) * kDim);
+            const float4* c1 = reinterpret_cast<const float4*>(book + static_cast<int64_t>(j1) * kDim);
+            float4 w0[kDim / 4], w1[kDim / 4];
 #pragma unroll
             for (int i = 0; i < kDim / 4; ++i) {
-              const float4 v = cw[i];
-              dot = __fmaf_rn(__fmul_rn(2.0f, r[4 * i]), v.x, dot);
-              dot = __fmaf_rn(__fmul_rn(2.0f, r[4 * i + 1]), v.y, dot);
-              dot = __fmaf_rn(__fmul_rn(2.0f, r[4 * i + 2]), v.z, dot);
-              dot = __fmaf_rn(__fmul_rn(2.0f, r[4 * i + 3]), v.w, dot);
+              w0[i] = c0[i];
+              w1[i] = c1[i];
             }
-            const float dist = __fadd_rn(__fsub_rn(norm, dot), sm.cn[j]);
-            if (best_i < 0 || dist < best_d) {
-              best_d = dist;
-              best_i = j;
+            const float n0 = cnorm[j0], n1 = cnorm[j1];
+            float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kDim / 4; ++i) {
+              const float t0 = __fmul_rn(2.0f, r[4 * i]), t1 = __fmul_rn(2.0f, r[4 * i + 1]);
+              const float t2 = __fmul_rn(2.0f, r[4 * i + 2]), t3 = __fmul_rn(2.0f, r[4 * i + 3]);
+              d0 = __fmaf_rn(t0, w0[i].x, d0);
+              d1 = __fmaf_rn(t0, w1[i].x, d1);
+              d0 = __fmaf_rn(t1, w0[i].y, d0);
+              d1 = __fmaf_rn(t1, w1[i].y, d1);
+              d0 = __fmaf_rn(t2, w0[i].z, d0);
+              d1 = __fmaf_rn(t2, w1[i].z, d1);
+              d0 = __fmaf_rn(t3, w0[i].w, d0);
+              d1 = __fmaf_rn(t3, w1[i].w, d1);
+            }
+            const float dist0 = __fadd_rn(__fsub_rn(norm, d0), n0);
+            if (winner < 0 || dist0 < best_d) {
+              best_d = dist0;
+              winner = j0;
+            }
+            if (b + 1 < ncand) {
+              const float dist1 = __fadd_rn(__fsub_rn(norm, d1), n1);
+              if (dist1 < best_d) {
+                best_d = dist1;
+                winner = j1;
+              }
             }
           }
-          winner = best_i;
         }
       }
       if (winner < 0) {
@@ -538,14 +607,12 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       const int nslow = sm.slow_count;
       if (nslow > 0) {
         // exact scan, one warp per row; 2r is read back from the A image
-        const float* book = a.books + static_cast<int64_t>(s) * a.k * kDim;
         for (int i = warp; i < nslow; i += 4) {
           const int sr = sm.slow_list[i];
           float tw[kDim];
           for (int d = 0; d < kDim; ++d)
             tw[d] = *reinterpret_cast<const float*>(a_bytes + sw128_offset(sr, d, kRows * 128u));
-          const int ix = exact_scan(tw, sm.norms[sr], book,
-                                    a.code_norm + static_cast<int64_t>(s) * a.kpad, a.k, lane);
+          const int ix = exact_scan(tw, sm.norms[sr], book, cnorm, a.k, lane);
           if (lane == 0) sm.sel[sr] = ix;
         }
         epi_bar();
@@ -553,10 +620,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         epi_bar();
         if (row == 0) sm.slow_count = 0;
       }
-      // ---- update the residual and the reconstruction
+      // ---- update the residual (the reconstruction is summed at the end)
       const float4* cw =
-          reinterpret_cast<const float4*>(a.books + (static_cast<int64_t>(s) * a.k + winner) * kDim);
-      float* rc = &sm.recon[row * kRStride];
+          reinterpret_cast<const float4*>(book + static_cast<int64_t>(winner) * kDim);
 #pragma unroll
       for (int i = 0; i < kDim / 4; ++i) {
         const float4 v = cw[i];
@@ -564,22 +630,34 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         r[4 * i + 1] = __fsub_rn(r[4 * i + 1], v.y);
         r[4 * i + 2] = __fsub_rn(r[4 * i + 2], v.z);
         r[4 * i + 3] = __fsub_rn(r[4 * i + 3], v.w);
-        rc[4 * i] = __fadd_rn(rc[4 * i], v.x);
-        rc[4 * i + 1] = __fadd_rn(rc[4 * i + 1], v.y);
-        rc[4 * i + 2] = __fadd_rn(rc[4 * i + 2], v.z);
-        rc[4 * i + 3] = __fadd_rn(rc[4 * i + 3], v.w);
       }
       if (valid) a.codes[static_cast<int64_t>(s) * a.rows + grow] = winner;
-      // the slow scan of other rows may still read the A image: write the
-      // next stage's operand only after every epilogue thread is here
-      epi_bar();
+      if (nslow > 0) epi_bar();  // the slow scan read the A image of other rows
     }
     if (!aborted && valid) {
+      // recon = sum of the chosen codewords in stage order from +0 (the same
+      // float32 additions as an incremental sum)
+      float acc[kDim];
+#pragma unroll
+      for (int d = 0; d < kDim; ++d) acc[d] = 0.0f;
+#pragma unroll 4
+      for (int s = 0; s < a.stages; ++s) {
+        const int c = a.codes[static_cast<int64_t>(s) * a.rows + grow];
+        const float4* cw = reinterpret_cast<const float4*>(
+            a.books + (static_cast<int64_t>(s) * a.k + c) * kDim);
+#pragma unroll
+        for (int i = 0; i < kDim / 4; ++i) {
+          const float4 v = cw[i];
+          acc[4 * i] = __fadd_rn(acc[4 * i], v.x);
+          acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], v.y);
+          acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], v.z);
+          acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], v.w);
+        }
+      }
       float4* dst = reinterpret_cast<float4*>(a.recon + grow * kDim);
-      const float* rc = &sm.recon[row * kRStride];
 #pragma unroll
       for (int i = 0; i < kDim / 4; ++i)
-        dst[i] = make_float4(rc[4 * i], rc[4 * i + 1], rc[4 * i + 2], rc[4 * i + 3]);
+        dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
       if (a.residual_out) {
         float4* res = reinterpret_cast<float4*>(a.residual_out + grow * kDim);
 #pragma unroll
@@ -587,7 +665,6 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           res[i] = make_float4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
       }
     }
-    if (aborted) sm.abort_flag = 1;
   }
 
   tc_fence_before();
@@ -612,7 +689,7 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
   const char* name = "moss_rvq_encode";
   if (rows < 0 || stages < 1 || k < 1) return fail(MOSS_ERR_VALUE, "%s: bad shape", name);
   if (d != rvqtc::kDim) return fail(MOSS_ERR_UNSUPPORTED, "%s: only 64-dim codewords are supported", name);
-  if (k > 4096 || stages > 65535)
+  if (k > rvqtc::kMaxCodes || stages > 65535)
     return fail(MOSS_ERR_UNSUPPORTED, "%s: at most 4096 codes per stage (use moss_rvq_encode_ffma)", name);
   if (rows == 0) return MOSS_OK;
   if (!x || !books || !packed || !code_norm || !stats || !codes || !recon)
@@ -634,7 +711,7 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
     if (e != cudaSuccess) return fail(MOSS_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  // The tensor-core image follows the FFMA layout in the packed buffer.
+  // The tensor-core tile images follow the FFMA layout in the packed buffer.
   const float* image = packed + stages * kpad * rvqtc::kDim;
   rvqtc::Args args{x, books, image, code_norm, stats, codes, recon, residual_out, rows,
                    static_cast<int>(stages), static_cast<int>(k), static_cast<int>(kpad)};

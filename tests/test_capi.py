@@ -73,7 +73,11 @@ def test_bad_arguments_map_to_value_errors(lib):
                                None) == _lib.ERR_VALUE
     # empty inputs are a no-op success
     assert lib.moss_scale_add(None, 0, None, 0, None, None, 0, 4, None) == _lib.OK
-    assert lib.moss_rvq_packed_floats(32, 1000, 64) == 32 * 1024 * 64
+    # k-major copy + tensor-core tile images (256 codes x (64 dims + an 8-wide
+    # norm block) each), codes padded to a multiple of 256
+    assert lib.moss_rvq_packed_floats(32, 1000, 64) == 32 * 1024 * 64 + 32 * 4 * 256 * 72
+    assert lib.moss_rvq_encode_ffma(None, 8, 32, None, None, None, None, 1, 4, None, None, None,
+                                    None) == _lib.ERR_UNSUPPORTED
 
 
 def test_python_wrappers_raise_reference_exceptions():
