@@ -81,17 +81,86 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& v, float* f) {
     f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
   }
 }
+// Two float32 values rounded (nearest even) to bf16 and packed, lo in the
+// low half: the same rounding as one scalar conversion per value.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 __device__ __forceinline__ uint4 pack_bf16x8(const float* f) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    w[i] = static_cast<uint32_t>(f32_to_bf16_bits(f[2 * i])) |
-           (static_cast<uint32_t>(f32_to_bf16_bits(f[2 * i + 1])) << 16);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+// Packed bf16 arithmetic, one correctly rounded (nearest even) result per
+// half.  The sum of two bf16 values rounds to the same bf16 value as the
+// float32 sum rounded to bf16 (the float32 sum is exact whenever the
+// exponents differ by at most 15; otherwise both round to the larger
+// operand).  The same holds for the product whenever its magnitude is at
+// least 2^-125; below that the float32 product can be inexact, so callers
+// recompute results whose exponent field is 0 or 1.
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// True when either half has a biased exponent of 0 or 1 (|v| < 2^-125).
+__device__ __forceinline__ bool bf16x2_tiny(uint32_t v) {
+  return (v & 0x7f00u) == 0u || (v & 0x7f000000u) == 0u;
+}
+
+// Division of numerators n < 2^31 by a run-time constant d >= 1 with one
+// multiply-high and two shifts (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994): with
+// l = ceil(log2 d) and m = ceil(2^(31+l) / d) < 2^32,
+// floor(n / d) = floor(m n / 2^(31+l)) = umulhi(m, 2n) >> l.
+struct FastDiv {
+  uint32_t d, m, l;
+};
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const unsigned long long m = ((1ull << (31 + l)) + d - 1) / d;
+  return FastDiv{d, static_cast<uint32_t>(m), l};
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv& f) {
+  return __umulhi(f.m, n << 1) >> f.l;
 }
 
 // Multiprocessor count of the current device (cached per device).
 int sm_count();
+
+// Raises the dynamic shared memory limit of `kernel` on the current device
+// once; `done` is the caller's per-kernel flag array indexed by device.
+constexpr int kMaxDevices = 64;
+template <typename K>
+inline void allow_dynamic_smem(K kernel, size_t bytes, bool* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (!done[dev]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(bytes));
+    done[dev] = true;
+  }
+}
+
+// Blocks of 256 threads of `kernel` that are resident on the whole device at
+// once (a persistent grid), capped at `work` and at least 1.
+template <typename K>
+inline int64_t persistent_grid(K kernel, size_t shmem, int64_t work) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, shmem) != cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  int64_t grid = static_cast<int64_t>(sm_count()) * per_sm;
+  if (grid > work) grid = work;
+  return grid < 1 ? 1 : grid;
+}
 
 }  // namespace moss

@@ -10,15 +10,64 @@
 //            gelu_tanh(v) = 0.5 * v * (1 + tanhf(k_beta * fma(0.044715, v^3, v)))
 //   y    = round(a * h_up)              (gated)   or   y = a (ungated)
 // For bf16 with the gate width a multiple of 8, each thread produces 8
-// outputs from 16-byte loads of the gate half, the up half and the bias.
-#include "common.cuh"
+// outputs from 16-byte loads of the gate half, the up half and the bias;
+// the bias adds and the gating product run as packed bf16 operations,
+// which give the same bits as the float32 op followed by the bf16 rounding.
+#include "pipeline.cuh"
 
 namespace moss {
 
-template <int ACT>
+// silu(v) = v / (1 + expf(-v)) when only its bf16 rounding is kept.
+//
+// Fast form: e^-v = 2^th * 2^tl with th = v * L rounded and tl the rest of
+// v * -log2(e) (one FMA gives v * L - th exactly, a second adds v times the
+// tail of the constant), so e = ex2.approx(th) * (1 + ln2 tl) carries the
+// error of ex2.approx (taken as 2^-21.5) and one rounding, independent of
+// |v|; q = v * rcp.approx(1 + e) adds two roundings and the 2^-23 of
+// rcp.approx.  That is within 11 units in the last place of q; the float32
+// value torch computes (expf within 2 ulp, two roundings) is within 6 of
+// the exact quotient, so the two round to the same bf16 value unless the
+// fast quotient's low 16 bits lie within 32 units of the rounding midpoint
+// 0x8000.  Those cases, |v| > 64 (where 1 + e or its reciprocal could leave
+// the normal range) and |v| < 2^-100 (zero, subnormal or NaN v) take the
+// exact torch formula.  The input is itself a bf16 value, so the exhaustive
+// test over all 65536 inputs checks the claim on the hardware.
+__device__ __forceinline__ float silu_exact(float v) {
+  return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+}
+
+__device__ __forceinline__ float silu_fast(float v, bool& risky) {
+  const float kL = -1.44269502162933349609375f;   // -log2(e) rounded to float
+  const float kLlo = -1.925963033500011e-08f;     // -log2(e) - kL
+  const float kLn2 = 0.693147182464599609375f;
+  const float th = __fmul_rn(v, kL);
+  const float tl = __fmaf_rn(v, kLlo, __fmaf_rn(v, kL, -th));
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(th));
+  e = __fmaf_rn(e, __fmul_rn(kLn2, tl), e);
+  const float d = __fadd_rn(1.0f, e);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  const float q = __fmul_rn(v, r);
+  const float av = fabsf(v);
+  risky = ((__float_as_uint(q) + 32u) & 0xffc0u) == 0x8000u || !(av <= 64.0f) ||
+          !(av >= 7.888609052e-31f);
+  return q;
+}
+
+__device__ __forceinline__ float silu_for_bf16(float v) {
+  bool risky;
+  const float q = silu_fast(v, risky);
+  return risky ? silu_exact(v) : q;
+}
+
+template <int ACT, int DT>
 __device__ __forceinline__ float activation(float v) {
   if constexpr (ACT == MOSS_ACT_SILU) {
-    return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    if constexpr (DT == MOSS_BF16) {
+      return silu_for_bf16(v);
+    } else {
+      return __fdiv_rn(v, __fadd_rn(1.0f, expf(-v)));
+    }
   } else if constexpr (ACT == MOSS_ACT_GELU_ERF) {
     const float k_alpha = 0.70710678118654752440f;
     return __fmul_rn(__fmul_rn(v, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(v, k_alpha))));
@@ -31,52 +80,139 @@ __device__ __forceinline__ float activation(float v) {
   }
 }
 
+// Without a bias there is no add at all (so -0 stays -0, as in torch).
 template <int DT, int ACT, bool GATED>
-__device__ __forceinline__ float gate_value(float xg, float bg, float xu, float bu) {
-  const float hg = round_to<DT>(__fadd_rn(xg, bg));
-  const float a = round_to<DT>(activation<ACT>(hg));
+__device__ __forceinline__ float gate_value(float xg, float bg, float xu, float bu, bool hasb) {
+  const float hg = hasb ? round_to<DT>(__fadd_rn(xg, bg)) : xg;
+  const float a = round_to<DT>(activation<ACT, DT>(hg));
   if constexpr (GATED) {
-    const float hu = round_to<DT>(__fadd_rn(xu, bu));
+    const float hu = hasb ? round_to<DT>(__fadd_rn(xu, bu)) : xu;
     return __fmul_rn(a, hu);
   } else {
     return a;
   }
 }
 
-// Vector path (bf16, 8 outputs per item).  out_w = width of the output row.
+// Eight bf16 outputs (four packed pairs) from packed gate, bias and up
+// values, without branches.  Bit j of `redo` is set when output j must be
+// recomputed by gate_exact_one: SiLU near a bf16 rounding midpoint (see
+// silu_fast) or a gating product below 2^-125 (see bf16x2_mul).
+template <int ACT, bool GATED>
+__device__ __forceinline__ uint4 gate_item_fast(const uint4& g4, const uint4& bg4, const uint4& u4,
+                                                const uint4& bu4, bool has_bias, uint32_t& redo) {
+  const uint32_t xg[4] = {g4.x, g4.y, g4.z, g4.w};
+  const uint32_t bg[4] = {bg4.x, bg4.y, bg4.z, bg4.w};
+  uint32_t a[4];
+  redo = 0;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t hg = has_bias ? bf16x2_add(xg[p], bg[p]) : xg[p];  // exact
+    const float v0 = __uint_as_float(hg << 16), v1 = __uint_as_float(hg & 0xffff0000u);
+    if constexpr (ACT == MOSS_ACT_SILU) {
+      bool r0, r1;
+      const float q0 = silu_fast(v0, r0), q1 = silu_fast(v1, r1);
+      redo |= (static_cast<uint32_t>(r0) | (static_cast<uint32_t>(r1) << 1)) << (2 * p);
+      a[p] = pack_bf16x2(q0, q1);
+    } else {
+      a[p] = pack_bf16x2(activation<ACT, MOSS_BF16>(v0), activation<ACT, MOSS_BF16>(v1));
+    }
+  }
+  if constexpr (GATED) {
+    const uint32_t xu[4] = {u4.x, u4.y, u4.z, u4.w};
+    const uint32_t bu[4] = {bu4.x, bu4.y, bu4.z, bu4.w};
+    uint32_t y[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t hu = has_bias ? bf16x2_add(xu[p], bu[p]) : xu[p];
+      y[p] = bf16x2_mul(a[p], hu);
+      redo |= static_cast<uint32_t>(bf16x2_tiny(y[p])) * (3u << (2 * p));
+    }
+    return make_uint4(y[0], y[1], y[2], y[3]);
+  } else {
+    return make_uint4(a[0], a[1], a[2], a[3]);
+  }
+}
+
+// One output from its bf16 inputs, the torch chain op by op in float32.
+template <int ACT, bool GATED>
+__device__ __forceinline__ uint16_t gate_exact_one(uint16_t xg, uint16_t bg, uint16_t xu,
+                                                   uint16_t bu, bool has_bias) {
+  const float hg = has_bias ? round_to<MOSS_BF16>(__fadd_rn(bf16_bits_to_f32(xg), bf16_bits_to_f32(bg)))
+                            : bf16_bits_to_f32(xg);
+  const float av = ACT == MOSS_ACT_SILU ? silu_exact(hg) : activation<ACT, MOSS_BF16>(hg);
+  const float a = round_to<MOSS_BF16>(av);
+  if constexpr (GATED) {
+    const float hu = has_bias ? round_to<MOSS_BF16>(__fadd_rn(bf16_bits_to_f32(xu), bf16_bits_to_f32(bu)))
+                              : bf16_bits_to_f32(xu);
+    return f32_to_bf16_bits(__fmul_rn(a, hu));
+  } else {
+    return f32_to_bf16_bits(a);
+  }
+}
+
+// Register-path item: fast outputs, then the flagged ones exactly (a
+// warp-uniform test first, so the exact code runs only when needed).
+template <int ACT, bool GATED>
+__device__ __forceinline__ uint4 gate_item(const uint4& g4, const uint4& bg4, const uint4& u4,
+                                           const uint4& bu4, bool has_bias) {
+  uint32_t redo;
+  uint4 y = gate_item_fast<ACT, GATED>(g4, bg4, u4, bu4, has_bias, redo);
+  if (__builtin_expect(__any_sync(__activemask(), redo != 0u), 0)) {
+    uint32_t w[4] = {y.x, y.y, y.z, y.w};
+    const uint32_t xg[4] = {g4.x, g4.y, g4.z, g4.w}, bg[4] = {bg4.x, bg4.y, bg4.z, bg4.w};
+    const uint32_t xu[4] = {u4.x, u4.y, u4.z, u4.w}, bu[4] = {bu4.x, bu4.y, bu4.z, bu4.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((redo >> j) & 1u) {
+        const int p = j >> 1, sh = (j & 1) * 16;
+        const uint16_t o = gate_exact_one<ACT, GATED>(
+            static_cast<uint16_t>(xg[p] >> sh), static_cast<uint16_t>(bg[p] >> sh),
+            static_cast<uint16_t>(xu[p] >> sh), static_cast<uint16_t>(bu[p] >> sh), has_bias);
+        w[p] = (w[p] & ~(0xffffu << sh)) | (static_cast<uint32_t>(o) << sh);
+      }
+    }
+    y = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  return y;
+}
+
+// Vector path (bf16, 8 outputs per item).  out_w = width of the output row;
+// rows * out_w / 8 < 2^31 (the host splits larger calls into row chunks).
 template <int ACT, bool GATED>
 __global__ void __launch_bounds__(256) gated_act_bf16x8_kernel(
     const uint16_t* __restrict__ x, const uint16_t* __restrict__ bias, uint16_t* __restrict__ y,
-    int64_t rows, int64_t width, int64_t out_w) {
-  const int64_t per_row = out_w / 8;
-  const int64_t items = rows * per_row;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; it < items;
-       it += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = it / per_row;
-    const int64_t c = (it - r * per_row) * 8;
-    float xg[8], bg[8], xu[8], bu[8], out[8];
-    unpack_bf16x8(*reinterpret_cast<const uint4*>(x + r * width + c), xg);
-    if (bias) {
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(bias + c), bg);
-    } else {
+    uint32_t items, FastDiv per_row, int64_t width, int64_t out_w) {
+  // Two items per iteration: all of their loads are issued before any math.
+  constexpr int kU = 2;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  const bool has_bias = bias != nullptr;
+  for (uint32_t it0 = blockIdx.x * blockDim.x + threadIdx.x; it0 < items; it0 += kU * stride) {
+    uint4 rg[kU], rb[kU], ru[kU], rbu[kU];
+    int64_t dst[kU];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) bg[i] = 0.0f;
-    }
-    if constexpr (GATED) {
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(x + r * width + out_w + c), xu);
-      if (bias) {
-        unpack_bf16x8(*reinterpret_cast<const uint4*>(bias + out_w + c), bu);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) bu[i] = 0.0f;
+    for (int j = 0; j < kU; ++j) {
+      const uint32_t it = it0 + j * stride;
+      rg[j] = rb[j] = ru[j] = rbu[j] = zero;
+      dst[j] = -1;
+      if (it < items) {
+        const uint32_t r = fast_div(it, per_row);
+        const int64_t c = static_cast<int64_t>(it - r * per_row.d) * 8;
+        const uint16_t* xr = x + static_cast<int64_t>(r) * width + c;
+        rg[j] = *reinterpret_cast<const uint4*>(xr);
+        if (has_bias) rb[j] = *reinterpret_cast<const uint4*>(bias + c);
+        if constexpr (GATED) {
+          ru[j] = *reinterpret_cast<const uint4*>(xr + out_w);
+          if (has_bias) rbu[j] = *reinterpret_cast<const uint4*>(bias + out_w + c);
+        }
+        dst[j] = static_cast<int64_t>(r) * out_w + c;
       }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      out[i] = gate_value<MOSS_BF16, ACT, GATED>(xg[i], bg[i], GATED ? xu[i] : 0.0f,
-                                                 GATED ? bu[i] : 0.0f);
+    for (int j = 0; j < kU; ++j) {
+      if (dst[j] < 0) continue;
+      *reinterpret_cast<uint4*>(y + dst[j]) = gate_item<ACT, GATED>(rg[j], rb[j], ru[j], rbu[j], has_bias);
     }
-    *reinterpret_cast<uint4*>(y + r * out_w + c) = pack_bf16x8(out);
   }
 }
 
@@ -97,7 +233,231 @@ __global__ void __launch_bounds__(256) gated_act_scalar_kernel(const void* __res
       xu = load_as_f32<DT>(x, r * width + out_w + c);
       bu = bias ? load_as_f32<DT>(bias, out_w + c) : 0.0f;
     }
-    store_from_f32<DT>(y, it, gate_value<DT, ACT, GATED>(xg, bg, xu, bu));
+    store_from_f32<DT>(y, it, gate_value<DT, ACT, GATED>(xg, bg, xu, bu, bias != nullptr));
+  }
+}
+
+// Activation tables.  The activation of a bf16 input rounded to bf16 is a
+// function of the 65536 input bit patterns only, so each activation is
+// tabulated once per device with the exact torch formula (activation_exact)
+// and the streaming kernel looks the values up: every output is then the
+// torch value by construction, whatever the input.
+__device__ __align__(16) uint16_t g_act_lut[3 * 65536];
+
+template <int ACT>
+__device__ __forceinline__ float activation_exact(float v) {
+  if constexpr (ACT == MOSS_ACT_SILU) {
+    return silu_exact(v);
+  } else {
+    return activation<ACT, MOSS_BF16>(v);
+  }
+}
+
+__global__ void act_lut_kernel() {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;  // grid covers 65536 exactly
+  const float v = bf16_bits_to_f32(static_cast<uint16_t>(h));
+  g_act_lut[h] = f32_to_bf16_bits(activation_exact<MOSS_ACT_SILU>(v));
+  g_act_lut[65536 + h] = f32_to_bf16_bits(activation_exact<MOSS_ACT_GELU_ERF>(v));
+  g_act_lut[2 * 65536 + h] = f32_to_bf16_bits(activation_exact<MOSS_ACT_GELU_TANH>(v));
+}
+
+// Builds the tables on the current device at its first use, on `s` (stream
+// order makes them visible to the kernels launched after it).
+static void ensure_act_lut(cudaStream_t s) {
+  static bool ready[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
+  if (!ready[dev]) {
+    act_lut_kernel<<<65536 / 256, 256, 0, s>>>();
+    ready[dev] = true;
+  }
+}
+
+// Streaming path (bf16, rows of at most kStageBytes): one CTA per SM.  A
+// producer thread streams tiles of whole rows of x into a ring of
+// shared-memory stages with bulk copies (the activation table once, beside
+// them); the consumer warps compute 8 outputs per 16-byte item from shared
+// memory and store them straight to y.  A consumer thread handles the same
+// (row in tile, column) items in every tile, so its bias values stay in
+// registers.
+namespace gstream {
+#ifndef MOSS_STREAM_CONSUMERS
+#define MOSS_STREAM_CONSUMERS 512
+#endif
+constexpr int kConsumers = MOSS_STREAM_CONSUMERS;
+constexpr int kThreads = kConsumers + 32;
+constexpr int kStages = 6;
+constexpr int kStageBytes = 16384;
+constexpr int kLutBytes = 65536 * 2;
+// 16-byte output items per consumer thread and tile (a stage holds at most
+// kStageBytes / 16 items of gate input).
+constexpr int kSlots = (kStageBytes / 16 + kConsumers - 1) / kConsumers;
+
+struct Args {
+  const uint16_t* x;
+  const uint16_t* bias;
+  uint16_t* y;
+  int64_t rows, width, out_w;
+  int tile_rows;        // rows per stage
+  uint32_t ntiles;
+  FastDiv per_row;      // 16-byte output items per row (out_w / 8)
+};
+
+// Layout: stages | table | barriers.
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + kLutBytes +
+                              (2 * kStages + 2) * 8;
+}  // namespace gstream
+
+// Two adjacent outputs from a packed pair of rounded gate inputs.
+__device__ __forceinline__ uint32_t lut_pair(const uint16_t* lut, uint32_t hg) {
+  return static_cast<uint32_t>(lut[hg & 0xffffu]) | (static_cast<uint32_t>(lut[hg >> 16]) << 16);
+}
+
+template <int ACT, bool GATED>
+__global__ void __launch_bounds__(gstream::kThreads, 1)
+    gated_act_stream_kernel(const gstream::Args a) {
+  using namespace gstream;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const uint16_t* lut = reinterpret_cast<const uint16_t*>(smem + kStages * kStageBytes);
+  unsigned long long* full =
+      reinterpret_cast<unsigned long long*>(smem + kStages * kStageBytes + kLutBytes);
+  unsigned long long* empty = full + kStages;
+  unsigned long long* lut_bar = full + 2 * kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2 * kStages + 1);
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      pipe::mbar_init(&full[s], 1);
+      pipe::mbar_init(&empty[s], kConsumers / 32);
+    }
+    pipe::mbar_init(lut_bar, 1);
+    *abort_flag = 0;
+    pipe::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (tid >= kConsumers) {  // producer warp: one thread issues every copy
+    if (tid != kConsumers) return;
+    uint32_t i = 0;
+    for (uint32_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x, ++i) {
+      const int s = static_cast<int>(i % kStages);
+      if (i >= kStages && !pipe::mbar_wait(&empty[s], ((i / kStages) - 1) & 1)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      const int64_t r0 = static_cast<int64_t>(tile) * a.tile_rows;
+      const int64_t nr = a.rows - r0 < a.tile_rows ? a.rows - r0 : a.tile_rows;
+      const uint32_t bytes = static_cast<uint32_t>(nr * a.width * 2);
+      pipe::mbar_arrive_expect_tx(&full[s], bytes);
+      pipe::bulk_g2s(smem + s * kStageBytes, a.x + r0 * a.width, bytes, &full[s]);
+      if (i == 0) {  // the first data tile is in flight; now the table
+        pipe::mbar_arrive_expect_tx(lut_bar, kLutBytes);
+        pipe::bulk_g2s(smem + kStages * kStageBytes, g_act_lut + ACT * 65536, kLutBytes, lut_bar);
+      }
+    }
+    // Drain: the copies of the last issued tiles must land before exit.
+    for (uint32_t j = i > kStages ? i - kStages : 0; j < i; ++j)
+      pipe::mbar_wait(&full[j % kStages], (j / kStages) & 1);
+    if (i > 0) pipe::mbar_wait(lut_bar, 0);
+    return;
+  }
+
+  // Consumer warps (the grid never exceeds the tile count, so every CTA
+  // has a first tile and the table copy is issued).
+  const int lane = tid & 31;
+  const bool has_bias = a.bias != nullptr;
+  const uint32_t full_items = static_cast<uint32_t>(a.tile_rows) * a.per_row.d;
+  uint32_t row[kSlots], col[kSlots];  // row in the tile (large: no item), column
+  uint32_t bg[kSlots][4], bu[kSlots][4];
+#pragma unroll
+  for (int m = 0; m < kSlots; ++m) {
+    const uint32_t it = tid + m * kConsumers;
+    row[m] = 0x7fffffffu;
+    col[m] = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) bg[m][p] = bu[m][p] = 0u;
+    if (it < full_items) {
+      row[m] = fast_div(it, a.per_row);
+      col[m] = (it - row[m] * a.per_row.d) * 8;
+      if (has_bias) {
+        const uint4 b = *reinterpret_cast<const uint4*>(a.bias + col[m]);
+        bg[m][0] = b.x; bg[m][1] = b.y; bg[m][2] = b.z; bg[m][3] = b.w;
+        if constexpr (GATED) {
+          const uint4 c = *reinterpret_cast<const uint4*>(a.bias + a.out_w + col[m]);
+          bu[m][0] = c.x; bu[m][1] = c.y; bu[m][2] = c.z; bu[m][3] = c.w;
+        }
+      }
+    }
+  }
+  if (!pipe::mbar_wait(lut_bar, 0)) {
+    *abort_flag = 1;
+    return;
+  }
+  uint32_t i = 0;
+  for (uint32_t tile = blockIdx.x; tile < a.ntiles; tile += gridDim.x, ++i) {
+    const int s = static_cast<int>(i % kStages);
+    if (*abort_flag || !pipe::mbar_wait(&full[s], (i / kStages) & 1)) {
+      *abort_flag = 1;
+      return;
+    }
+    const int64_t r0 = static_cast<int64_t>(tile) * a.tile_rows;
+    const uint32_t nr = static_cast<uint32_t>(a.rows - r0 < a.tile_rows ? a.rows - r0 : a.tile_rows);
+    const uint16_t* st = reinterpret_cast<const uint16_t*>(smem + s * kStageBytes);
+    uint16_t* yt = a.y + r0 * a.out_w;
+    // Products below 2^-125 (see bf16x2_mul) are flagged and redone in
+    // float32 afterwards, so the main loop has no data-dependent branch.
+    uint32_t redo_all = 0;
+#pragma unroll
+    for (int m = 0; m < kSlots; ++m) {
+      if (row[m] < nr) {
+        const uint16_t* xr = st + row[m] * static_cast<uint32_t>(a.width) + col[m];
+        const uint4 g4 = *reinterpret_cast<const uint4*>(xr);
+        uint32_t out[4] = {g4.x, g4.y, g4.z, g4.w};
+        uint4 u4 = make_uint4(0u, 0u, 0u, 0u);
+        if constexpr (GATED) u4 = *reinterpret_cast<const uint4*>(xr + a.out_w);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          if (has_bias) out[p] = bf16x2_add(out[p], bg[m][p]);  // exact, see bf16x2_add
+          out[p] = lut_pair(lut, out[p]);
+        }
+        if constexpr (GATED) {
+          uint32_t xu[4] = {u4.x, u4.y, u4.z, u4.w};
+          uint32_t tiny = 0;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            if (has_bias) xu[p] = bf16x2_add(xu[p], bu[m][p]);
+            out[p] = bf16x2_mul(out[p], xu[p]);
+            tiny |= static_cast<uint32_t>(bf16x2_tiny(out[p])) << p;
+          }
+          redo_all |= tiny << (4 * m);
+        }
+        *reinterpret_cast<uint4*>(yt + static_cast<int64_t>(row[m]) * a.out_w + col[m]) =
+            make_uint4(out[0], out[1], out[2], out[3]);
+      }
+    }
+    if constexpr (GATED) {
+      const uint32_t am = __activemask();
+      if (__builtin_expect(__any_sync(am, redo_all != 0u), 0)) {
+        for (int m = 0; m < kSlots; ++m) {
+          if (!((redo_all >> (4 * m)) & 0xfu)) continue;
+          const uint16_t* xr = st + row[m] * static_cast<uint32_t>(a.width) + col[m];
+          for (int j = 0; j < 8; ++j) {
+            if (!((redo_all >> (4 * m + j / 2)) & 1u)) continue;
+            float g = bf16_bits_to_f32(xr[j]), u = bf16_bits_to_f32(xr[a.out_w + j]);
+            if (has_bias) {
+              g = round_to<MOSS_BF16>(__fadd_rn(g, bf16_bits_to_f32(a.bias[col[m] + j])));
+              u = round_to<MOSS_BF16>(__fadd_rn(u, bf16_bits_to_f32(a.bias[a.out_w + col[m] + j])));
+            }
+            const float av = bf16_bits_to_f32(lut[f32_to_bf16_bits(g)]);
+            yt[static_cast<int64_t>(row[m]) * a.out_w + col[m] + j] =
+                f32_to_bf16_bits(__fmul_rn(av, u));
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) pipe::mbar_arrive(&empty[s]);
   }
 }
 
@@ -105,13 +465,39 @@ template <int ACT, bool GATED>
 static void launch_gated(const void* x, const void* bias, void* y, int dtype, int64_t rows,
                          int64_t width, int64_t out_w, bool vec, cudaStream_t s) {
   const int sms = sm_count();
+  if (vec && width * 2 <= gstream::kStageBytes && rows < 0x7fffffffLL) {
+    ensure_act_lut(s);
+    gstream::Args a{};
+    a.x = static_cast<const uint16_t*>(x);
+    a.bias = static_cast<const uint16_t*>(bias);
+    a.y = static_cast<uint16_t*>(y);
+    a.rows = rows;
+    a.width = width;
+    a.out_w = out_w;
+    a.tile_rows = static_cast<int>(gstream::kStageBytes / (width * 2));
+    a.ntiles = static_cast<uint32_t>((rows + a.tile_rows - 1) / a.tile_rows);
+    a.per_row = make_fastdiv(static_cast<uint32_t>(out_w / 8));
+    const size_t shmem = gstream::kSmemBytes;
+    static bool attr_done[kMaxDevices] = {};  // per instantiation and device
+    allow_dynamic_smem(gated_act_stream_kernel<ACT, GATED>, shmem, attr_done);
+    const uint32_t grid = a.ntiles < static_cast<uint32_t>(sms) ? a.ntiles : static_cast<uint32_t>(sms);
+    gated_act_stream_kernel<ACT, GATED><<<grid, gstream::kThreads, shmem, s>>>(a);
+    return;
+  }
   if (vec) {
-    const int64_t items = rows * (out_w / 8);
-    int64_t grid = (items + 255) / 256;
-    if (grid > static_cast<int64_t>(sms) * 8) grid = static_cast<int64_t>(sms) * 8;
-    gated_act_bf16x8_kernel<ACT, GATED><<<static_cast<unsigned>(grid), 256, 0, s>>>(
-        static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(bias),
-        static_cast<uint16_t*>(y), rows, width, out_w);
+    // Row chunks of fewer than 2^31 items of 8 outputs.
+    const int64_t per_row = out_w / 8;
+    const int64_t chunk = 0x7fffffffLL / per_row;
+    const FastDiv fd = make_fastdiv(static_cast<uint32_t>(per_row));
+    for (int64_t r0 = 0; r0 < rows; r0 += chunk) {
+      const int64_t nr = rows - r0 < chunk ? rows - r0 : chunk;
+      const int64_t items = nr * per_row;
+      int64_t grid = (items + 255) / 256;
+      if (grid > static_cast<int64_t>(sms) * 8) grid = static_cast<int64_t>(sms) * 8;
+      gated_act_bf16x8_kernel<ACT, GATED><<<static_cast<unsigned>(grid), 256, 0, s>>>(
+          static_cast<const uint16_t*>(x) + r0 * width, static_cast<const uint16_t*>(bias),
+          static_cast<uint16_t*>(y) + r0 * out_w, static_cast<uint32_t>(items), fd, width, out_w);
+    }
   } else {
     const int64_t items = rows * out_w;
     int64_t grid = (items + 255) / 256;

@@ -8,9 +8,9 @@
 // multiple of 4 (and 16-byte aligned pointers) PyTorch runs its vectorised
 // layer-norm forward, whose arithmetic is reproduced here operation for
 // operation:
-//   * a block of 128 threads (4 warps of 32) per row; thread j (j = lane +
-//     32*warp) reads float4 vectors j, j+128, j+256, ... and pushes their
-//     elements, in order, through a Welford update with a float count:
+//   * a block of 128 threads (4 warps of 32) per row; thread j reads float4
+//     vectors j, j+128, j+256, ... and pushes their elements, in order,
+//     through a Welford update with a float count:
 //       delta = v - mean; count += 1; mean = fma(delta, 1/count, mean);
 //       m2 = fma(delta, v - mean, m2)
 //   * a shuffle-down tree (offsets 16..1) inside each warp, then a two-level
@@ -21,10 +21,12 @@
 //       m2 = fma(delta*delta*cA, nB, m2A + m2B),  delta = meanB - meanA
 //   * var = m2 / n; rstd = rsqrtf(var + eps);
 //     y = fma(gamma, rstd * (x - mean), beta).
-// The 128-thread block is emulated by ONE warp per row: lane L carries the
-// four Welford states of the virtual threads L, L+32, L+64, L+96 and runs the
-// four shuffle trees side by side, so no shared memory and no block barrier
-// is needed and a CTA streams several rows at once.
+// The kernel uses the same 128-thread row blocks, so every thread holds at
+// most four float4 vectors (n <= 2048) in ~40 registers and up to 16 rows
+// are resident per SM, keeping enough loads in flight for HBM.  The
+// reciprocals of the per-thread Welford counts (1..16) are compile-time
+// constants (IEEE division evaluated by the compiler); the merges use the
+// correctly rounded reciprocal instruction.
 #include "common.cuh"
 
 namespace moss {
@@ -35,12 +37,19 @@ struct Welford {
   float count;
 };
 
-__device__ __forceinline__ Welford welford_push(Welford w, float v) {
+// 1/c for c = 0..16, correctly rounded (c = 0 unused).
+__device__ __constant__ float kRcpSmall[17] = {
+    0.0f,        1.0f / 1.0f,  1.0f / 2.0f,  1.0f / 3.0f,  1.0f / 4.0f,  1.0f / 5.0f,
+    1.0f / 6.0f, 1.0f / 7.0f,  1.0f / 8.0f,  1.0f / 9.0f,  1.0f / 10.0f, 1.0f / 11.0f,
+    1.0f / 12.0f, 1.0f / 13.0f, 1.0f / 14.0f, 1.0f / 15.0f, 1.0f / 16.0f};
+
+// Welford update to the new count c (1 <= c <= 16), whose reciprocal comes
+// from the table (a constant-bank operand once the loops are unrolled).
+__device__ __forceinline__ Welford welford_push(Welford w, float v, int c) {
   const float delta = __fsub_rn(v, w.mean);
-  const float count = __fadd_rn(w.count, 1.0f);
-  const float mean = __fmaf_rn(delta, __frcp_rn(count), w.mean);
+  const float mean = __fmaf_rn(delta, kRcpSmall[c], w.mean);
   const float m2 = __fmaf_rn(delta, __fsub_rn(v, mean), w.m2);
-  return {mean, m2, count};
+  return {mean, m2, static_cast<float>(c)};
 }
 
 // Merge of the thread's own state b with a partner state a.
@@ -57,33 +66,6 @@ __device__ __forceinline__ Welford welford_merge(Welford b, Welford a) {
     return {mean, m2, count};
   }
   return {0.0f, 0.0f, count};
-}
-
-__device__ __forceinline__ Welford shfl_down_welford(const Welford& w, int offset) {
-  Welford o;
-  o.mean = __shfl_down_sync(0xffffffffu, w.mean, offset);
-  o.m2 = __shfl_down_sync(0xffffffffu, w.m2, offset);
-  o.count = __shfl_down_sync(0xffffffffu, w.count, offset);
-  return o;
-}
-
-// Reduces the four virtual-warp states of every lane to the row statistics
-// (mean, m2) exactly as the 4-warp block would, and broadcasts them.
-__device__ __forceinline__ void reduce_row_stats(Welford (&w)[4], float& mean, float& m2) {
-#pragma unroll
-  for (int offset = 16; offset > 0; offset >>= 1) {
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const Welford other = shfl_down_welford(w[v], offset);
-      w[v] = welford_merge(w[v], other);
-    }
-  }
-  // Cross-warp tree of the emulated block (lane 0 holds each warp result).
-  Welford w0 = welford_merge(w[0], w[2]);
-  const Welford w1 = welford_merge(w[1], w[3]);
-  w0 = welford_merge(w0, w1);
-  mean = __shfl_sync(0xffffffffu, w0.mean, 0);
-  m2 = __shfl_sync(0xffffffffu, w0.m2, 0);
 }
 
 template <int DT>
@@ -108,97 +90,120 @@ __device__ __forceinline__ float scale_add1(float x, float u, float s) {
   return __fadd_rn(x, __fmul_rn(u, s));
 }
 
-// One warp per row; NV = number of float4 vectors each lane holds (row width
-// n <= 128*NV).  HAS_U selects the fused residual form.
-template <int NV, int XDT, int UDT, bool HAS_U>
-__global__ void __launch_bounds__(256) residual_ln_kernel(
+__device__ __forceinline__ float4 ln_out(float4 v, float mean, float rstd, const float* gamma,
+                                         const float* beta, int i) {
+  float4 o;
+  if (gamma && beta) {
+    // gamma * (rstd * (x - mean)) + beta with the outer multiply-add fused
+    const float4 g = reinterpret_cast<const float4*>(gamma)[i];
+    const float4 b = reinterpret_cast<const float4*>(beta)[i];
+    o.x = __fmaf_rn(g.x, __fmul_rn(rstd, __fsub_rn(v.x, mean)), b.x);
+    o.y = __fmaf_rn(g.y, __fmul_rn(rstd, __fsub_rn(v.y, mean)), b.y);
+    o.z = __fmaf_rn(g.z, __fmul_rn(rstd, __fsub_rn(v.z, mean)), b.z);
+    o.w = __fmaf_rn(g.w, __fmul_rn(rstd, __fsub_rn(v.w, mean)), b.w);
+  } else if (gamma) {
+    const float4 g = reinterpret_cast<const float4*>(gamma)[i];
+    o.x = __fmul_rn(g.x, __fmul_rn(rstd, __fsub_rn(v.x, mean)));
+    o.y = __fmul_rn(g.y, __fmul_rn(rstd, __fsub_rn(v.y, mean)));
+    o.z = __fmul_rn(g.z, __fmul_rn(rstd, __fsub_rn(v.z, mean)));
+    o.w = __fmul_rn(g.w, __fmul_rn(rstd, __fsub_rn(v.w, mean)));
+  } else if (beta) {
+    // without gamma the product rstd * (x - mean) itself fuses with the add
+    const float4 b = reinterpret_cast<const float4*>(beta)[i];
+    o.x = __fmaf_rn(rstd, __fsub_rn(v.x, mean), b.x);
+    o.y = __fmaf_rn(rstd, __fsub_rn(v.y, mean), b.y);
+    o.z = __fmaf_rn(rstd, __fsub_rn(v.z, mean), b.z);
+    o.w = __fmaf_rn(rstd, __fsub_rn(v.w, mean), b.w);
+  } else {
+    o.x = __fmul_rn(rstd, __fsub_rn(v.x, mean));
+    o.y = __fmul_rn(rstd, __fsub_rn(v.y, mean));
+    o.z = __fmul_rn(rstd, __fsub_rn(v.z, mean));
+    o.w = __fmul_rn(rstd, __fsub_rn(v.w, mean));
+  }
+  return o;
+}
+
+// One 128-thread block per row.  NVT = float4 vectors per thread
+// (n <= 512 * NVT).  HAS_U selects the fused residual form.
+template <int NVT, int XDT, int UDT, bool HAS_U>
+__global__ void __launch_bounds__(128) residual_ln_kernel(
     const void* __restrict__ x, const void* __restrict__ u, const float* __restrict__ scale,
-    const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int64_t rows,
-    int n, float* __restrict__ residual_out, float* __restrict__ normed_out,
+    const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int n,
+    float* __restrict__ residual_out, float* __restrict__ normed_out,
     float* __restrict__ mean_out, float* __restrict__ rstd_out, bool x_vec, bool u_vec) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
+  __shared__ float red[4][3];
+  __shared__ float stats[2];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int64_t row = blockIdx.x;
   const int nvec = n >> 2;
   const int64_t base4 = row * nvec;
 
-  float4 val[NV];
-  Welford w[4];
-#pragma unroll
-  for (int v = 0; v < 4; ++v) w[v] = {0.0f, 0.0f, 0.0f};
-
   // Issue every load of the row before any arithmetic.
-  float4 xu[NV];
+  float4 val[NVT], upd[NVT];
 #pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int i = lane + 32 * v;
+  for (int m = 0; m < NVT; ++m) {
+    const int i = tid + 128 * m;
     if (i < nvec) {
-      val[v] = load4<XDT>(x, base4 + i, x_vec);
-      if constexpr (HAS_U) xu[v] = load4<UDT>(u, base4 + i, u_vec);
+      val[m] = load4<XDT>(x, base4 + i, x_vec);
+      if constexpr (HAS_U) upd[m] = load4<UDT>(u, base4 + i, u_vec);
     }
   }
+  Welford w = {0.0f, 0.0f, 0.0f};
 #pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int i = lane + 32 * v;
+  for (int m = 0; m < NVT; ++m) {
+    const int i = tid + 128 * m;
     if (i < nvec) {
       if constexpr (HAS_U) {
         const float4 s = reinterpret_cast<const float4*>(scale)[i];
-        val[v].x = scale_add1(val[v].x, xu[v].x, s.x);
-        val[v].y = scale_add1(val[v].y, xu[v].y, s.y);
-        val[v].z = scale_add1(val[v].z, xu[v].z, s.z);
-        val[v].w = scale_add1(val[v].w, xu[v].w, s.w);
-        if (residual_out != nullptr) reinterpret_cast<float4*>(residual_out)[base4 + i] = val[v];
+        val[m].x = scale_add1(val[m].x, upd[m].x, s.x);
+        val[m].y = scale_add1(val[m].y, upd[m].y, s.y);
+        val[m].z = scale_add1(val[m].z, upd[m].z, s.z);
+        val[m].w = scale_add1(val[m].w, upd[m].w, s.w);
+        if (residual_out != nullptr) reinterpret_cast<float4*>(residual_out)[base4 + i] = val[m];
       }
-      Welford& ws = w[v & 3];
-      ws = welford_push(ws, val[v].x);
-      ws = welford_push(ws, val[v].y);
-      ws = welford_push(ws, val[v].z);
-      ws = welford_push(ws, val[v].w);
+      // counts 4m+1 .. 4m+4: a valid vector m implies vectors 0..m-1 were valid
+      w = welford_push(w, val[m].x, 4 * m + 1);
+      w = welford_push(w, val[m].y, 4 * m + 2);
+      w = welford_push(w, val[m].z, 4 * m + 3);
+      w = welford_push(w, val[m].w, 4 * m + 4);
     }
   }
-
-  float mean, m2;
-  reduce_row_stats(w, mean, m2);
-  const float var = __fdiv_rn(m2, static_cast<float>(n));
-  const float rstd = rsqrtf(__fadd_rn(var, eps));
-
 #pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int i = lane + 32 * v;
-    if (i < nvec) {
-      const float4 g = gamma ? reinterpret_cast<const float4*>(gamma)[i] : make_float4(1.f, 1.f, 1.f, 1.f);
-      const float4 bt = beta ? reinterpret_cast<const float4*>(beta)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 o;
-      // gamma * (rstd * (x - mean)) + beta with the outer multiply-add
-      // fused; without gamma the product rstd * (x - mean) itself fuses with
-      // the beta add, so each affine combination has its own expression.
-      if (gamma && beta) {
-        o.x = __fmaf_rn(g.x, __fmul_rn(rstd, __fsub_rn(val[v].x, mean)), bt.x);
-        o.y = __fmaf_rn(g.y, __fmul_rn(rstd, __fsub_rn(val[v].y, mean)), bt.y);
-        o.z = __fmaf_rn(g.z, __fmul_rn(rstd, __fsub_rn(val[v].z, mean)), bt.z);
-        o.w = __fmaf_rn(g.w, __fmul_rn(rstd, __fsub_rn(val[v].w, mean)), bt.w);
-      } else if (gamma) {
-        o.x = __fmul_rn(g.x, __fmul_rn(rstd, __fsub_rn(val[v].x, mean)));
-        o.y = __fmul_rn(g.y, __fmul_rn(rstd, __fsub_rn(val[v].y, mean)));
-        o.z = __fmul_rn(g.z, __fmul_rn(rstd, __fsub_rn(val[v].z, mean)));
-        o.w = __fmul_rn(g.w, __fmul_rn(rstd, __fsub_rn(val[v].w, mean)));
-      } else if (beta) {
-        o.x = __fmaf_rn(rstd, __fsub_rn(val[v].x, mean), bt.x);
-        o.y = __fmaf_rn(rstd, __fsub_rn(val[v].y, mean), bt.y);
-        o.z = __fmaf_rn(rstd, __fsub_rn(val[v].z, mean), bt.z);
-        o.w = __fmaf_rn(rstd, __fsub_rn(val[v].w, mean), bt.w);
-      } else {
-        o.x = __fmul_rn(rstd, __fsub_rn(val[v].x, mean));
-        o.y = __fmul_rn(rstd, __fsub_rn(val[v].y, mean));
-        o.z = __fmul_rn(rstd, __fsub_rn(val[v].z, mean));
-        o.w = __fmul_rn(rstd, __fsub_rn(val[v].w, mean));
-      }
-      reinterpret_cast<float4*>(normed_out)[base4 + i] = o;
-    }
+  for (int offset = 16; offset > 0; offset >>= 1) {
+    Welford o;
+    o.mean = __shfl_down_sync(0xffffffffu, w.mean, offset);
+    o.m2 = __shfl_down_sync(0xffffffffu, w.m2, offset);
+    o.count = __shfl_down_sync(0xffffffffu, w.count, offset);
+    w = welford_merge(w, o);
   }
   if (lane == 0) {
-    if (mean_out) mean_out[row] = mean;
+    red[warp][0] = w.mean;
+    red[warp][1] = w.m2;
+    red[warp][2] = w.count;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const Welford w0 = {red[0][0], red[0][1], red[0][2]};
+    const Welford w1 = {red[1][0], red[1][1], red[1][2]};
+    const Welford w2 = {red[2][0], red[2][1], red[2][2]};
+    const Welford w3 = {red[3][0], red[3][1], red[3][2]};
+    const Welford t = welford_merge(welford_merge(w0, w2), welford_merge(w1, w3));
+    const float var = __fdiv_rn(t.m2, static_cast<float>(n));
+    const float rstd = rsqrtf(__fadd_rn(var, eps));
+    stats[0] = t.mean;
+    stats[1] = rstd;
+    if (mean_out) mean_out[row] = t.mean;
     if (rstd_out) rstd_out[row] = rstd;
+  }
+  __syncthreads();
+  const float mean = stats[0], rstd = stats[1];
+#pragma unroll
+  for (int m = 0; m < NVT; ++m) {
+    const int i = tid + 128 * m;
+    if (i < nvec) {
+      reinterpret_cast<float4*>(normed_out)[base4 + i] = ln_out(val[m], mean, rstd, gamma, beta, i);
+    }
   }
 }
 
@@ -236,51 +241,40 @@ __global__ void __launch_bounds__(256) scale_add_scalar_kernel(const void* __res
 }
 
 // ------------------------------------------------------------------ launchers
-template <int NV, int XDT, int UDT, bool HAS_U>
+template <int NVT, int XDT, int UDT, bool HAS_U>
 static void launch_ln(const void* x, const void* u, const float* scale, const float* gamma,
                       const float* beta, float eps, int64_t rows, int n, float* res,
                       float* normed, float* mean, float* rstd, bool xv, bool uv,
                       cudaStream_t s) {
-  constexpr int kRowsPerCta = 8;
-  const int64_t grid = (rows + kRowsPerCta - 1) / kRowsPerCta;
-  residual_ln_kernel<NV, XDT, UDT, HAS_U><<<static_cast<unsigned>(grid), 32 * kRowsPerCta, 0, s>>>(
-      x, u, scale, gamma, beta, eps, rows, n, res, normed, mean, rstd, xv, uv);
+  residual_ln_kernel<NVT, XDT, UDT, HAS_U><<<static_cast<unsigned>(rows), 128, 0, s>>>(
+      x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
 }
 
 template <int XDT, int UDT, bool HAS_U>
-static int dispatch_nv(int nv, const void* x, const void* u, const float* scale,
-                       const float* gamma, const float* beta, float eps, int64_t rows, int n,
-                       float* res, float* normed, float* mean, float* rstd, bool xv, bool uv,
-                       cudaStream_t s) {
-#define MOSS_LN_CASE(K)                                                                       \
-  case K:                                                                                     \
-    launch_ln<K, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean, \
-                                  rstd, xv, uv, s);                                           \
-    return MOSS_OK;
-  switch (nv) {
-    MOSS_LN_CASE(1)
-    MOSS_LN_CASE(2)
-    MOSS_LN_CASE(3)
-    MOSS_LN_CASE(4)
-    MOSS_LN_CASE(5)
-    MOSS_LN_CASE(6)
-    MOSS_LN_CASE(7)
-    MOSS_LN_CASE(8)
-    MOSS_LN_CASE(10)
-    MOSS_LN_CASE(12)
-    MOSS_LN_CASE(16)
+static int dispatch_nvt(int nvt, const void* x, const void* u, const float* scale,
+                        const float* gamma, const float* beta, float eps, int64_t rows, int n,
+                        float* res, float* normed, float* mean, float* rstd, bool xv, bool uv,
+                        cudaStream_t s) {
+  switch (nvt) {
+    case 1:
+      launch_ln<1, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
+                                    rstd, xv, uv, s);
+      return MOSS_OK;
+    case 2:
+      launch_ln<2, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
+                                    rstd, xv, uv, s);
+      return MOSS_OK;
+    case 3:
+      launch_ln<3, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
+                                    rstd, xv, uv, s);
+      return MOSS_OK;
+    case 4:
+      launch_ln<4, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
+                                    rstd, xv, uv, s);
+      return MOSS_OK;
     default:
       return MOSS_ERR_UNSUPPORTED;
   }
-#undef MOSS_LN_CASE
-}
-
-static int round_nv(int nv) {
-  if (nv <= 8) return nv;
-  if (nv <= 10) return 10;
-  if (nv <= 12) return 12;
-  if (nv <= 16) return 16;
-  return -1;
 }
 
 static int ln_common(const char* name, const void* x, int x_dtype, const void* u, int u_dtype,
@@ -301,7 +295,6 @@ static int ln_common(const char* name, const void* x, int x_dtype, const void* u
                 "%s: width %lld is not a multiple of 4 (PyTorch uses its non-vectorised "
                 "layer norm there)",
                 name, static_cast<long long>(n));
-  if (n > (1 << 24)) return fail(MOSS_ERR_UNSUPPORTED, "%s: width above 2^24", name);
   if ((gamma && !aligned16(gamma)) || (beta && !aligned16(beta)) || !aligned16(normed_out) ||
       (residual_out && !aligned16(residual_out)) || (scale && !aligned16(scale)))
     return fail(MOSS_ERR_UNSUPPORTED,
@@ -312,10 +305,11 @@ static int ln_common(const char* name, const void* x, int x_dtype, const void* u
     return fail(MOSS_ERR_VALUE, "%s: plain layer norm takes float32 input", name);
   if (u == nullptr && !aligned16(x))
     return fail(MOSS_ERR_UNSUPPORTED, "%s: x must be 16-byte aligned", name);
-  const int nv = round_nv(static_cast<int>((n / 4 + 31) / 32));
-  if (nv < 0)
+  const int nvt = static_cast<int>((n / 4 + 127) / 128);
+  if (nvt > 4)
     return fail(MOSS_ERR_UNSUPPORTED, "%s: width %lld above the 2048 supported", name,
                 static_cast<long long>(n));
+  if (rows > 0x7fffffffLL) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many rows", name);
   if (rows == 0) return MOSS_OK;
   const bool xv = (x_dtype == MOSS_F32) ? aligned16(x) : ((reinterpret_cast<uintptr_t>(x) & 7u) == 0);
   const bool uv = u == nullptr ? true
@@ -325,20 +319,20 @@ static int ln_common(const char* name, const void* x, int x_dtype, const void* u
   const int ni = static_cast<int>(n);
   int st;
   if (u == nullptr) {
-    st = dispatch_nv<MOSS_F32, MOSS_F32, false>(nv, x, nullptr, nullptr, gamma, beta, eps, rows,
-                                                ni, nullptr, normed_out, mean, rstd, xv, uv, s);
+    st = dispatch_nvt<MOSS_F32, MOSS_F32, false>(nvt, x, nullptr, nullptr, gamma, beta, eps, rows,
+                                                 ni, nullptr, normed_out, mean, rstd, xv, uv, s);
   } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_F32) {
-    st = dispatch_nv<MOSS_F32, MOSS_F32, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
-                                               residual_out, normed_out, mean, rstd, xv, uv, s);
+    st = dispatch_nvt<MOSS_F32, MOSS_F32, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
+                                                residual_out, normed_out, mean, rstd, xv, uv, s);
   } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_BF16) {
-    st = dispatch_nv<MOSS_F32, MOSS_BF16, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
-                                                residual_out, normed_out, mean, rstd, xv, uv, s);
-  } else if (x_dtype == MOSS_BF16 && u_dtype == MOSS_F32) {
-    st = dispatch_nv<MOSS_BF16, MOSS_F32, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
-                                                residual_out, normed_out, mean, rstd, xv, uv, s);
-  } else {
-    st = dispatch_nv<MOSS_BF16, MOSS_BF16, true>(nv, x, u, scale, gamma, beta, eps, rows, ni,
+    st = dispatch_nvt<MOSS_F32, MOSS_BF16, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
                                                  residual_out, normed_out, mean, rstd, xv, uv, s);
+  } else if (x_dtype == MOSS_BF16 && u_dtype == MOSS_F32) {
+    st = dispatch_nvt<MOSS_BF16, MOSS_F32, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
+                                                 residual_out, normed_out, mean, rstd, xv, uv, s);
+  } else {
+    st = dispatch_nvt<MOSS_BF16, MOSS_BF16, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
+                                                  residual_out, normed_out, mean, rstd, xv, uv, s);
   }
   if (st != MOSS_OK) return fail(st, "%s: unsupported width", name);
   return launch_status(name);

@@ -34,7 +34,7 @@ class ResidualVectorQuantizer:
         self.stages, self.codes, self.dim = self.books.shape
         lib = _lib.load()
         floats = lib.moss_rvq_packed_floats(self.stages, self.codes, self.dim)
-        kpad = floats // max(1, 2 * self.stages * self.dim)  # two layouts per code
+        kpad = -(-self.codes // 256) * 256  # codes rounded up to whole 256-code chunks
         dev = self.books.device
         self.code_norm = torch.empty((self.stages, kpad), device=dev, dtype=torch.float32)
         self.packed = torch.empty(floats, device=dev, dtype=torch.float32)

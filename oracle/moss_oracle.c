@@ -250,10 +250,12 @@ EXPORT void oracle_gated_act(const float* x, const float* bias, float* y, int64_
   int64_t out_w = gated ? width / 2 : width;
   for (int64_t r = 0; r < rows; ++r)
     for (int64_t c = 0; c < out_w; ++c) {
-      float hg = round_dtype(x[r * width + c] + (bias ? bias[c] : 0.0f), bf16);
+      /* without a bias there is no add (so -0 stays -0, as in torch) */
+      float hg = bias ? round_dtype(x[r * width + c] + bias[c], bf16) : x[r * width + c];
       float a = round_dtype(act_eval(hg, act), bf16);
       if (gated) {
-        float hu = round_dtype(x[r * width + out_w + c] + (bias ? bias[out_w + c] : 0.0f), bf16);
+        float hu = bias ? round_dtype(x[r * width + out_w + c] + bias[out_w + c], bf16)
+                        : x[r * width + out_w + c];
         y[r * out_w + c] = round_dtype(a * hu, bf16);
       } else {
         y[r * out_w + c] = a;

@@ -167,6 +167,31 @@ def test_silu_gate_config3(moss, cuda_device):
 
 
 @pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
+def test_activation_exhaustive_bf16(moss, cuda_device, act):
+    """Every one of the 65,536 bf16 bit patterns as the gate input (up = 1 and
+    up = a random bf16), with and without a bias: bit-exact against torch."""
+    bits = torch.arange(65536, dtype=torch.int32).to(torch.int16)
+    gate = bits.view(torch.bfloat16).reshape(-1, 128).to(cuda_device)
+    g = torch.Generator().manual_seed(31)
+    up = torch.randn(gate.shape, generator=g).to(cuda_device, torch.bfloat16)
+    x = torch.cat([gate, up], dim=1)
+    for bias in (None, (0.5 * torch.randn(256, generator=g)).to(cuda_device, torch.bfloat16)):
+        y = moss.gated_activation(x, bias, act, gated=True)
+        h = x if bias is None else x + bias
+        gh, uh = h[:, :128], h[:, 128:]
+        if act == "silu":
+            a = torch.nn.functional.silu(gh)
+        elif act == "gelu":
+            a = torch.nn.functional.gelu(gh)
+        else:
+            a = torch.nn.functional.gelu(gh, approximate="tanh")
+        ref = a * uh
+        nan = torch.isnan(ref)
+        assert torch.equal(torch.isnan(y), nan)
+        assert torch.equal(y.view(torch.int16)[~nan], ref.view(torch.int16)[~nan]), bias is None
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
 @pytest.mark.parametrize("gated", [True, False])
 def test_activations_match_torch(moss, cuda_device, act, gated):
     g = torch.Generator().manual_seed(9)
@@ -192,3 +217,58 @@ def test_activations_match_torch(moss, cuda_device, act, gated):
     y2 = moss.gated_activation(x2, b2, act, gated=gated)
     r2 = torch_gated(x2, b2, act, gated)
     assert torch.allclose(y2, r2, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(3, 5, 203, 64), (2, 1, 1000, 128), (1, 40, 37, 32)])
+def test_rope_streaming_and_register_paths_agree(moss, cuda_device, dtype, shape):
+    """Contiguous q/k take the shared-memory streaming kernel; the same values
+    behind a padded time stride take the register kernel.  Ragged last tiles
+    in every shape; both must give the same bits, with and without tables."""
+    b, h, t, d = shape
+    g = torch.Generator().manual_seed(11)
+    qc = torch.randn(b, h, t, d, generator=g).to(cuda_device, dtype)
+    kc = torch.randn(b, h, t, d, generator=g).to(cuda_device, dtype)
+    qp = torch.zeros(b, h, t, d + 16, device=cuda_device, dtype=dtype)[..., :d]
+    kp = torch.zeros(b, h, t, d + 16, device=cuda_device, dtype=dtype)[..., :d]
+    qp.copy_(qc)
+    kp.copy_(kc)
+    offset = torch.arange(b, device=cuda_device) * 1000 + 3
+    bits = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    fq, fk = moss.rope(qc, kc, offset, 10000.0)
+    pq, pk = moss.rope(qp, kp, offset, 10000.0)
+    assert torch.equal(fq.view(bits), pq.view(bits)) and torch.equal(fk.view(bits), pk.view(bits))
+    cos, sin = reference_tables(offset, t, d, 10000.0, cuda_device)
+    rq, rk = moss.rotate(qc, kc, cos, sin)
+    sq, sk = moss.rotate(qp, kp, cos, sin)
+    assert torch.equal(rq.view(bits), sq.view(bits)) and torch.equal(rk.view(bits), sk.view(bits))
+    assert torch.equal(rq.view(bits), fq.view(bits)) and torch.equal(rk.view(bits), fk.view(bits))
+    sl = slice(0, 8)
+    oq, ok = O.rotate(qc[:, sl].float().cpu().numpy(), kc[:, sl].float().cpu().numpy(),
+                      cos.cpu().numpy(), sin.cpu().numpy(), dtype == torch.bfloat16)
+    assert same_bits(rq[:, sl].float().cpu().numpy(), oq)
+    assert same_bits(rk[:, sl].float().cpu().numpy(), ok)
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu"])
+def test_gate_rows_wider_than_a_stage(moss, cuda_device, act):
+    """Rows of 40,000 bytes exceed one shared-memory stage and take the
+    register kernel; ragged row counts take partial stages."""
+    g = torch.Generator().manual_seed(12)
+    for rows, width in ((3, 20000), (171, 192), (1, 16)):
+        x = torch.randn(rows, width, generator=g).to(cuda_device, torch.bfloat16)
+        bias = torch.randn(width, generator=g).to(cuda_device, torch.bfloat16)
+        for b in (bias, None):
+            y = moss.gated_activation(x, b, act, gated=True)
+            ref = torch_gated(x, b, act, True) if b is not None else torch_gated_nobias(x, act)
+            assert torch.equal(y.view(torch.int16), ref.view(torch.int16)), (rows, width, b is None)
+
+
+def torch_gated_nobias(x, act):
+    w = x.shape[-1] // 2
+    gate, up = x[..., :w], x[..., w:]
+    if act == "silu":
+        a = torch.nn.functional.silu(gate)
+    else:
+        a = torch.nn.functional.gelu(gate)
+    return a * up
