@@ -12,12 +12,19 @@ path).  The metric is audio seconds per second: each frame is 80 ms of
   e2e        the same metric through the public API with host buffers: every
              step copies the frames in from pinned host memory and the codes
              and reconstruction back out.
-  roofline   FP32 FFMA roofline of the encode kernel (algorithmic FLOPs per
-             launch / CUDA-event launch time vs SMs x 128 lanes x 2 x max
-             clock); DRAM traffic from the committed ncu summary.
+  roofline   the encode kernel against the tensor-core (TF32) peak: it
+             screens every codeword with tcgen05 TF32 dot products and
+             re-ranks the survivors exactly in FP32.  achieved = algorithmic
+             FLOPs per launch (8192 x 32 x 1024 x 64 x 2) / CUDA-event launch
+             time; peak = half the measured dense bf16 GEMM rate; the FP32
+             FFMA peak (SMs x 128 lanes x 2 x max clock) is given beside it.
+             DRAM traffic per launch comes from the committed ncu summary.
   kernels    the other hot-path kernels (residual+LayerNorm, RoPE, SiLU
-             gate, LFQ decode) at their workload sizes vs the measured HBM
-             copy bandwidth, inputs rotated through > L2-sized sets.
+             gate) at their workload sizes vs the measured HBM copy
+             bandwidth, launches captured in a CUDA graph with inputs rotated
+             through > L2-sized sets; and the all-FFMA quantizer kernel.
+  clocks     SM clock and clock-event reasons sampled during the timed
+             region.
   cpu_baseline  the CPU oracle port of the same quantizer on the host
              cores (bounded sample).
 
@@ -55,7 +62,7 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=500)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-kernels", action="store_true", help="skip the per-kernel HBM lines")
@@ -83,75 +90,111 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "sm_max_mhz": 1965.0}, "fallback"
 
 
-def profile_traffic(name):
-    """DRAM bytes per launch from a committed ncu summary, if one exists."""
-    path = os.path.join(REPO, "profiles", f"{name}.txt")
-    if not os.path.exists(path):
+def profile_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from its committed ncu summary
+    (profiles/<kernel>.<workload>.txt), if one exists."""
+    import glob
+
+    paths = sorted(glob.glob(os.path.join(REPO, "profiles", f"{kernel}.*.txt")))
+    if not paths:
         return None
-    m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", open(path).read())
+    m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", open(paths[0]).read())
     return float(m.group(1)) if m else None
 
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons during the timed region: NVML read
+    every 10 ms from a thread (nvidia-smi -lms 100 when NVML is missing).
+    Only reads; nothing about the GPU is changed."""
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.samples = []
-        self.proc = None
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
+    SMI_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []  # (time, sm_mhz, max_mhz, set of reasons)
+        self.stop_flag = threading.Event()
         self.thread = None
+        self.proc = None
+        self.source = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.gpu)],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
-            return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(
+                uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.nvml = pynvml
+            self.source = "nvml"
+            self.thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        except Exception:
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "100", "-i", str(self.device.index or 0)],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except OSError:
+                return
+            self.source = "nvidia-smi"
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
         self.thread.start()
 
-    def _read(self):
+    def _poll_nvml(self):
+        nv, h = self.nvml, self.handle
+        max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self.stop_flag.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+            except Exception:
+                break
+            reasons = {n for n, b in self.REASONS.items() if bits & b}
+            self.samples.append((time.time(), sm, max_mhz, reasons))
+            self.stop_flag.wait(0.01)
+
+    def _read_smi(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.samples.append((time.time(), parts))
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            reasons = {n for n, v in zip(names, parts[5:9]) if v.lower() == "active"}
+            self.samples.append((time.time(), sm, mx, reasons))
 
     def stop(self):
+        self.stop_flag.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self, t0, t1):
-        window = [s for t, s in self.samples if t0 <= t <= t1]
-        rows = window if window else [s for _, s in self.samples]
+        window = [s for s in self.samples if t0 <= s[0] <= t1]
+        rows = window if window else self.samples
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-
-        def num(v):
-            try:
-                return float(v)
-            except ValueError:
-                return None
-
-        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
         reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
-            for name, v in zip(names, r[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": num(rows[0][2]), "reasons": sorted(reasons),
-                "samples": len(rows), "in_window": bool(window)}
+            reasons |= r[3]
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": rows[0][2],
+                "reasons": sorted(reasons), "samples": len(rows), "in_window": bool(window),
+                "source": self.source}
 
 
 # ---------------------------------------------------------------- CPU oracle
@@ -272,7 +315,7 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     nbytes = 4 * rows * n * 4 + 3 * n * 4
     out["residual_layer_norm"] = {
         "shape": [1, rows, n], "us": t * 1e6, "bytes": nbytes, "gbs": nbytes / t / 1e9,
-        "frac": nbytes / t / 1e9 / hbm_peak, "traffic": profile_traffic("residual_layer_norm")}
+        "frac": nbytes / t / 1e9 / hbm_peak, "traffic": profile_traffic("residual_ln_kernel")}
     del sets
 
     # config 3a: RoPE on q, k [4,16,2048,64] bf16 (phase in-kernel)
@@ -297,7 +340,7 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     nbytes = 4 * b * h * tt * d * 2
     out["rope"] = {"shape": [b, h, tt, d], "us": t * 1e6, "bytes": nbytes,
                    "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
-                   "traffic": profile_traffic("rope")}
+                   "traffic": profile_traffic("rope_stream_kernel")}
     del sets
 
     # config 3b: SiLU gate + bias, [4,2048,4096] bf16 -> [4,2048,2048]
@@ -316,7 +359,7 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     nbytes = rows * width * 2 + width * 2 + rows * width // 2 * 2
     out["silu_gate"] = {"shape": [4, 2048, 4096], "us": t * 1e6, "bytes": nbytes,
                         "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
-                        "traffic": profile_traffic("silu_gate")}
+                        "traffic": profile_traffic("gated_act_stream_kernel")}
     del sets
     torch.cuda.synchronize()
     return out
@@ -364,7 +407,7 @@ def run_b200(args):
         step()
     torch.cuda.synchronize()
 
-    sampler = ClockSampler(local_rank)
+    sampler = ClockSampler(dev)
     sampler.start()
     time.sleep(0.3)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -465,7 +508,7 @@ def run_b200(args):
     fp32_peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
     achieved = FRAMES * FLOP_PER_FRAME / per_launch / 1e12
     tf32_peak = float(peaks["bf16_tflops"]) / 2
-    traffic = profile_traffic("rvq_tc")
+    traffic = profile_traffic("rvq_tc_kernel")
     line = {
         "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
         "value": value,

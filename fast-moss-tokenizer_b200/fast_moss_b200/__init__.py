@@ -2,13 +2,16 @@
 
 Drop-in for the data-parallel hot path of fast_moss (kadirnar/fast-moss-tokenizer):
 the same kernel-level functions (`rotate`, `scale_add`, `select`, `prepare`)
-backed by hand-written sm_100a CUDA kernels in libfast_moss_b200.so, plus
+and entry points (`optimized`, `StreamingCodec`, `codec`, `encode_fixed`,
+`load_model`) backed by hand-written sm_100a CUDA kernels in
+libfast_moss_b200.so, plus
 the fused forms (residual + LayerNorm, in-kernel RoPE phase, gated
 activation, fused LFQ decode, the whole multi-stage residual VQ in one
 kernel).
 """
 
 from . import _lib
+from .graphs import GraphedCallable
 from .quantizer import decode_latents, select
 from .quantizer_prepare import prepare
 from .rvq import ResidualVectorQuantizer
@@ -20,6 +23,10 @@ from .v2_pointwise import (
     rotate,
     scale_add,
 )
+from .streaming import StreamingCodec
+from .v2_codec import codec, encode_fixed
+from .v2_loading import load_model
+from .v2_runtime import V2Runtime, optimized, validate
 
 __all__ = [
     "rotate",
@@ -32,6 +39,14 @@ __all__ = [
     "decode_latents",
     "prepare",
     "ResidualVectorQuantizer",
+    "GraphedCallable",
+    "StreamingCodec",
+    "codec",
+    "encode_fixed",
+    "load_model",
+    "optimized",
+    "V2Runtime",
+    "validate",
 ]
 
 

@@ -13,7 +13,10 @@
  *     human-readable message for the calling thread is in moss_last_error().
  *     The Python host layer maps MOSS_ERR_VALUE -> ValueError and the others
  *     -> RuntimeError, the same exception classes the reference raises.
- *   - Calls on distinct streams are independent (no shared mutable state).
+ *   - Calls on distinct streams are independent.  The only state shared
+ *     between calls is read-only after its first use on a device: the SM
+ *     count and the bf16 activation tables of moss_gated_act (built by one
+ *     kernel on the caller's stream at the first bf16 call on a device).
  *
  * Dtype codes: MOSS_F32 = float32, MOSS_BF16 = bfloat16 (stored as uint16).
  *
