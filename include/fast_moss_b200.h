@@ -232,6 +232,31 @@ MOSS_API int moss_rvq_encode_ffma(const float* x, int64_t rows, int64_t d,
                     float* residual_out, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * moss_rvq_encode_static -- no reference counterpart.  The quantizer of
+ * moss_rvq_encode for callers that cannot allocate device memory (a host
+ * binding that owns only its input and output buffers, or a process held to
+ * a fixed device-memory budget): the prepared codebooks live in a static
+ * device array of this library instead of caller buffers, and each call runs
+ * moss_rvq_prepare_codebooks into it and then moss_rvq_encode, both on
+ * `stream`.  Same arguments and results as moss_rvq_encode minus the
+ * prepared buffers.
+ *   - Capacity: at most 32 stages x 1024 codes, d == 64; larger sizes return
+ *     MOSS_ERR_VALUE.  The array takes 17,957,376 bytes of device memory on
+ *     every device the library is used on.
+ *   - Nothing in the array has to start at zero: every call rewrites all of
+ *     it that the encode reads.
+ *   - The first call on each device looks up the array's address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture
+ *     on the device.
+ *   - Calls that overlap in time on one device (other streams or host
+ *     threads) race on the shared array; serialise them.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rvq_encode_static(const float* x, int64_t rows, int64_t d,
+                    const float* books, int64_t stages, int64_t k,
+                    int32_t* codes, float* recon, float* residual_out,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
  * Residual-VQ dequantisation: recon[r] = sum_s books[s][codes[s][r]] in
  * stage order (float32 adds starting from zero).  Codes outside [0, k) are
  * reported through the device error word and contribute nothing.

@@ -94,3 +94,13 @@ def test_python_wrappers_raise_reference_exceptions():
         fm.prepare(torch.zeros(1, 8, 4))  # CPU tensor
     with pytest.raises(ValueError, match="B,D,T"):
         fm.select(x, x, x, torch.zeros(3), x)
+
+
+def test_static_quantizer_rejects_sizes_beyond_its_scratch(lib):
+    """moss_rvq_encode_static checks sizes before any device work."""
+    from fast_moss_b200 import _lib
+
+    for stages, k, d in ((33, 1024, 64), (32, 1025, 64), (4, 16, 32)):
+        st = lib.moss_rvq_encode_static(None, 10, d, None, stages, k, None, None, None, None)
+        assert st == _lib.ERR_VALUE
+        assert b"static scratch" in lib.moss_last_error()
