@@ -7,8 +7,9 @@
  *     allocated inside a call and nothing is freed.
  *   - Sizes are int64_t element counts; strides are int64_t element strides.
  *   - `stream` is a cudaStream_t passed as void*; NULL means the legacy default
- *     stream.  Every call is stream-ordered, never synchronises the host and is
- *     therefore legal inside CUDA-graph capture.
+ *     stream.  Unless its declaration says otherwise, every call is
+ *     stream-ordered, never synchronises the host and is therefore legal
+ *     inside CUDA-graph capture.
  *   - Return value: MOSS_OK (0) on success, otherwise a status code below; a
  *     human-readable message for the calling thread is in moss_last_error().
  *     The Python host layer maps MOSS_ERR_VALUE -> ValueError and the others
