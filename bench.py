@@ -480,10 +480,9 @@ def run_b200(args):
     sampler.stop()
     clocks = sampler.summary(t0, t1)
 
-    times = torch.tensor([kernel_s, e2e_s, 0.0 if ok else 1.0], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    kernel_s, e2e_s, bad = times.tolist()
+    from fast_moss_b200.shards import max_over_ranks
+
+    kernel_s, e2e_s, bad = max_over_ranks([kernel_s, e2e_s, 0.0 if ok else 1.0], device=dev)
 
     kernels = None
     if rank == 0 and not args.no_kernels:

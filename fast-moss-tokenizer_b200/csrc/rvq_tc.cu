@@ -45,10 +45,12 @@ constexpr int kDim = 64;
 constexpr int kRows = 128;
 constexpr int kTileCodes = 256;
 constexpr int kSlots = 2;
-constexpr int kRec = 16;     // screening records per row and stage
-constexpr int kMaxCand = 32;  // candidates resolved exactly per row and stage
-constexpr int kEpiThreads = 128;
-constexpr int kThreads = 192;
+constexpr int kRec = 8;       // screening records per row, column half and stage
+constexpr int kQueue = 256;   // candidates resolved exactly per epilogue warp and stage
+constexpr int kEpiThreads = 256;  // two threads per row (column halves)
+constexpr int kThreads = kEpiThreads + 64;
+constexpr int kProducerWarp = kEpiThreads / 32;
+constexpr int kMmaWarp = kProducerWarp + 1;
 constexpr uint32_t kMainBytes = kTileCodes * kDim * 4;   // 65536: swizzled dims
 constexpr uint32_t kExtraBytes = kTileCodes * 8 * 4;     // 8192: norm column block
 constexpr uint32_t kTileBytes = kMainBytes + kExtraBytes;  // 73728 per tile image
@@ -59,11 +61,18 @@ struct __align__(1024) Smem {
   float btile[kSlots][kTileBytes / 4];  // tile images (each 1024-aligned)
   float a[kRows * kDim];                // 2r, K-major SW128 image
   float a_extra[kRows * 8];             // [1, 0 x 7] per row, no-swizzle K block
-  float cmax[8][kRows];  // chunk maxima of the current tile
-  float rec_max[kRec][kRows];
-  uint32_t rec_mask[kRec][kRows];
-  int cand[kMaxCand][kRows];
-  unsigned char rec_chunk[kRec][kRows];
+  // Per screening slot (column part x local row, at most 256 slots):
+  float cmax[4][2 * kRows];  // chunk maxima of the current tile
+  float rec_max[kRec][2 * kRows];
+  uint32_t rec_mask[kRec][2 * kRows];
+  unsigned char rec_chunk[kRec][2 * kRows];
+  float amax_h[2 * kRows];  // running screening maximum
+  int nrec_h[2 * kRows];
+  float window[kRows];
+  int pre_slow[kRows];  // row fails the screening preconditions this stage
+  int row_bad[kRows];   // row's candidates did not fit the resolve queue
+  unsigned long long best[kRows];  // (orderable distance << 32) | code
+  int queue[kEpiThreads / 32][kQueue];  // (row << 16) | code
   float norms[kRows];
   int sel[kRows];
   int slow_list[kRows];
@@ -75,6 +84,8 @@ struct __align__(1024) Smem {
   alignas(8) unsigned long long t_empty[2];
   alignas(8) unsigned long long a_full;
 };
+// The dynamic allocation adds 1024 bytes of alignment slack.
+static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the sm_100 per-block limit");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -136,9 +147,10 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// Barrier of the epilogue warps (both column halves).
 __device__ __forceinline__ void epi_bar() {
   __syncwarp();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 __device__ __forceinline__ int epi_bar_or(int pred) {
   int out;
@@ -146,7 +158,7 @@ __device__ __forceinline__ int epi_bar_or(int pred) {
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 2, 128, p;\n\t"
+      "bar.red.or.pred q, 2, 256, p;\n\t"
       "selp.b32 %0, 1, 0, q;\n\t}"
       : "=r"(out)
       : "r"(pred)
@@ -244,6 +256,7 @@ struct Args {
   int stages;
   int k;
   int kpad;
+  int rows_per_cta;  // 128, or 64 with every row in two TMEM lanes
 };
 
 // Exact NaN-aware selection of one row by one warp (pinned arithmetic).
@@ -282,42 +295,42 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
-// Keeps the records whose chunk maximum is still inside the window.
-__device__ __noinline__ int compact_records(Smem& sm, int row, float athr) {
+// Keeps the records (of one column half) whose chunk maximum is still
+// inside the window.
+__device__ __noinline__ int compact_records(Smem& sm, int slot, float athr) {
   int w = 0;
   for (int e = 0; e < kRec; ++e) {
-    if (sm.rec_max[e][row] >= athr) {
-      sm.rec_max[w][row] = sm.rec_max[e][row];
-      sm.rec_mask[w][row] = sm.rec_mask[e][row];
-      sm.rec_chunk[w][row] = sm.rec_chunk[e][row];
+    if (sm.rec_max[e][slot] >= athr) {
+      sm.rec_max[w][slot] = sm.rec_max[e][slot];
+      sm.rec_mask[w][slot] = sm.rec_mask[e][slot];
+      sm.rec_chunk[w][slot] = sm.rec_chunk[e][slot];
       ++w;
     }
   }
   return w;
 }
 
-// Screening record: stores {chunk max, mask, chunk}, prefetches the masked
-// codewords and returns the new record count (kRec + 1 once the records
-// overflowed; compaction of records that left the window is the rare case).
-__device__ __forceinline__ int add_record(Smem& sm, int row, int chunk, uint32_t mask, float cmx,
-                                          float athr, int nrec, const float* book,
-                                          const float* cnorm) {
+// Screening record: stores {chunk max, mask, chunk} and returns the new
+// record count (kRec + 1 once the records overflowed; compaction of records
+// that left the window is the rare case).
+__device__ __forceinline__ int add_record(Smem& sm, int slot, int chunk, uint32_t mask, float cmx,
+                                          float athr, int nrec) {
   if (nrec >= kRec) {
     if (nrec > kRec) return nrec;
-    nrec = compact_records(sm, row, athr);
+    nrec = compact_records(sm, slot, athr);
     if (nrec == kRec) return kRec + 1;
   }
-  sm.rec_max[nrec][row] = cmx;
-  sm.rec_mask[nrec][row] = mask;
-  sm.rec_chunk[nrec][row] = static_cast<unsigned char>(chunk);
-  for (uint32_t m = mask; m; m &= m - 1) {
-    const int j = chunk * 32 + (__ffs(m) - 1);
-    const float* cw = book + static_cast<int64_t>(j) * kDim;
-    prefetch_l1(cw);
-    prefetch_l1(cw + 32);
-    prefetch_l1(cnorm + j);
-  }
+  sm.rec_max[nrec][slot] = cmx;
+  sm.rec_mask[nrec][slot] = mask;
+  sm.rec_chunk[nrec][slot] = static_cast<unsigned char>(chunk);
   return nrec + 1;
+}
+
+// Float ordering as an unsigned key (finite values; -0 is mapped to +0 by
+// the caller so that equal distances compare equal).
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 // Maximum of 32 accumulator values as a depth-5 tree (independent pairs).
@@ -354,7 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   const int warp = tid >> 5, lane = tid & 31;
   const int ntiles = a.kpad / kTileCodes;
   const int total_tiles = a.stages * ntiles;
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kRows;
+  const int rpc = a.rows_per_cta;
+  const int copies = kRows / rpc;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * rpc;
 
   if (tid == 0) {
     for (int i = 0; i < kSlots; ++i) {
@@ -365,11 +380,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kEpiThreads);
     }
-    mbar_init(&sm.a_full, kEpiThreads);
+    mbar_init(&sm.a_full, rpc);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.slow_count = 0;
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&sm.tmem_base)),
                  "r"(kTmemCols)
@@ -381,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       for (int q = 0; q < total_tiles; ++q) {
@@ -393,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t a_base = smem_u32(sm.a);
@@ -440,11 +455,23 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int row = tid;  // TMEM lane == row (warps 0..3)
-    const int64_t grow = row0 + row;
+    // The CTA's rpc rows sit in the 128 TMEM lanes `copies` times (lane L
+    // holds local row L % rpc).  Warp w reads the lanes of quarter w % 4, and
+    // the 2 * copies warps that see a row split every tile's 256 columns
+    // into equal parts.  The part-0 thread of a row owns it (residual in
+    // registers): it writes the A operand, resolves and updates.
+    const int quarter = warp & 3;
+    const int qpr = 4 / copies;               // lane quarters per copy
+    const int lr = (quarter % qpr) * 32 + lane;  // local row
+    const int part = (quarter / qpr) * 2 + (warp >> 2);
+    const int nparts = 2 * copies;
+    const int cpp = 8 / nparts;               // 32-code chunks per part and tile
+    const int slot = part * rpc + lr;
+    const bool owner = part == 0;
+    const int64_t grow = row0 + lr;
     const bool valid = grow < a.rows;
     float r[kDim];
-    if (valid) {
+    if (owner && valid) {
       const float4* src = reinterpret_cast<const float4*>(a.x + grow * kDim);
 #pragma unroll
       for (int i = 0; i < kDim / 4; ++i) {
@@ -456,41 +483,50 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       for (int d = 0; d < kDim; ++d) r[d] = 0.0f;
     }
     unsigned char* a_bytes = reinterpret_cast<unsigned char*>(sm.a);
-    {
+    if (owner) {
       unsigned char* e = reinterpret_cast<unsigned char*>(sm.a_extra);
+      for (int cp = 0; cp < copies; ++cp) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        *reinterpret_cast<float*>(e + plain_offset(row, k)) = k == 0 ? 1.0f : 0.0f;
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float*>(e + plain_offset(lr + cp * rpc, k)) = k == 0 ? 1.0f : 0.0f;
+      }
     }
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
 
     int q = 0;
     bool aborted = false;
     for (int s = 0; s < a.stages; ++s) {
       const float* book = a.books + static_cast<int64_t>(s) * a.k * kDim;
       const float* cnorm = a.code_norm + static_cast<int64_t>(s) * a.kpad;
-      // norm and the A operand (2r) of this stage
-      float norm = 0.0f;
-#pragma unroll
-      for (int d = 0; d < kDim; ++d) norm = __fmaf_rn(r[d], r[d], norm);
-      sm.norms[row] = norm;
-#pragma unroll
-      for (int c = 0; c < kDim / 4; ++c) {
-        float4 v = make_float4(__fmul_rn(2.0f, r[4 * c]), __fmul_rn(2.0f, r[4 * c + 1]),
-                               __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
-        *reinterpret_cast<float4*>(a_bytes + sw128_offset(row, 4 * c, kRows * 128u)) = v;
-      }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&sm.a_full);
-
-      // screening window and preconditions
       const float cn_max = a.stats[s * 4 + 0];
       const bool book_ok = a.stats[s * 4 + 1] == 0.0f;
-      const float sc = __fmul_rn(2.0f, sqrtf(norm)) * sqrtf(cn_max);
-      const bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
-      const float margin = sc * 0.00390625f + cn_max * 0.001953125f +
-                           (norm + cn_max) * 9.5367431640625e-07f + 1e-30f;
-      const float window = 2.0f * margin * 1.0001f;
+      float norm = 0.0f;
+      if (owner) {
+        // norm and the A operand (2r) of this stage, in every copy
+#pragma unroll
+        for (int d = 0; d < kDim; ++d) norm = __fmaf_rn(r[d], r[d], norm);
+        sm.norms[lr] = norm;
+#pragma unroll
+        for (int c = 0; c < kDim / 4; ++c) {
+          float4 v = make_float4(__fmul_rn(2.0f, r[4 * c]), __fmul_rn(2.0f, r[4 * c + 1]),
+                                 __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
+          for (int cp = 0; cp < copies; ++cp)
+            *reinterpret_cast<float4*>(a_bytes + sw128_offset(lr + cp * rpc, 4 * c, kRows * 128u)) = v;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&sm.a_full);
+        // screening window and preconditions
+        const float sc = __fmul_rn(2.0f, sqrtf(norm)) * sqrtf(cn_max);
+        const bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
+        const float margin = sc * 0.00390625f + cn_max * 0.001953125f +
+                             (norm + cn_max) * 9.5367431640625e-07f + 1e-30f;
+        sm.window[lr] = 2.0f * margin * 1.0001f;
+        sm.pre_slow[lr] = slow || !valid ? 1 : 0;
+        sm.row_bad[lr] = 0;
+        sm.best[lr] = ~0ull;
+      }
+      epi_bar();  // the window is visible to every part
+      const float window = sm.window[lr];
       float amax = -CUDART_INF_F;
       int nrec = 0;
 
@@ -502,112 +538,123 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           break;
         }
         tc_fence_after();
-        const uint32_t tcol = tmem + lane_base + static_cast<uint32_t>(abuf * 256);
-        // Pass 1: the eight chunk maxima of this tile (independent chains),
-        // then one threshold for the whole tile.
+        const uint32_t tcol =
+            tmem + lane_base + static_cast<uint32_t>(abuf * 256 + part * cpp * 32);
+        // Pass 1: the chunk maxima of this part of the tile, then one threshold.
         uint32_t va[32], vb[32];
         float tmax = -CUDART_INF_F;
 #pragma unroll 1
-        for (int c = 0; c < 8; c += 2) {
+        for (int c = 0; c < cpp; c += 2) {
           tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
           tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
           tmem_wait_ld(va);
           tmem_wait_ld(vb);
           const float ca = max32(va), cb = max32(vb);
-          sm.cmax[c][row] = ca;
-          sm.cmax[c + 1][row] = cb;
+          sm.cmax[c][slot] = ca;
+          sm.cmax[c + 1][slot] = cb;
           tmax = fmaxf(tmax, fmaxf(ca, cb));
         }
         amax = fmaxf(amax, tmax);
         const float athr = amax - window;
         // Pass 2: window masks of the chunks that reach the threshold.
 #pragma unroll 1
-        for (int c = 0; c < 8; c += 2) {
+        for (int c = 0; c < cpp; c += 2) {
           tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
           tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
           tmem_wait_ld(va);
           tmem_wait_ld(vb);
-          const uint32_t ma = mask32(va, athr);
-          const uint32_t mb = mask32(vb, athr);
-          if (ma) nrec = add_record(sm, row, t * 8 + c, ma, sm.cmax[c][row], athr, nrec, book, cnorm);
-          if (mb)
-            nrec = add_record(sm, row, t * 8 + c + 1, mb, sm.cmax[c + 1][row], athr, nrec, book, cnorm);
+          const uint32_t ma = valid ? mask32(va, athr) : 0u;
+          const uint32_t mb = valid ? mask32(vb, athr) : 0u;
+          const int chunk = t * 8 + part * cpp + c;
+          if (ma) nrec = add_record(sm, slot, chunk, ma, sm.cmax[c][slot], athr, nrec);
+          if (mb) nrec = add_record(sm, slot, chunk + 1, mb, sm.cmax[c + 1][slot], athr, nrec);
         }
         tc_fence_before();
         mbar_arrive(&sm.t_empty[abuf]);
       }
       if (aborted) break;
+      sm.amax_h[slot] = amax;
+      sm.nrec_h[slot] = nrec;
+      epi_bar();  // every part's records are complete
 
-      // ---- resolve the stage: surviving records -> exact winner
-      int winner = -1;
-      if (!slow && nrec <= kRec) {
-        const float athr = amax - window;
-        int ncand = 0;
+      // ---- resolve the stage: every surviving candidate gets its exact
+      // distance.  The lanes of a warp share the candidates of its 32 rows
+      // (from the A image, 2r in shared memory); per row the smallest
+      // (distance, code) key wins, i.e. the first minimum.
+      bool fast = sm.pre_slow[lr] == 0;
+      float gmax = -CUDART_INF_F;
+      for (int p = 0; p < nparts; ++p) {
+        fast = fast && sm.nrec_h[p * rpc + lr] <= kRec;
+        gmax = fmaxf(gmax, sm.amax_h[p * rpc + lr]);
+      }
+      const float athr = gmax - window;
+      int cnt = 0;
+      if (fast) {
         for (int e = 0; e < nrec; ++e) {
-          if (sm.rec_max[e][row] < athr) continue;
-          const int base = sm.rec_chunk[e][row] * 32;
-          for (uint32_t m = sm.rec_mask[e][row]; m; m &= m - 1) {
-            if (ncand < kMaxCand) sm.cand[ncand][row] = base + (__ffs(m) - 1);
-            ++ncand;
-          }
-        }
-        if (ncand == 1) {
-          winner = sm.cand[0][row];
-        } else if (ncand > 1 && ncand <= kMaxCand) {
-          // exact distances, two candidates at a time: both codewords are
-          // loaded before the two independent FMA chains run; candidates are
-          // in ascending code order, so the first minimum wins
-          float best_d = 0.0f;
-          for (int b = 0; b < ncand; b += 2) {
-            const int j0 = sm.cand[b][row];
-            const int j1 = sm.cand[b + 1 < ncand ? b + 1 : b][row];
-            const float4* c0 = reinterpret_cast<const float4*>(book + static_cast<int64_t>(j0) * kDim);
-            const float4* c1 = reinterpret_cast<const float4*>(book + static_cast<int64_t>(j1) * kDim);
-            float4 w0[kDim / 4], w1[kDim / 4];
-#pragma unroll
-            for (int i = 0; i < kDim / 4; ++i) {
-              w0[i] = c0[i];
-              w1[i] = c1[i];
-            }
-            const float n0 = cnorm[j0], n1 = cnorm[j1];
-            float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-            for (int i = 0; i < kDim / 4; ++i) {
-              const float t0 = __fmul_rn(2.0f, r[4 * i]), t1 = __fmul_rn(2.0f, r[4 * i + 1]);
-              const float t2 = __fmul_rn(2.0f, r[4 * i + 2]), t3 = __fmul_rn(2.0f, r[4 * i + 3]);
-              d0 = __fmaf_rn(t0, w0[i].x, d0);
-              d1 = __fmaf_rn(t0, w1[i].x, d1);
-              d0 = __fmaf_rn(t1, w0[i].y, d0);
-              d1 = __fmaf_rn(t1, w1[i].y, d1);
-              d0 = __fmaf_rn(t2, w0[i].z, d0);
-              d1 = __fmaf_rn(t2, w1[i].z, d1);
-              d0 = __fmaf_rn(t3, w0[i].w, d0);
-              d1 = __fmaf_rn(t3, w1[i].w, d1);
-            }
-            const float dist0 = __fadd_rn(__fsub_rn(norm, d0), n0);
-            if (winner < 0 || dist0 < best_d) {
-              best_d = dist0;
-              winner = j0;
-            }
-            if (b + 1 < ncand) {
-              const float dist1 = __fadd_rn(__fsub_rn(norm, d1), n1);
-              if (dist1 < best_d) {
-                best_d = dist1;
-                winner = j1;
-              }
-            }
+          if (sm.rec_max[e][slot] >= athr) {
+            const uint32_t m = sm.rec_mask[e][slot];
+            cnt += __popc(m);
           }
         }
       }
-      if (winner < 0) {
-        const int slot = atomicAdd(&sm.slow_count, 1);
-        sm.slow_list[slot] = row;
+      int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int total = __shfl_sync(0xffffffffu, incl, 31);
+      int* queue = sm.queue[warp];
+      if (incl > kQueue) {
+        sm.row_bad[lr] = 1;  // does not fit: exact scan
+      } else if (cnt > 0) {
+        int pos = incl - cnt;
+        for (int e = 0; e < nrec; ++e) {
+          if (sm.rec_max[e][slot] < athr) continue;
+          const int base = sm.rec_chunk[e][slot] * 32;
+          for (uint32_t m = sm.rec_mask[e][slot]; m; m &= m - 1)
+            queue[pos++] = (lr << 16) | (base + (__ffs(m) - 1));
+        }
+      }
+      // entries [0, nq) are written: the rows whose candidates all fit
+      const int nq = total <= kQueue ? total : __reduce_max_sync(0xffffffffu, incl <= kQueue ? incl : 0);
+      __syncwarp();
+      for (int i = lane; i < nq; i += 32) {
+        const int ent = queue[i];
+        const int rr = ent >> 16, j = ent & 0xffff;
+        if (j >= a.k) continue;  // padding columns never reach the window
+        const float4* cw = reinterpret_cast<const float4*>(book + static_cast<int64_t>(j) * kDim);
+        float4 w[kDim / 4];
+#pragma unroll
+        for (int i4 = 0; i4 < kDim / 4; ++i4) w[i4] = cw[i4];
+        const float nj = cnorm[j];
+        float dot = 0.0f;
+#pragma unroll
+        for (int i4 = 0; i4 < kDim / 4; ++i4) {
+          const float4 tw =
+              *reinterpret_cast<const float4*>(a_bytes + sw128_offset(rr, 4 * i4, kRows * 128u));
+          dot = __fmaf_rn(tw.x, w[i4].x, dot);
+          dot = __fmaf_rn(tw.y, w[i4].y, dot);
+          dot = __fmaf_rn(tw.z, w[i4].z, dot);
+          dot = __fmaf_rn(tw.w, w[i4].w, dot);
+        }
+        const float dist = __fadd_rn(__fadd_rn(__fsub_rn(sm.norms[rr], dot), nj), 0.0f);
+        atomicMin(&sm.best[rr],
+                  (static_cast<unsigned long long>(order_key(dist)) << 32) | static_cast<uint32_t>(j));
+      }
+      epi_bar();  // every candidate of every row is in
+      int winner = -1;
+      if (owner && fast && sm.row_bad[lr] == 0 && sm.best[lr] != ~0ull)
+        winner = static_cast<int>(sm.best[lr] & 0xffffffffu);
+      if (owner && valid && winner < 0) {
+        const int at = atomicAdd(&sm.slow_count, 1);
+        sm.slow_list[at] = lr;
       }
       epi_bar();
       const int nslow = sm.slow_count;
       if (nslow > 0) {
         // exact scan, one warp per row; 2r is read back from the A image
-        for (int i = warp; i < nslow; i += 4) {
+        for (int i = warp; i < nslow; i += kEpiThreads / 32) {
           const int sr = sm.slow_list[i];
           float tw[kDim];
           for (int d = 0; d < kDim; ++d)
@@ -616,25 +663,29 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           if (lane == 0) sm.sel[sr] = ix;
         }
         epi_bar();
-        if (winner < 0) winner = sm.sel[row];
+        if (owner && valid && winner < 0) winner = sm.sel[lr];
         epi_bar();
-        if (row == 0) sm.slow_count = 0;
+        if (warp == 0 && lane == 0) sm.slow_count = 0;
       }
-      // ---- update the residual (the reconstruction is summed at the end)
-      const float4* cw =
-          reinterpret_cast<const float4*>(book + static_cast<int64_t>(winner) * kDim);
+      if (owner && valid) {
+        // ---- update the residual (the reconstruction is summed at the end)
+        const float4* cw =
+            reinterpret_cast<const float4*>(book + static_cast<int64_t>(winner) * kDim);
 #pragma unroll
-      for (int i = 0; i < kDim / 4; ++i) {
-        const float4 v = cw[i];
-        r[4 * i] = __fsub_rn(r[4 * i], v.x);
-        r[4 * i + 1] = __fsub_rn(r[4 * i + 1], v.y);
-        r[4 * i + 2] = __fsub_rn(r[4 * i + 2], v.z);
-        r[4 * i + 3] = __fsub_rn(r[4 * i + 3], v.w);
+        for (int i = 0; i < kDim / 4; ++i) {
+          const float4 v = cw[i];
+          r[4 * i] = __fsub_rn(r[4 * i], v.x);
+          r[4 * i + 1] = __fsub_rn(r[4 * i + 1], v.y);
+          r[4 * i + 2] = __fsub_rn(r[4 * i + 2], v.z);
+          r[4 * i + 3] = __fsub_rn(r[4 * i + 3], v.w);
+        }
+        a.codes[static_cast<int64_t>(s) * a.rows + grow] = winner;
       }
-      if (valid) a.codes[static_cast<int64_t>(s) * a.rows + grow] = winner;
-      if (nslow > 0) epi_bar();  // the slow scan read the A image of other rows
+      // the slow scan read the A image and the resolve read the other parts'
+      // records: both must be finished before the next stage rewrites them
+      epi_bar();
     }
-    if (!aborted && valid) {
+    if (owner && !aborted && valid) {
       // recon = sum of the chosen codewords in stage order from +0 (the same
       // float32 additions as an incremental sum)
       float acc[kDim];
@@ -670,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(kTmemCols)
                  : "memory");
@@ -698,7 +749,10 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
       !aligned16(recon) || (residual_out && !aligned16(residual_out)))
     return fail(MOSS_ERR_VALUE, "%s: buffers must be 16-byte aligned", name);
   const int64_t kpad = (k + rvqtc::kTileCodes - 1) / rvqtc::kTileCodes * rvqtc::kTileCodes;
-  const int64_t grid = (rows + rvqtc::kRows - 1) / rvqtc::kRows;
+  // 64 rows per CTA (each in two TMEM lanes, so four threads share a row's
+  // columns) while that fills at most one CTA per SM, else 128.
+  const int rows_per_cta = rows <= static_cast<int64_t>(sm_count()) * 64 ? 64 : rvqtc::kRows;
+  const int64_t grid = (rows + rows_per_cta - 1) / rows_per_cta;
   if (grid > 0x7fffffffLL) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many rows", name);
   const size_t smem = sizeof(rvqtc::Smem) + 1024;
   static bool configured[64] = {false};
@@ -714,7 +768,8 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
   // The tensor-core tile images follow the FFMA layout in the packed buffer.
   const float* image = packed + stages * kpad * rvqtc::kDim;
   rvqtc::Args args{x, books, image, code_norm, stats, codes, recon, residual_out, rows,
-                   static_cast<int>(stages), static_cast<int>(k), static_cast<int>(kpad)};
+                   static_cast<int>(stages), static_cast<int>(k), static_cast<int>(kpad),
+                   rows_per_cta};
   rvqtc::rvq_tc_kernel<<<static_cast<unsigned>(grid), rvqtc::kThreads, smem, as_stream(stream)>>>(args);
   return launch_status(name);
 }
