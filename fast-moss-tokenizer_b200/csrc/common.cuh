@@ -150,12 +150,12 @@ inline void allow_dynamic_smem(K kernel, size_t bytes, bool* done) {
   }
 }
 
-// Blocks of 256 threads of `kernel` that are resident on the whole device at
-// once (a persistent grid), capped at `work` and at least 1.
+// Blocks of `threads` threads of `kernel` that are resident on the whole
+// device at once (a persistent grid), capped at `work` and at least 1.
 template <typename K>
-inline int64_t persistent_grid(K kernel, size_t shmem, int64_t work) {
+inline int64_t persistent_grid(K kernel, int threads, size_t shmem, int64_t work) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, shmem) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, shmem) != cudaSuccess ||
       per_sm < 1)
     per_sm = 1;
   int64_t grid = static_cast<int64_t>(sm_count()) * per_sm;

@@ -12,10 +12,15 @@
 // Work decomposition: a tile is one batch index and TT time steps for ALL
 // heads, so the phase table of a tile (TT x d/2 (c, s) pairs, evaluated once
 // into shared memory -- the phase does not depend on the head) serves every
-// head.  With 16-byte rows (innermost stride 1: a qkv projection output
-// viewed as [b,h,t,d] qualifies) persistent blocks walk the tiles, issuing
-// the next tile's q/k loads and phase table before rotating the current one;
-// other layouts take a per-pair strided path.
+// head.  Three kernels share that decomposition:
+//   * rope_stream_kernel, for q and k whose time rows are contiguous within
+//     each head: bulk copies stage whole tiles in shared memory (one CTA
+//     per SM, producer thread + consumer warps);
+//   * rope_vec_kernel, for other layouts with 16-byte rows (innermost
+//     stride 1, e.g. a qkv projection output viewed as [b,h,t,d]):
+//     persistent blocks that issue the next tile's loads and phase table
+//     before rotating the current one;
+//   * rope_pair_kernel, one interleaved pair per item, for any strides.
 #include "pipeline.cuh"
 
 namespace moss {
@@ -570,7 +575,7 @@ static int rope_common(const char* name, RopeArgs a, int dtype, bool tables, voi
       // Persistent grid: as many blocks as fit on the device at once.
 #define MOSS_ROPE_V(DT, TB, KI)                                                               \
   do {                                                                                        \
-    const int64_t grid = persistent_grid(rope_vec_kernel<DT, TB, KI>, shmem, ntiles);         \
+    const int64_t grid = persistent_grid(rope_vec_kernel<DT, TB, KI>, 256, shmem, ntiles);         \
     rope_vec_kernel<DT, TB, KI><<<static_cast<unsigned>(grid), 256, shmem, s>>>(a, static_cast<uint32_t>(ntiles));   \
   } while (0)
       if (dtype == MOSS_BF16) {

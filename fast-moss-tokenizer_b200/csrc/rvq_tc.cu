@@ -529,14 +529,13 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       const float window = sm.window[lr];
       float amax = -CUDART_INF_F;
       int nrec = 0;
-
+      // A timed-out wait is agreed on at the end of the stage (all threads
+      // run the same tiles; after a timeout this thread stops waiting and
+      // the stage's values are discarded).
+      int timed_out = 0;
       for (int t = 0; t < ntiles; ++t, ++q) {
         const int abuf = q & 1;
-        const int timed_out = mbar_wait(&sm.t_full[abuf], (q >> 1) & 1) ? 0 : 1;
-        if (epi_bar_or(timed_out)) {
-          aborted = true;
-          break;
-        }
+        if (!timed_out && !mbar_wait(&sm.t_full[abuf], (q >> 1) & 1)) timed_out = 1;
         tc_fence_after();
         const uint32_t tcol =
             tmem + lane_base + static_cast<uint32_t>(abuf * 256 + part * cpp * 32);
@@ -572,10 +571,12 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         tc_fence_before();
         mbar_arrive(&sm.t_empty[abuf]);
       }
-      if (aborted) break;
       sm.amax_h[slot] = amax;
       sm.nrec_h[slot] = nrec;
-      epi_bar();  // every part's records are complete
+      if (epi_bar_or(timed_out)) {  // every part's records are complete
+        aborted = true;
+        break;
+      }
 
       // ---- resolve the stage: every surviving candidate gets its exact
       // distance.  The lanes of a warp share the candidates of its 32 rows
