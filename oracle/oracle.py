@@ -53,7 +53,16 @@ def _i64(v):
 
 
 def max_threads():
-    return int(lib().oracle_max_threads())
+    """Host threads the oracle may use: every CPU this process may run on
+    (launchers such as torchrun set OMP_NUM_THREADS=1, which would otherwise
+    cap the OpenMP default)."""
+    import os
+
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    return max(1, n)
 
 
 def bf16_round(x):
