@@ -299,9 +299,18 @@ namespace rstream {
 #endif
 constexpr int kConsumers = MOSS_ROPE_CONSUMERS;
 constexpr int kThreads = kConsumers + 32;
-constexpr int kStages = 4;
-constexpr int kStageBytes = 32768;
-constexpr int kMaxPairs = 2048;  // (c, s) pairs per tile table
+#ifndef MOSS_ROPE_STAGES
+#define MOSS_ROPE_STAGES 3
+#endif
+#ifndef MOSS_ROPE_STAGE_BYTES
+#define MOSS_ROPE_STAGE_BYTES 49152
+#endif
+constexpr int kStages = MOSS_ROPE_STAGES;
+constexpr int kStageBytes = MOSS_ROPE_STAGE_BYTES;
+#ifndef MOSS_ROPE_MAX_PAIRS
+#define MOSS_ROPE_MAX_PAIRS 2048
+#endif
+constexpr int kMaxPairs = MOSS_ROPE_MAX_PAIRS;  // (c, s) pairs per tile table
 // Items (16 bytes of q and 16 of k) per consumer thread and tile.
 constexpr int kSlots = (kStageBytes / 32 + kConsumers - 1) / kConsumers;
 

@@ -492,6 +492,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       }
     }
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    // The A operand (2r, in every copy) of the next stage is written as soon
+    // as the residual is known, so that its MMA starts before the bookkeeping
+    // of the stage boundary.
+    auto write_a = [&]() {
+#pragma unroll
+      for (int c = 0; c < kDim / 4; ++c) {
+        float4 v = make_float4(__fmul_rn(2.0f, r[4 * c]), __fmul_rn(2.0f, r[4 * c + 1]),
+                               __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
+        for (int cp = 0; cp < copies; ++cp)
+          *reinterpret_cast<float4*>(a_bytes + sw128_offset(lr + cp * rpc, 4 * c, kRows * 128u)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&sm.a_full);
+    };
+    if (owner) write_a();
 
     int q = 0;
     bool aborted = false;
@@ -502,19 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       const bool book_ok = a.stats[s * 4 + 1] == 0.0f;
       float norm = 0.0f;
       if (owner) {
-        // norm and the A operand (2r) of this stage, in every copy
 #pragma unroll
         for (int d = 0; d < kDim; ++d) norm = __fmaf_rn(r[d], r[d], norm);
         sm.norms[lr] = norm;
-#pragma unroll
-        for (int c = 0; c < kDim / 4; ++c) {
-          float4 v = make_float4(__fmul_rn(2.0f, r[4 * c]), __fmul_rn(2.0f, r[4 * c + 1]),
-                                 __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
-          for (int cp = 0; cp < copies; ++cp)
-            *reinterpret_cast<float4*>(a_bytes + sw128_offset(lr + cp * rpc, 4 * c, kRows * 128u)) = v;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&sm.a_full);
         // screening window and preconditions
         const float sc = __fmul_rn(2.0f, sqrtf(norm)) * sqrtf(cn_max);
         const bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
@@ -682,6 +687,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         }
         a.codes[static_cast<int64_t>(s) * a.rows + grow] = winner;
       }
+      // every reader of this stage's A image (MMA, exact distances, slow
+      // scan) is done: the next stage's operand can go in
+      if (owner && s + 1 < a.stages) write_a();
       // the slow scan read the A image and the resolve read the other parts'
       // records: both must be finished before the next stage rewrites them
       epi_bar();
