@@ -23,6 +23,11 @@ path).  The metric is audio seconds per second: each frame is 80 ms of
              gate) at their workload sizes vs the measured HBM copy
              bandwidth, launches captured in a CUDA graph with inputs rotated
              through > L2-sized sets; and the all-FFMA quantizer kernel.
+  stack      the codec's streaming transformer stack (24 x 1280, 20 heads,
+             ffn 5120) on the hot-path kernels under the batched CUDA-graph
+             scheduler: 125 chunks of 80 ms per stream at 1 and 64 streams,
+             with and without the per-chunk host copies, and the eager torch
+             stack on the host cores beside it.
   clocks     SM clock and clock-event reasons sampled during the timed
              region.
   cpu_baseline  the CPU oracle port of the same quantizer on the host
@@ -67,6 +72,8 @@ def parse_args():
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-kernels", action="store_true", help="skip the per-kernel HBM lines")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-stack", action="store_true",
+                   help="skip the streaming transformer stack lines")
     return p.parse_args()
 
 
@@ -365,6 +372,86 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     return out
 
 
+def stack_lines(torch, dev, cpu=True):
+    """The codec's streaming transformer stack (24 layers, hidden 1280, 20
+    heads, feed-forward 5120, FP32 weights seeded 2, bf16 GEMMs) over 125
+    chunks of 80 ms = 10 s of audio per stream, one CUDA graph replay per
+    chunk.  Every chunk is copied in from pinned host memory and its output
+    back out inside the timed region (the streaming use); one stream is the
+    reference's StreamingCodec shape, 64 streams the batched scheduler.
+    The CPU baseline is the eager oracle stack on the host cores (bf16
+    GEMMs, a bounded sample of chunks)."""
+    from fast_moss_b200.transformer import (BatchedStreams, StackConfig, StreamingTransformer,
+                                            init_weights)
+
+    cfg = StackConfig()
+    chunks = 125
+    weights = init_weights(cfg, seed=2)
+    stack = StreamingTransformer(cfg, weights, dev)
+    out = {"workload": "streaming stack: 24 layers, hidden 1280, 20 heads, ffn 5120, "
+                       "context 250 tokens, 4 tokens per 80 ms chunk, 125 chunks per stream",
+           "metric": "audio-sec/sec (RTF x streams)", "dtype": "bf16 GEMMs, f32 residual"}
+    for streams in (1, 64):
+        sched = BatchedStreams(stack, streams=streams, chunks_per_graph=1)
+        g = torch.Generator().manual_seed(4)
+        host = torch.randn(streams, cfg.chunk_tokens * chunks, cfg.dim, generator=g).pin_memory()
+        host_out = torch.empty_like(host).pin_memory()
+        x_dev = torch.empty(streams, cfg.chunk_tokens, cfg.dim, device=dev)
+        stream = torch.cuda.current_stream(dev)
+
+        def run(copies):
+            sched.reset()
+            for c in range(chunks):
+                sl = slice(c * cfg.chunk_tokens, (c + 1) * cfg.chunk_tokens)
+                if copies:
+                    x_dev.copy_(host[:, sl], non_blocking=True)
+                y = sched.push(x_dev)
+                if copies:
+                    host_out[:, sl].copy_(y, non_blocking=True)
+
+        times = {}
+        for copies in (False, True):
+            run(copies)
+            torch.cuda.synchronize()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            run(copies)
+            s1.record(stream)
+            s1.synchronize()
+            times[copies] = s0.elapsed_time(s1) * 1e-3
+        audio = streams * chunks * 0.08
+        out[f"streams_{streams}"] = {
+            "e2e": audio / times[True], "device": audio / times[False],
+            "ms_per_chunk_e2e": times[True] / chunks * 1e3,
+            "ms_per_chunk_device": times[False] / chunks * 1e3,
+            "h2d_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4,
+            "d2h_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4}
+        sched.release()
+        del sched
+    torch.cuda.synchronize()
+    if cpu:
+        from oracle.stack import EagerStack
+
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        ref = EagerStack(cfg, weights, "cpu", 1)
+        g = torch.Generator().manual_seed(4)
+        feats = torch.randn(1, cfg.chunk_tokens * 4, cfg.dim, generator=g)
+        ref.step(feats[:, :4])  # warm-up
+        n = 0
+        t = time.perf_counter()
+        while n < 3 or (time.perf_counter() - t < 10.0 and n < 8):
+            c = 1 + n % 3
+            ref.step(feats[:, 4 * c:4 * (c + 1)])
+            n += 1
+        dt = (time.perf_counter() - t) / n
+        out["cpu_baseline"] = {"value": 0.08 / dt, "unit": "audio-sec/sec", "cores":
+                               torch.get_num_threads(), "kind": "port",
+                               "sample": f"{n} chunks of one stream, eager torch stack on the "
+                                         f"host (bf16 GEMMs)"}
+    return out
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -494,6 +581,9 @@ def run_b200(args):
                "kind": "port",
                "sample": f"{rows} of {FRAMES} frames x {STAGES} stages ({dt:.1f} s, oracle "
                          f"C port, OpenMP)"}
+    stack = None
+    if rank == 0 and not args.no_stack:
+        stack = stack_lines(torch, dev, cpu=world == 1 and not args.no_cpu)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -563,6 +653,8 @@ def run_b200(args):
                            "rvq_ffma": ffma, **kernels}
     else:
         line["kernels"] = {"rvq_ffma": ffma}
+    if stack is not None:
+        line["stack"] = stack
     print(json.dumps(line), flush=True)
 
 

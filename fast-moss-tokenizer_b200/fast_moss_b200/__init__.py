@@ -7,7 +7,8 @@ and entry points (`optimized`, `StreamingCodec`, `codec`, `encode_fixed`,
 libfast_moss_b200.so, plus
 the fused forms (residual + LayerNorm, in-kernel RoPE phase, gated
 activation, fused LFQ decode, the whole multi-stage residual VQ in one
-kernel).
+kernel), and the streaming transformer stack with its batched CUDA-graph
+scheduler (`StreamingTransformer`, `BatchedStreams`).
 """
 
 from . import _lib
@@ -24,6 +25,7 @@ from .v2_pointwise import (
     scale_add,
 )
 from .streaming import StreamingCodec
+from .transformer import BatchedStreams, StackConfig, StreamingTransformer
 from .v2_codec import codec, encode_fixed
 from .v2_loading import load_model
 from .v2_runtime import V2Runtime, optimized, validate
@@ -41,6 +43,9 @@ __all__ = [
     "ResidualVectorQuantizer",
     "GraphedCallable",
     "StreamingCodec",
+    "StackConfig",
+    "StreamingTransformer",
+    "BatchedStreams",
     "codec",
     "encode_fixed",
     "load_model",

@@ -1,0 +1,284 @@
+"""Streaming codec transformer stack on the B200 kernels, and the batched
+streaming scheduler that replays it under CUDA graphs.
+
+The layer is the one the reference patches (fast_moss/v2_runtime.py:231-276):
+pre-LayerNorm attention with RoPE (:186-224) over a bounded causal history,
+residual + layer scale, pre-LayerNorm feed-forward, residual + layer scale;
+FP32 residual stream and parameters, bf16 GEMMs on cached bf16 weights
+(:77-106, F.linear as in :104).  Per layer the hot-path ops run as the
+native kernels of libfast_moss_b200:
+
+  LayerNorm of the stack input              moss_layer_norm
+  rotary phase + rotation of q and k         moss_rope
+  residual + layer scale 1 + LayerNorm 2     moss_residual_layer_norm (one pass)
+  feed-forward bias + activation             moss_gated_act
+  residual + layer scale 2 + next LN 1       moss_residual_layer_norm
+                                             (moss_scale_add after the last layer)
+
+GEMMs (cuBLAS) and attention (SDPA) stay library calls, as in the reference.
+
+The attention history of every layer is a ring of `context + chunk_tokens - 1`
+token slots per stream ([streams, heads, slots, head_dim] bf16 keys and
+values, plus the position held by each slot; position p lives in slot
+p mod slots).  A query at position p attends to the keys at positions
+p - context < p' <= p that have been written, which includes causal
+attention inside the chunk; the extra chunk_tokens - 1 slots keep the keys
+that the chunk's first queries still see while the chunk's own keys go in.  All state lives at fixed addresses and
+is updated in place, so a chunk step can be captured once and replayed.
+"""
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .graphs import GraphedCallable
+from .v2_pointwise import gated_activation, layer_norm, residual_layer_norm, rope, scale_add
+
+
+@dataclass(frozen=True)
+class StackConfig:
+    """Shape of a streaming transformer stack.
+
+    The defaults are the codec's streaming stack: 24 layers, hidden 1280,
+    20 heads, feed-forward 5120, 4 tokens per 80 ms chunk.  `context` is the
+    attention history in tokens (250 tokens = 5 s of audio at 50 tokens/s).
+    The feed-forward is Linear (no bias) -> act(h + bias) -> Linear (bias);
+    `gated` makes the first Linear twice as wide and gates act(h[:, :ffn])
+    with h[:, ffn:].
+    """
+
+    layers: int = 24
+    dim: int = 1280
+    heads: int = 20
+    ffn: int = 5120
+    context: int = 250
+    chunk_tokens: int = 4
+    max_period: float = 10000.0
+    activation: str = "gelu"
+    gated: bool = False
+    eps: float = 1e-5
+
+    def __post_init__(self):
+        if self.dim % self.heads or (self.dim // self.heads) % 2:
+            raise ValueError("dim must split into heads of even width")
+        if self.context < self.chunk_tokens:
+            raise ValueError("context must hold at least one chunk of tokens")
+        if min(self.layers, self.ffn, self.chunk_tokens) < 1:
+            raise ValueError("layers, ffn and chunk_tokens must be positive")
+
+    @property
+    def head_dim(self):
+        return self.dim // self.heads
+
+    @property
+    def history_slots(self):
+        return self.context + self.chunk_tokens - 1
+
+
+WEIGHT_NAMES = ("norm1_w", "norm1_b", "qkv_w", "qkv_b", "out_w", "out_b", "ls1", "norm2_w",
+                "norm2_b", "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "ls2")
+
+
+def init_weights(cfg, seed=2):
+    """Seeded random FP32 weights on the CPU: every matrix, bias and layer
+    scale ~ 0.02 N(0, 1); LayerNorm weights 1 + 0.02 N(0, 1), biases
+    0.02 N(0, 1).  Drawn in a fixed order, so the values do not depend on
+    the device they are later moved to."""
+    g = torch.Generator().manual_seed(seed)
+    d, f = cfg.dim, cfg.ffn
+    f1 = 2 * f if cfg.gated else f
+
+    def n(*shape):
+        return 0.02 * torch.randn(*shape, generator=g)
+
+    layers = []
+    for _ in range(cfg.layers):
+        layers.append({
+            "norm1_w": 1 + n(d), "norm1_b": n(d),
+            "qkv_w": n(3 * d, d), "qkv_b": n(3 * d),
+            "out_w": n(d, d), "out_b": n(d),
+            "ls1": n(d),
+            "norm2_w": 1 + n(d), "norm2_b": n(d),
+            "ffn1_w": n(f1, d), "ffn1_b": n(f1),
+            "ffn2_w": n(d, f), "ffn2_b": n(d),
+            "ls2": n(d),
+        })
+    return layers
+
+
+class StreamHistory:
+    """Attention history of `streams` independent streams, updated in place.
+
+    keys[i], values[i]: [streams, heads, slots, head_dim] bf16 of layer i;
+    slot_pos: [streams, slots] int64, the position held by each slot
+    (-1: empty); pos: [streams] int64, the position of the next token.
+    """
+
+    def __init__(self, cfg, streams, device):
+        if streams < 1:
+            raise ValueError("streams must be >= 1")
+        shape = (streams, cfg.heads, cfg.history_slots, cfg.head_dim)
+        self.streams = streams
+        self.context = cfg.context
+        self.max_tokens = cfg.chunk_tokens
+        self.keys = [torch.zeros(shape, device=device, dtype=torch.bfloat16)
+                     for _ in range(cfg.layers)]
+        self.values = [torch.zeros(shape, device=device, dtype=torch.bfloat16)
+                       for _ in range(cfg.layers)]
+        self.slot_pos = torch.full((streams, cfg.history_slots), -1, device=device,
+                                   dtype=torch.int64)
+        self.pos = torch.zeros(streams, device=device, dtype=torch.int64)
+
+    def reset(self, streams=None):
+        """Starts the given streams (all by default) afresh, in place.  The
+        old keys stay in memory but are masked out (their slots are empty)."""
+        with torch.inference_mode():
+            if streams is None:
+                self.slot_pos.fill_(-1)
+                self.pos.zero_()
+            else:
+                idx = torch.as_tensor(streams, device=self.pos.device, dtype=torch.int64)
+                self.slot_pos.index_fill_(0, idx, -1)
+                self.pos.index_fill_(0, idx, 0)
+
+    def advance(self, tokens):
+        """Writes the slot positions of the next `tokens` tokens and returns
+        (positions [S, T], slots [S, T], attention mask [S, 1, T, slots])."""
+        if not 1 <= tokens <= self.max_tokens:
+            raise ValueError(f"a chunk holds 1 to {self.max_tokens} tokens")
+        positions = self.pos[:, None] + torch.arange(tokens, device=self.pos.device)
+        slots = torch.remainder(positions, self.slot_pos.shape[1])
+        self.slot_pos.scatter_(1, slots, positions)
+        held = self.slot_pos[:, None, :]
+        query = positions[:, :, None]
+        mask = (held >= 0) & (held <= query) & (held > query - self.context)
+        return positions, slots, mask[:, None]
+
+
+class StreamingTransformer:
+    """The stack: FP32 parameters on one CUDA device, bf16 GEMM weights cached
+    once (the reference's cached Linear, fast_moss/v2_runtime.py:77-106)."""
+
+    def __init__(self, cfg, weights, device):
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise ValueError("StreamingTransformer runs on a CUDA device")
+        if len(weights) != cfg.layers:
+            raise ValueError("one weight dict per layer expected")
+        self.cfg = cfg
+        self.device = device
+        self.layers = []
+        for w in weights:
+            p = {k: w[k].to(device=device, dtype=torch.float32).contiguous() for k in WEIGHT_NAMES}
+            for k in ("qkv_w", "qkv_b", "out_w", "out_b", "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b"):
+                p[k + "16"] = p[k].to(torch.bfloat16)
+            self.layers.append(p)
+
+    def history(self, streams):
+        return StreamHistory(self.cfg, streams, self.device)
+
+    @torch.inference_mode()
+    def step(self, x, hist):
+        """One chunk [streams, T, dim] FP32 through every layer; advances the
+        history by T tokens and returns the FP32 residual stream."""
+        cfg = self.cfg
+        s, t, d = x.shape
+        if d != cfg.dim or s != hist.streams or x.dtype != torch.float32 or x.device != self.device:
+            raise ValueError("expected a [streams, tokens, dim] FP32 chunk on the stack's device")
+        h, dh = cfg.heads, cfg.head_dim
+        offset = hist.pos  # position of the chunk's first token (advanced at the end)
+        _, slots, mask = hist.advance(t)
+        index = slots[:, None, :, None].expand(s, h, t, dh)
+        first = self.layers[0]
+        x = x.contiguous()
+        normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps)
+        for i, p in enumerate(self.layers):
+            qkv = F.linear(normed.to(torch.bfloat16), p["qkv_w16"], p["qkv_b16"])
+            qkv = qkv.view(s, t, 3, h, dh)
+            q, k = rope(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), offset,
+                        cfg.max_period)
+            hist.keys[i].scatter_(2, index, k)
+            hist.values[i].scatter_(2, index, qkv[:, :, 2].transpose(1, 2))
+            a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i], attn_mask=mask)
+            u = F.linear(a.transpose(1, 2).reshape(s, t, d), p["out_w16"], p["out_b16"])
+            x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps)
+            f = F.linear(normed.to(torch.bfloat16), p["ffn1_w16"])
+            f = gated_activation(f, p["ffn1_b16"], cfg.activation, cfg.gated)
+            u = F.linear(f, p["ffn2_w16"], p["ffn2_b16"])
+            if i + 1 < len(self.layers):
+                nxt = self.layers[i + 1]
+                x, normed = residual_layer_norm(x, u, p["ls2"], nxt["norm1_w"], nxt["norm1_b"],
+                                                cfg.eps)
+            else:
+                x = scale_add(x, u, p["ls2"])
+        hist.pos.add_(t)
+        return x
+
+
+class BatchedStreams:
+    """Many streams of a StreamingTransformer advanced together under one
+    CUDA graph (the scheduler that replaces fast_moss/streaming.py's one
+    B=1 graph per 80 ms chunk).
+
+    `streams` independent streams share every weight read; `chunks_per_graph`
+    chunks are captured back to back in one graph, so a replay covers
+    chunks_per_graph x 80 ms of every stream.  Each replay writes its
+    output into a static buffer; `__call__` copies it straight into a
+    buffer allocated once per call (no per-chunk clone, no concatenation).
+    Use it on the CUDA stream and host thread that built it.
+    """
+
+    def __init__(self, stack, streams=1, chunks_per_graph=1):
+        if chunks_per_graph < 1:
+            raise ValueError("chunks_per_graph must be >= 1")
+        self.stack = stack
+        self.streams = int(streams)
+        self.chunks_per_graph = int(chunks_per_graph)
+        self.span = stack.cfg.chunk_tokens * self.chunks_per_graph
+        self.history = stack.history(self.streams)
+        t = stack.cfg.chunk_tokens
+        m = self.chunks_per_graph
+
+        def run(features):
+            out = torch.empty_like(features)
+            for c in range(m):
+                out[:, c * t:(c + 1) * t] = stack.step(features[:, c * t:(c + 1) * t],
+                                                       self.history)
+            return (out,)
+
+        example = torch.zeros(self.streams, self.span, stack.cfg.dim, device=stack.device)
+        self.graph = GraphedCallable(run, example)
+        self.history.reset()  # warm-up and capture advanced the history
+
+    def reset(self, streams=None):
+        """Starts the given streams (all by default) afresh before the next replay."""
+        self.history.reset(streams)
+
+    def push(self, features):
+        """Advances every stream by one replay: features [streams, span, dim]
+        FP32 on the device.  Returns the static output (valid until the
+        next push)."""
+        return self.graph.replay(features)[0]
+
+    @torch.inference_mode()
+    def __call__(self, features, *, reset=True):
+        """Runs [streams, tokens, dim] features through the stack chunk by
+        chunk (zero-padded to whole replays) and returns [streams, tokens, dim]."""
+        if features.ndim != 3 or features.shape[0] != self.streams or \
+                features.shape[2] != self.stack.cfg.dim:
+            raise ValueError("expected [streams, tokens, dim] features")
+        if reset:
+            self.reset()
+        n = features.shape[1]
+        pad = (-n) % self.span
+        if pad:
+            features = F.pad(features, (0, 0, 0, pad))
+        out = torch.empty_like(features)
+        for g in range(features.shape[1] // self.span):
+            sl = slice(g * self.span, (g + 1) * self.span)
+            out[:, sl].copy_(self.push(features[:, sl]))
+        return out[:, :n]
+
+    def release(self):
+        self.graph.release()

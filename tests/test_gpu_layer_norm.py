@@ -139,3 +139,53 @@ def test_unsupported_widths_raise(moss, cuda_device):
     x = torch.randn(4, 4096, device=cuda_device)
     with pytest.raises(UnsupportedError):
         moss.layer_norm(x, None, None)
+
+
+# Thousands of rows (several rows per resident block slot on every SM),
+# every dtype pair, widths with and without 16-byte rows, NaN and inf.
+@pytest.mark.parametrize("rows", [1187, 2072, 3001])
+@pytest.mark.parametrize("n", [8, 100, 1024, 1280, 2048])
+@pytest.mark.parametrize("dtypes", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
+                                    (torch.bfloat16, torch.float32),
+                                    (torch.bfloat16, torch.bfloat16)])
+def test_many_rows_match_torch_cuda(moss, cuda_device, rows, n, dtypes):
+    g = torch.Generator().manual_seed(rows * 7 + n)
+    x = (torch.randn(rows, n, generator=g) * 3 + 10).to(cuda_device, dtypes[0])
+    u = torch.randn(rows, n, generator=g).to(cuda_device, dtypes[1])
+    x[5, 3] = float("nan")
+    x[rows - 1, 0] = float("inf")
+    gamma = torch.randn(n, generator=g).to(cuda_device)
+    beta = torch.randn(n, generator=g).to(cuda_device)
+    ls = torch.randn(n, generator=g).to(cuda_device)
+    r, normed, mean, rstd = moss.residual_layer_norm(x, u, ls, gamma, beta, 1e-5,
+                                                     return_stats=True)
+    rr, rn, rm, rs = torch_reference(x, u, ls, gamma, beta, 1e-5)
+    assert same_bits(r.cpu().numpy(), rr.cpu().numpy())
+    assert same_bits(normed.cpu().numpy(), rn.cpu().numpy())
+    assert same_bits(mean.cpu().numpy(), rm.cpu().numpy())
+    assert same_bits(rstd.cpu().numpy(), rs.cpu().numpy())
+
+
+@pytest.mark.parametrize("rows", [1200, 4097])
+def test_many_rows_plain_layer_norm_and_affine_variants(moss, cuda_device, rows):
+    n = 1024
+    g = torch.Generator().manual_seed(rows)
+    x = (torch.randn(rows, n, generator=g) * 2 - 5).to(cuda_device)
+    gamma = torch.randn(n, generator=g).to(cuda_device)
+    beta = torch.randn(n, generator=g).to(cuda_device)
+    for w, b in ((gamma, beta), (None, None), (gamma, None), (None, beta)):
+        y, mean, rstd = moss.layer_norm(x, w, b, 1e-5, return_stats=True)
+        ref, rm, rs = torch.native_layer_norm(x, (n,), w, b, 1e-5)
+        assert same_bits(y.cpu().numpy(), ref.cpu().numpy())
+        assert same_bits(mean.cpu().numpy(), rm.reshape(-1).cpu().numpy())
+        assert same_bits(rstd.cpu().numpy(), rs.reshape(-1).cpu().numpy())
+    # an input that starts 4 bytes past a 16-byte boundary takes scalar loads
+    buf = torch.empty(rows * n + 1, device=cuda_device)
+    xs = buf[1:].view(rows, n)
+    xs.copy_(x)
+    ls = torch.randn(n, generator=g).to(cuda_device)
+    u = torch.randn(rows, n, generator=g).to(cuda_device)
+    r, normed = moss.residual_layer_norm(xs, u, ls, gamma, beta, 1e-5)
+    rr, rn, _, _ = torch_reference(x, u, ls, gamma, beta, 1e-5)
+    assert same_bits(r.cpu().numpy(), rr.cpu().numpy())
+    assert same_bits(normed.cpu().numpy(), rn.cpu().numpy())
