@@ -295,6 +295,14 @@ __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
+// Shared-memory vector store at a 32-bit shared address.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, float x0, float x1, float x2,
+                                             float x3) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x0), "f"(x1), "f"(x2),
+               "f"(x3)
+               : "memory");
+}
+
 // Keeps the records (of one column half) whose chunk maximum is still
 // inside the window.
 __device__ __noinline__ int compact_records(Smem& sm, int slot, float athr) {
@@ -360,9 +368,13 @@ __device__ __forceinline__ uint32_t mask32(const uint32_t (&acc)[32], float athr
 
 __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   extern __shared__ unsigned char smem_raw[];
-  // 1024-byte alignment for the swizzled operand images.
+  // 1024-byte alignment for the swizzled operand images, by pointer
+  // arithmetic on the shared array: the compiler then keeps the shared state
+  // space for every access through `sm` (an integer round trip would turn
+  // them into generic accesses).
   Smem& sm = *reinterpret_cast<Smem*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+      smem_raw +
+      ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u));
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int ntiles = a.kpad / kTileCodes;
@@ -496,12 +508,14 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     // as the residual is known, so that its MMA starts before the bookkeeping
     // of the stage boundary.
     auto write_a = [&]() {
+      const uint32_t a_base = smem_u32(sm.a);
 #pragma unroll
       for (int c = 0; c < kDim / 4; ++c) {
-        float4 v = make_float4(__fmul_rn(2.0f, r[4 * c]), __fmul_rn(2.0f, r[4 * c + 1]),
-                               __fmul_rn(2.0f, r[4 * c + 2]), __fmul_rn(2.0f, r[4 * c + 3]));
-        for (int cp = 0; cp < copies; ++cp)
-          *reinterpret_cast<float4*>(a_bytes + sw128_offset(lr + cp * rpc, 4 * c, kRows * 128u)) = v;
+        const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
+        const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
+        st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
+        if (copies == 2)
+          st_shared_v4(a_base + sw128_offset(lr + rpc, 4 * c, kRows * 128u), x0, x1, x2, x3);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&sm.a_full);
@@ -510,11 +524,17 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
 
     int q = 0;
     bool aborted = false;
+    // The stage's codebook statistics are loaded one stage ahead.
+    float next_cn_max = a.stats[0], next_flag = a.stats[1];
     for (int s = 0; s < a.stages; ++s) {
       const float* book = a.books + static_cast<int64_t>(s) * a.k * kDim;
       const float* cnorm = a.code_norm + static_cast<int64_t>(s) * a.kpad;
-      const float cn_max = a.stats[s * 4 + 0];
-      const bool book_ok = a.stats[s * 4 + 1] == 0.0f;
+      const float cn_max = next_cn_max;
+      const bool book_ok = next_flag == 0.0f;
+      if (s + 1 < a.stages) {
+        next_cn_max = a.stats[(s + 1) * 4 + 0];
+        next_flag = a.stats[(s + 1) * 4 + 1];
+      }
       float norm = 0.0f;
       if (owner) {
 #pragma unroll
@@ -544,34 +564,51 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         tc_fence_after();
         const uint32_t tcol =
             tmem + lane_base + static_cast<uint32_t>(abuf * 256 + part * cpp * 32);
-        // Pass 1: the chunk maxima of this part of the tile, then one threshold.
         uint32_t va[32], vb[32];
-        float tmax = -CUDART_INF_F;
-#pragma unroll 1
-        for (int c = 0; c < cpp; c += 2) {
-          tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
-          tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
+        if (cpp == 2) {
+          // 64 rows per CTA: the part's two chunks are loaded once and kept
+          // in registers for the mask.
+          tmem_load32(tcol, va);
+          tmem_load32(tcol + 32u, vb);
           tmem_wait_ld(va);
           tmem_wait_ld(vb);
           const float ca = max32(va), cb = max32(vb);
-          sm.cmax[c][slot] = ca;
-          sm.cmax[c + 1][slot] = cb;
-          tmax = fmaxf(tmax, fmaxf(ca, cb));
-        }
-        amax = fmaxf(amax, tmax);
-        const float athr = amax - window;
-        // Pass 2: window masks of the chunks that reach the threshold.
-#pragma unroll 1
-        for (int c = 0; c < cpp; c += 2) {
-          tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
-          tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
-          tmem_wait_ld(va);
-          tmem_wait_ld(vb);
+          amax = fmaxf(amax, fmaxf(ca, cb));
+          const float athr = amax - window;
           const uint32_t ma = valid ? mask32(va, athr) : 0u;
           const uint32_t mb = valid ? mask32(vb, athr) : 0u;
-          const int chunk = t * 8 + part * cpp + c;
-          if (ma) nrec = add_record(sm, slot, chunk, ma, sm.cmax[c][slot], athr, nrec);
-          if (mb) nrec = add_record(sm, slot, chunk + 1, mb, sm.cmax[c + 1][slot], athr, nrec);
+          const int chunk = t * 8 + part * cpp;
+          if (ma) nrec = add_record(sm, slot, chunk, ma, ca, athr, nrec);
+          if (mb) nrec = add_record(sm, slot, chunk + 1, mb, cb, athr, nrec);
+        } else {
+          // Pass 1: the chunk maxima of this part of the tile, then one
+          // threshold; pass 2: window masks of the chunks that reach it.
+          float tmax = -CUDART_INF_F;
+#pragma unroll 1
+          for (int c = 0; c < cpp; c += 2) {
+            tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
+            tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
+            tmem_wait_ld(va);
+            tmem_wait_ld(vb);
+            const float ca = max32(va), cb = max32(vb);
+            sm.cmax[c][slot] = ca;
+            sm.cmax[c + 1][slot] = cb;
+            tmax = fmaxf(tmax, fmaxf(ca, cb));
+          }
+          amax = fmaxf(amax, tmax);
+          const float athr = amax - window;
+#pragma unroll 1
+          for (int c = 0; c < cpp; c += 2) {
+            tmem_load32(tcol + static_cast<uint32_t>(c * 32), va);
+            tmem_load32(tcol + static_cast<uint32_t>((c + 1) * 32), vb);
+            tmem_wait_ld(va);
+            tmem_wait_ld(vb);
+            const uint32_t ma = valid ? mask32(va, athr) : 0u;
+            const uint32_t mb = valid ? mask32(vb, athr) : 0u;
+            const int chunk = t * 8 + part * cpp + c;
+            if (ma) nrec = add_record(sm, slot, chunk, ma, sm.cmax[c][slot], athr, nrec);
+            if (mb) nrec = add_record(sm, slot, chunk + 1, mb, sm.cmax[c + 1][slot], athr, nrec);
+          }
         }
         tc_fence_before();
         mbar_arrive(&sm.t_empty[abuf]);
@@ -594,12 +631,26 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         gmax = fmaxf(gmax, sm.amax_h[p * rpc + lr]);
       }
       const float athr = gmax - window;
+      // Count the surviving candidates, keeping the first four in registers
+      // for the queue fill and sending their codewords on their way into L1
+      // (the lane that resolves a candidate reads it from there).
       int cnt = 0;
+      int c0 = 0, c1 = 0, c2 = 0, c3 = 0;
       if (fast) {
         for (int e = 0; e < nrec; ++e) {
-          if (sm.rec_max[e][slot] >= athr) {
-            const uint32_t m = sm.rec_mask[e][slot];
-            cnt += __popc(m);
+          if (sm.rec_max[e][slot] < athr) continue;
+          const int base = sm.rec_chunk[e][slot] * 32;
+          for (uint32_t m = sm.rec_mask[e][slot]; m; m &= m - 1) {
+            const int j = base + (__ffs(m) - 1);
+            if (cnt < 4) {
+              prefetch_l1(book + static_cast<int64_t>(j < a.k ? j : 0) * kDim);
+              prefetch_l1(book + static_cast<int64_t>(j < a.k ? j : 0) * kDim + 32);
+              c3 = cnt == 3 ? j : c3;
+              c2 = cnt == 2 ? j : c2;
+              c1 = cnt == 1 ? j : c1;
+              c0 = cnt == 0 ? j : c0;
+            }
+            ++cnt;
           }
         }
       }
@@ -613,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       int* queue = sm.queue[warp];
       if (incl > kQueue) {
         sm.row_bad[lr] = 1;  // does not fit: exact scan
-      } else if (cnt > 0) {
+      } else if (cnt > 4) {  // rare: walk the records again
         int pos = incl - cnt;
         for (int e = 0; e < nrec; ++e) {
           if (sm.rec_max[e][slot] < athr) continue;
@@ -621,6 +672,12 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           for (uint32_t m = sm.rec_mask[e][slot]; m; m &= m - 1)
             queue[pos++] = (lr << 16) | (base + (__ffs(m) - 1));
         }
+      } else if (cnt > 0) {
+        const int pos = incl - cnt;
+        queue[pos] = (lr << 16) | c0;
+        if (cnt > 1) queue[pos + 1] = (lr << 16) | c1;
+        if (cnt > 2) queue[pos + 2] = (lr << 16) | c2;
+        if (cnt > 3) queue[pos + 3] = (lr << 16) | c3;
       }
       // entries [0, nq) are written: the rows whose candidates all fit
       const int nq = total <= kQueue ? total : __reduce_max_sync(0xffffffffu, incl <= kQueue ? incl : 0);

@@ -15,7 +15,10 @@ native kernels of libfast_moss_b200:
   residual + layer scale 2 + next LN 1       moss_residual_layer_norm
                                              (moss_scale_add after the last layer)
 
-GEMMs (cuBLAS) and attention (SDPA) stay library calls, as in the reference.
+GEMMs (cuBLAS) and attention (SDPA) stay library calls, as in the reference;
+attention is pinned to SDPA's memory-efficient backend, which runs these
+few-query, masked shapes about twice as fast as the backend chosen by
+default on B200 (66 us against 121 us per layer at 64 streams).
 
 The attention history of every layer is a ring of `context + chunk_tokens - 1`
 token slots per stream ([streams, heads, slots, head_dim] bf16 keys and
@@ -31,6 +34,7 @@ from dataclasses import dataclass
 
 import torch
 import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .graphs import GraphedCallable
 from .v2_pointwise import gated_activation, layer_norm, residual_layer_norm, rope, scale_add
@@ -200,7 +204,9 @@ class StreamingTransformer:
                         cfg.max_period)
             hist.keys[i].scatter_(2, index, k)
             hist.values[i].scatter_(2, index, qkv[:, :, 2].transpose(1, 2))
-            a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i], attn_mask=mask)
+            with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
+                a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
+                                                   attn_mask=mask)
             u = F.linear(a.transpose(1, 2).reshape(s, t, d), p["out_w16"], p["out_b16"])
             x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps)
             f = F.linear(normed.to(torch.bfloat16), p["ffn1_w16"])

@@ -13,7 +13,8 @@ Restates, with stock torch ops only, the layer the reference patches
     dtype (v2_pointwise.py:8-47);
   * feed-forward bias + activation: the eager bf16 chain act(h + b);
   * GEMMs (F.linear on the cached bf16 weights, v2_runtime.py:104) and SDPA
-    attention are the same library calls as the product path.
+    attention (memory-efficient backend) are the same library calls as the
+    product path.
 
 It keeps its own history tensors, so the product stack and this oracle can
 be stepped side by side on the same chunks.  Only tests, the smoke check and
@@ -24,6 +25,7 @@ import math
 
 import torch
 import torch.nn.functional as F
+from torch.nn.attention import SDPBackend, sdpa_kernel
 
 
 def rotary_tables(offset, t, d, period):
@@ -126,7 +128,9 @@ class EagerStack:
             k = rotate(qkv[:, :, 1].transpose(1, 2), cos, sin)
             self.keys[i].scatter_(2, index, k)
             self.values[i].scatter_(2, index, qkv[:, :, 2].transpose(1, 2))
-            a = F.scaled_dot_product_attention(q, self.keys[i], self.values[i], attn_mask=mask)
+            with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]):
+                a = F.scaled_dot_product_attention(q, self.keys[i], self.values[i],
+                                                   attn_mask=mask)
             u = F.linear(a.transpose(1, 2).reshape(s, t, d), p["out_w16"], p["out_b16"])
             x = x + u.float() * p["ls1"]
             normed = F.layer_norm(x, (d,), p["norm2_w"], p["norm2_b"], cfg.eps)
