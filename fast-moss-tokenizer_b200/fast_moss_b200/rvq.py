@@ -85,6 +85,61 @@ class ResidualVectorQuantizer:
                 torch.cuda.current_stream(dev).cuda_stream)
         return codes, recon
 
+    def encode_host_batches(self, xs, codes_out, recon_out, *, depth=2,
+                            algorithm="tensor_core"):
+        """Quantizes a sequence of batches that live in (pinned) host memory.
+
+        xs[i]: FP32 rows [N_i, D] on the host; codes_out[i] (int32 [S, N_i])
+        and recon_out[i] ([N_i, D]) are host tensors that receive the
+        results.  Batch i+1 is copied in on one copy stream and batch i-1's
+        results are copied out on another while batch i is quantized, with
+        `depth` device buffer sets in rotation (events order every reuse).
+        Work is queued on the current stream's device; on return the current
+        stream waits for the last copy out (synchronize before reading the
+        host outputs).
+        """
+        if not len(xs) == len(codes_out) == len(recon_out):
+            raise ValueError("xs, codes_out and recon_out must have the same length")
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        dev = self.books.device
+        main = torch.cuda.current_stream(dev)
+        h2d = torch.cuda.Stream(device=dev)
+        d2h = torch.cuda.Stream(device=dev)
+        bufs = {}
+        freed = [None] * depth  # event: buffer set b may be overwritten
+        for i, (xh, ch, rh) in enumerate(zip(xs, codes_out, recon_out)):
+            n = xh.shape[0]
+            if xh.ndim != 2 or xh.shape[1] != self.dim or xh.dtype != torch.float32 or xh.is_cuda:
+                raise ValueError(f"xs[{i}] must be FP32 host rows [N, {self.dim}]")
+            if ch.shape != (self.stages, n) or ch.dtype != torch.int32 or ch.is_cuda:
+                raise ValueError(f"codes_out[{i}] must be an int32 host tensor [stages, N]")
+            if rh.shape != (n, self.dim) or rh.dtype != torch.float32 or rh.is_cuda:
+                raise ValueError(f"recon_out[{i}] must be an FP32 host tensor [N, dim]")
+            b = i % depth
+            x_d, c_d, r_d = bufs.get((b, n)) or bufs.setdefault((b, n), (
+                torch.empty((n, self.dim), device=dev, dtype=torch.float32),
+                torch.empty((self.stages, n), device=dev, dtype=torch.int32),
+                torch.empty((n, self.dim), device=dev, dtype=torch.float32)))
+            if freed[b] is not None:
+                h2d.wait_event(freed[b])
+            with torch.cuda.stream(h2d):
+                x_d.copy_(xh, non_blocking=True)
+                loaded = torch.cuda.Event()
+                loaded.record(h2d)
+            main.wait_event(loaded)
+            self.encode(x_d, codes=c_d, recon=r_d, algorithm=algorithm)
+            done = torch.cuda.Event()
+            done.record(main)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                ch.copy_(c_d, non_blocking=True)
+                rh.copy_(r_d, non_blocking=True)
+                freed[b] = torch.cuda.Event()
+                freed[b].record(d2h)
+        main.wait_stream(d2h)
+        main.wait_stream(h2d)
+
     def decode(self, codes):
         """Dequantizes int32 codes [S, N] to recon [N, D] (stage order sum)."""
         if codes.ndim != 2 or codes.shape[0] != self.stages or codes.dtype != torch.int32:

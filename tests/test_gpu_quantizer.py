@@ -194,3 +194,27 @@ def test_rvq_decode_and_buffers(moss, cuda_device):
     assert same_bits(q.decode(codes).cpu().numpy(), O.rvq_decode(codes.cpu().numpy(), books))
     with pytest.raises(ValueError):
         q.encode(torch.zeros(3, 32, device=cuda_device))
+
+
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_rvq_host_batches_pipeline(moss, cuda_device, depth):
+    """Batches copied in, quantized and copied out with the copies overlapped
+    give the same bits as quantizing each batch on its own."""
+    rng = np.random.default_rng(21)
+    books = (rng.standard_normal((6, 1024, 64)) / 8).astype(np.float32)
+    q = moss.ResidualVectorQuantizer(dev(books, cuda_device))
+    sizes = [700, 700, 33, 1500, 700, 1]
+    xs = [torch.from_numpy(rng.standard_normal((n, 64)).astype(np.float32)).pin_memory()
+          for n in sizes]
+    codes = [torch.empty((6, n), dtype=torch.int32).pin_memory() for n in sizes]
+    recon = [torch.empty((n, 64)).pin_memory() for n in sizes]
+    q.encode_host_batches(xs, codes, recon, depth=depth)
+    torch.cuda.synchronize()
+    for x, c, r in zip(xs, codes, recon):
+        wc, wr = q.encode(x.to(cuda_device))
+        assert torch.equal(c, wc.cpu())
+        assert same_bits(r.numpy(), wr.cpu().numpy())
+    with pytest.raises(ValueError):
+        q.encode_host_batches(xs[:2], codes[:1], recon[:2])
+    with pytest.raises(ValueError):
+        q.encode_host_batches([xs[0].to(cuda_device)], codes[:1], recon[:1])
