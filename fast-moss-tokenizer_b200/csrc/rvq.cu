@@ -434,8 +434,8 @@ __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restric
         *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = 0.0f;
       }
       code_norm[static_cast<int64_t>(s) * kpad + j] = CUDART_INF_F;
-      // padding codes screen far below every real code
-      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -1.0e38f;
+      // padding codes screen at -inf, below every real (finite) code
+      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -CUDART_INF_F;
       for (int e = 1; e < 8; ++e) *reinterpret_cast<float*>(tile + tc_extra_offset(i, e)) = 0.0f;
     }
   }

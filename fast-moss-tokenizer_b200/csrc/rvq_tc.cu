@@ -341,17 +341,24 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// Maximum of 32 accumulator values as a depth-5 tree (independent pairs).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of 32 accumulator values: a depth-4 tree of three-input maxima
+// (16 instructions).
 __device__ __forceinline__ float max32(const uint32_t (&acc)[32]) {
-  float m[16];
+  float m[11];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) m[j] = fmaxf(__uint_as_float(acc[j]), __uint_as_float(acc[j + 16]));
-#pragma unroll
-  for (int w = 8; w > 0; w >>= 1) {
-#pragma unroll
-    for (int j = 0; j < w; ++j) m[j] = fmaxf(m[j], m[j + w]);
-  }
-  return m[0];
+  for (int j = 0; j < 10; ++j)
+    m[j] = max3f(__uint_as_float(acc[3 * j]), __uint_as_float(acc[3 * j + 1]),
+                 __uint_as_float(acc[3 * j + 2]));
+  m[10] = fmaxf(__uint_as_float(acc[30]), __uint_as_float(acc[31]));
+  const float a = max3f(m[0], m[1], m[2]), b = max3f(m[3], m[4], m[5]);
+  const float c = max3f(m[6], m[7], m[8]), d = fmaxf(m[9], m[10]);
+  return fmaxf(max3f(a, b, c), d);
 }
 
 // Bit j set iff acc[j] >= athr; four independent 8-bit partial masks.
@@ -509,13 +516,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     // of the stage boundary.
     auto write_a = [&]() {
       const uint32_t a_base = smem_u32(sm.a);
+      if (copies == 2) {
 #pragma unroll
-      for (int c = 0; c < kDim / 4; ++c) {
-        const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
-        const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
-        st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
-        if (copies == 2)
+        for (int c = 0; c < kDim / 4; ++c) {
+          const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
+          const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
+          st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
           st_shared_v4(a_base + sw128_offset(lr + rpc, 4 * c, kRows * 128u), x0, x1, x2, x3);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < kDim / 4; ++c) {
+          const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
+          const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
+          st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
+        }
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&sm.a_full);
@@ -626,25 +641,41 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       // (distance, code) key wins, i.e. the first minimum.
       bool fast = sm.pre_slow[lr] == 0;
       float gmax = -CUDART_INF_F;
-      for (int p = 0; p < nparts; ++p) {
-        fast = fast && sm.nrec_h[p * rpc + lr] <= kRec;
-        gmax = fmaxf(gmax, sm.amax_h[p * rpc + lr]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        if (p < nparts) {
+          fast = fast && sm.nrec_h[p * rpc + lr] <= kRec;
+          gmax = fmaxf(gmax, sm.amax_h[p * rpc + lr]);
+        }
       }
       const float athr = gmax - window;
+      // A row needs the exact scan when its preconditions failed or its
+      // candidates overflow the queue; the flag rides on the next barrier.
+      int slow_flag = (owner && valid && !fast) ? 1 : 0;
       // Count the surviving candidates, keeping the first four in registers
       // for the queue fill and sending their codewords on their way into L1
       // (the lane that resolves a candidate reads it from there).
       int cnt = 0;
       int c0 = 0, c1 = 0, c2 = 0, c3 = 0;
       if (fast) {
-        for (int e = 0; e < nrec; ++e) {
-          if (sm.rec_max[e][slot] < athr) continue;
+        // the records' fields are loaded together, then walked
+        float rmax[kRec];
+        uint32_t rmask[kRec];
+#pragma unroll
+        for (int e = 0; e < kRec; ++e) {
+          rmax[e] = e < nrec ? sm.rec_max[e][slot] : -CUDART_INF_F;
+          rmask[e] = e < nrec ? sm.rec_mask[e][slot] : 0u;
+        }
+#pragma unroll
+        for (int e = 0; e < kRec; ++e) {
+          if (rmax[e] < athr || rmask[e] == 0u) continue;
           const int base = sm.rec_chunk[e][slot] * 32;
-          for (uint32_t m = sm.rec_mask[e][slot]; m; m &= m - 1) {
+          for (uint32_t m = rmask[e]; m; m &= m - 1) {
             const int j = base + (__ffs(m) - 1);
             if (cnt < 4) {
-              prefetch_l1(book + static_cast<int64_t>(j < a.k ? j : 0) * kDim);
-              prefetch_l1(book + static_cast<int64_t>(j < a.k ? j : 0) * kDim + 32);
+              const int jc = j < a.k ? j : 0;
+              prefetch_l1(book + static_cast<int64_t>(jc) * kDim);
+              prefetch_l1(book + static_cast<int64_t>(jc) * kDim + 32);
               c3 = cnt == 3 ? j : c3;
               c2 = cnt == 2 ? j : c2;
               c1 = cnt == 1 ? j : c1;
@@ -664,6 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       int* queue = sm.queue[warp];
       if (incl > kQueue) {
         sm.row_bad[lr] = 1;  // does not fit: exact scan
+        slow_flag = 1;
       } else if (cnt > 4) {  // rare: walk the records again
         int pos = incl - cnt;
         for (int e = 0; e < nrec; ++e) {
@@ -705,16 +737,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         atomicMin(&sm.best[rr],
                   (static_cast<unsigned long long>(order_key(dist)) << 32) | static_cast<uint32_t>(j));
       }
-      epi_bar();  // every candidate of every row is in
+      // every candidate of every row is in; is any row flagged?
+      const int any_slow = epi_bar_or(slow_flag);
       int winner = -1;
       if (owner && fast && sm.row_bad[lr] == 0 && sm.best[lr] != ~0ull)
         winner = static_cast<int>(sm.best[lr] & 0xffffffffu);
-      if (owner && valid && winner < 0) {
-        const int at = atomicAdd(&sm.slow_count, 1);
-        sm.slow_list[at] = lr;
+      int nslow = 0;
+      if (any_slow) {
+        if (owner && valid && winner < 0) {
+          const int at = atomicAdd(&sm.slow_count, 1);
+          sm.slow_list[at] = lr;
+        }
+        epi_bar();
+        nslow = sm.slow_count;
       }
-      epi_bar();
-      const int nslow = sm.slow_count;
       if (nslow > 0) {
         // exact scan, one warp per row; 2r is read back from the A image
         for (int i = warp; i < nslow; i += kEpiThreads / 32) {
@@ -729,6 +765,13 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         if (owner && valid && winner < 0) winner = sm.sel[lr];
         epi_bar();
         if (warp == 0 && lane == 0) sm.slow_count = 0;
+      }
+      if (owner && valid && winner < 0) {
+        // Unreachable: on the fast path the screening maximum is a real code
+        // (padding codes screen at -inf, real ones are finite), so every
+        // unflagged row has a resolved candidate.  Kept in bounds, reported.
+        record_device_error(MOSS_ERR_UNSUPPORTED);
+        winner = 0;
       }
       if (owner && valid) {
         // ---- update the residual (the reconstruction is summed at the end)
