@@ -68,6 +68,39 @@ __device__ __forceinline__ Welford welford_merge(Welford b, Welford a) {
   return {0.0f, 0.0f, count};
 }
 
+// The merge of two states whose counts are compile-time constants: every
+// thread of a row holds 4 * NVT values when the row width is a multiple of
+// 512, so the counts of the whole reduction tree are known in advance, and
+// the reciprocal and the two weights are the same correctly rounded values
+// the general merge computes (IEEE float constant expressions).
+template <int CA, int CB>
+struct MergeWeights {
+  static constexpr float count = static_cast<float>(CA + CB);
+  static constexpr float coef = 1.0f / count;
+  static constexpr float na = static_cast<float>(CA) * coef;
+  static constexpr float nb = static_cast<float>(CB) * coef;
+};
+
+template <int CA, int CB>
+__device__ __forceinline__ Welford welford_merge_const(Welford b, Welford a) {
+  using W = MergeWeights<CA, CB>;
+  const float delta = __fsub_rn(b.mean, a.mean);
+  const float mean = __fmaf_rn(W::na, a.mean, __fmul_rn(W::nb, b.mean));
+  const float m2 = __fmaf_rn(__fmul_rn(__fmul_rn(delta, delta), static_cast<float>(CA)), W::nb,
+                             __fadd_rn(a.m2, b.m2));
+  return {mean, m2, W::count};
+}
+
+// Shuffle-down level with offset O of the full-row reduction (every lane's
+// count is C before the level).
+template <int C, int O>
+__device__ __forceinline__ Welford shuffle_level_const(Welford w) {
+  Welford o;
+  o.mean = __shfl_down_sync(0xffffffffu, w.mean, O);
+  o.m2 = __shfl_down_sync(0xffffffffu, w.m2, O);
+  return welford_merge_const<C, C>(w, o);
+}
+
 template <int DT>
 __device__ __forceinline__ float4 load4(const void* base, int64_t i4, bool vec_ok) {
   if constexpr (DT == MOSS_F32) {
@@ -125,7 +158,7 @@ __device__ __forceinline__ float4 ln_out(float4 v, float mean, float rstd, const
 
 // One 128-thread block per row.  NVT = float4 vectors per thread
 // (n <= 512 * NVT).  HAS_U selects the fused residual form.
-template <int NVT, int XDT, int UDT, bool HAS_U>
+template <int NVT, int XDT, int UDT, bool HAS_U, bool FULL>
 __global__ void __launch_bounds__(128) residual_ln_kernel(
     const void* __restrict__ x, const void* __restrict__ u, const float* __restrict__ scale,
     const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int n,
@@ -169,13 +202,22 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
       w = welford_push(w, val[m].w, 4 * m + 4);
     }
   }
+  if constexpr (FULL) {
+    constexpr int C = 4 * NVT;
+    w = shuffle_level_const<C, 16>(w);
+    w = shuffle_level_const<2 * C, 8>(w);
+    w = shuffle_level_const<4 * C, 4>(w);
+    w = shuffle_level_const<8 * C, 2>(w);
+    w = shuffle_level_const<16 * C, 1>(w);
+  } else {
 #pragma unroll
-  for (int offset = 16; offset > 0; offset >>= 1) {
-    Welford o;
-    o.mean = __shfl_down_sync(0xffffffffu, w.mean, offset);
-    o.m2 = __shfl_down_sync(0xffffffffu, w.m2, offset);
-    o.count = __shfl_down_sync(0xffffffffu, w.count, offset);
-    w = welford_merge(w, o);
+    for (int offset = 16; offset > 0; offset >>= 1) {
+      Welford o;
+      o.mean = __shfl_down_sync(0xffffffffu, w.mean, offset);
+      o.m2 = __shfl_down_sync(0xffffffffu, w.m2, offset);
+      o.count = __shfl_down_sync(0xffffffffu, w.count, offset);
+      w = welford_merge(w, o);
+    }
   }
   if (lane == 0) {
     red[warp][0] = w.mean;
@@ -188,7 +230,14 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
     const Welford w1 = {red[1][0], red[1][1], red[1][2]};
     const Welford w2 = {red[2][0], red[2][1], red[2][2]};
     const Welford w3 = {red[3][0], red[3][1], red[3][2]};
-    const Welford t = welford_merge(welford_merge(w0, w2), welford_merge(w1, w3));
+    Welford t;
+    if constexpr (FULL) {
+      constexpr int CW = 128 * NVT;  // values per warp
+      t = welford_merge_const<2 * CW, 2 * CW>(welford_merge_const<CW, CW>(w0, w2),
+                                              welford_merge_const<CW, CW>(w1, w3));
+    } else {
+      t = welford_merge(welford_merge(w0, w2), welford_merge(w1, w3));
+    }
     const float var = __fdiv_rn(t.m2, static_cast<float>(n));
     const float rstd = rsqrtf(__fadd_rn(var, eps));
     stats[0] = t.mean;
@@ -246,8 +295,13 @@ static void launch_ln(const void* x, const void* u, const float* scale, const fl
                       const float* beta, float eps, int64_t rows, int n, float* res,
                       float* normed, float* mean, float* rstd, bool xv, bool uv,
                       cudaStream_t s) {
-  residual_ln_kernel<NVT, XDT, UDT, HAS_U><<<static_cast<unsigned>(rows), 128, 0, s>>>(
-      x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
+  if (n == 512 * NVT) {  // every thread holds 4 * NVT values: constant merge weights
+    residual_ln_kernel<NVT, XDT, UDT, HAS_U, true><<<static_cast<unsigned>(rows), 128, 0, s>>>(
+        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
+  } else {
+    residual_ln_kernel<NVT, XDT, UDT, HAS_U, false><<<static_cast<unsigned>(rows), 128, 0, s>>>(
+        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
+  }
 }
 
 template <int XDT, int UDT, bool HAS_U>
