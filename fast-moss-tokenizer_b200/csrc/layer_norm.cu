@@ -162,8 +162,9 @@ template <int NVT, int XDT, int UDT, bool HAS_U, bool FULL>
 __global__ void __launch_bounds__(128) residual_ln_kernel(
     const void* __restrict__ x, const void* __restrict__ u, const float* __restrict__ scale,
     const float* __restrict__ gamma, const float* __restrict__ beta, float eps, int n,
-    float* __restrict__ residual_out, float* __restrict__ normed_out,
-    float* __restrict__ mean_out, float* __restrict__ rstd_out, bool x_vec, bool u_vec) {
+    float* __restrict__ residual_out, void* __restrict__ normed_out,
+    float* __restrict__ mean_out, float* __restrict__ rstd_out, bool x_vec, bool u_vec,
+    bool out_bf16) {
   __shared__ float red[4][3];
   __shared__ float stats[2];
   const int tid = threadIdx.x;
@@ -251,7 +252,17 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
   for (int m = 0; m < NVT; ++m) {
     const int i = tid + 128 * m;
     if (i < nvec) {
-      reinterpret_cast<float4*>(normed_out)[base4 + i] = ln_out(val[m], mean, rstd, gamma, beta, i);
+      const float4 o = ln_out(val[m], mean, rstd, gamma, beta, i);
+      if (out_bf16) {
+        // the consumer's cast: round to nearest even, as torch's .to(bfloat16)
+        reinterpret_cast<uint2*>(normed_out)[base4 + i] = make_uint2(
+            static_cast<uint32_t>(f32_to_bf16_bits(o.x)) |
+                (static_cast<uint32_t>(f32_to_bf16_bits(o.y)) << 16),
+            static_cast<uint32_t>(f32_to_bf16_bits(o.z)) |
+                (static_cast<uint32_t>(f32_to_bf16_bits(o.w)) << 16));
+      } else {
+        reinterpret_cast<float4*>(normed_out)[base4 + i] = o;
+      }
     }
   }
 }
@@ -293,38 +304,38 @@ __global__ void __launch_bounds__(256) scale_add_scalar_kernel(const void* __res
 template <int NVT, int XDT, int UDT, bool HAS_U>
 static void launch_ln(const void* x, const void* u, const float* scale, const float* gamma,
                       const float* beta, float eps, int64_t rows, int n, float* res,
-                      float* normed, float* mean, float* rstd, bool xv, bool uv,
+                      void* normed, float* mean, float* rstd, bool xv, bool uv, bool ob,
                       cudaStream_t s) {
   if (n == 512 * NVT) {  // every thread holds 4 * NVT values: constant merge weights
     residual_ln_kernel<NVT, XDT, UDT, HAS_U, true><<<static_cast<unsigned>(rows), 128, 0, s>>>(
-        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
+        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv, ob);
   } else {
     residual_ln_kernel<NVT, XDT, UDT, HAS_U, false><<<static_cast<unsigned>(rows), 128, 0, s>>>(
-        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv);
+        x, u, scale, gamma, beta, eps, n, res, normed, mean, rstd, xv, uv, ob);
   }
 }
 
 template <int XDT, int UDT, bool HAS_U>
 static int dispatch_nvt(int nvt, const void* x, const void* u, const float* scale,
                         const float* gamma, const float* beta, float eps, int64_t rows, int n,
-                        float* res, float* normed, float* mean, float* rstd, bool xv, bool uv,
-                        cudaStream_t s) {
+                        float* res, void* normed, float* mean, float* rstd, bool xv, bool uv,
+                        bool ob, cudaStream_t s) {
   switch (nvt) {
     case 1:
       launch_ln<1, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
-                                    rstd, xv, uv, s);
+                                    rstd, xv, uv, ob, s);
       return MOSS_OK;
     case 2:
       launch_ln<2, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
-                                    rstd, xv, uv, s);
+                                    rstd, xv, uv, ob, s);
       return MOSS_OK;
     case 3:
       launch_ln<3, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
-                                    rstd, xv, uv, s);
+                                    rstd, xv, uv, ob, s);
       return MOSS_OK;
     case 4:
       launch_ln<4, XDT, UDT, HAS_U>(x, u, scale, gamma, beta, eps, rows, n, res, normed, mean,
-                                    rstd, xv, uv, s);
+                                    rstd, xv, uv, ob, s);
       return MOSS_OK;
     default:
       return MOSS_ERR_UNSUPPORTED;
@@ -333,8 +344,8 @@ static int dispatch_nvt(int nvt, const void* x, const void* u, const float* scal
 
 static int ln_common(const char* name, const void* x, int x_dtype, const void* u, int u_dtype,
                      const float* scale, const float* gamma, const float* beta, float eps,
-                     int64_t rows, int64_t n, float* residual_out, float* normed_out,
-                     float* mean, float* rstd, void* stream) {
+                     int64_t rows, int64_t n, float* residual_out, void* normed_out,
+                     int normed_dtype, float* mean, float* rstd, void* stream) {
   if (rows < 0 || n <= 0) return fail(MOSS_ERR_VALUE, "%s: rows must be >= 0 and n > 0", name);
   if (x == nullptr || normed_out == nullptr)
     return fail(MOSS_ERR_VALUE, "%s: null input or output pointer", name);
@@ -349,7 +360,11 @@ static int ln_common(const char* name, const void* x, int x_dtype, const void* u
                 "%s: width %lld is not a multiple of 4 (PyTorch uses its non-vectorised "
                 "layer norm there)",
                 name, static_cast<long long>(n));
-  if ((gamma && !aligned16(gamma)) || (beta && !aligned16(beta)) || !aligned16(normed_out) ||
+  if (normed_dtype != MOSS_F32 && normed_dtype != MOSS_BF16)
+    return fail(MOSS_ERR_VALUE, "%s: normalised output dtype must be float32 or bfloat16", name);
+  const bool ob = normed_dtype == MOSS_BF16;
+  if ((gamma && !aligned16(gamma)) || (beta && !aligned16(beta)) ||
+      (ob ? (reinterpret_cast<uintptr_t>(normed_out) & 7u) != 0 : !aligned16(normed_out)) ||
       (residual_out && !aligned16(residual_out)) || (scale && !aligned16(scale)))
     return fail(MOSS_ERR_UNSUPPORTED,
                 "%s: gamma/beta/scale/outputs must be 16-byte aligned (PyTorch uses its "
@@ -374,19 +389,19 @@ static int ln_common(const char* name, const void* x, int x_dtype, const void* u
   int st;
   if (u == nullptr) {
     st = dispatch_nvt<MOSS_F32, MOSS_F32, false>(nvt, x, nullptr, nullptr, gamma, beta, eps, rows,
-                                                 ni, nullptr, normed_out, mean, rstd, xv, uv, s);
+                                                 ni, nullptr, normed_out, mean, rstd, xv, uv, ob, s);
   } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_F32) {
     st = dispatch_nvt<MOSS_F32, MOSS_F32, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
-                                                residual_out, normed_out, mean, rstd, xv, uv, s);
+                                                residual_out, normed_out, mean, rstd, xv, uv, ob, s);
   } else if (x_dtype == MOSS_F32 && u_dtype == MOSS_BF16) {
     st = dispatch_nvt<MOSS_F32, MOSS_BF16, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
-                                                 residual_out, normed_out, mean, rstd, xv, uv, s);
+                                                 residual_out, normed_out, mean, rstd, xv, uv, ob, s);
   } else if (x_dtype == MOSS_BF16 && u_dtype == MOSS_F32) {
     st = dispatch_nvt<MOSS_BF16, MOSS_F32, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
-                                                 residual_out, normed_out, mean, rstd, xv, uv, s);
+                                                 residual_out, normed_out, mean, rstd, xv, uv, ob, s);
   } else {
     st = dispatch_nvt<MOSS_BF16, MOSS_BF16, true>(nvt, x, u, scale, gamma, beta, eps, rows, ni,
-                                                  residual_out, normed_out, mean, rstd, xv, uv, s);
+                                                  residual_out, normed_out, mean, rstd, xv, uv, ob, s);
   }
   if (st != MOSS_OK) return fail(st, "%s: unsupported width", name);
   return launch_status(name);
@@ -400,7 +415,7 @@ extern "C" int moss_layer_norm(const float* x, const float* gamma, const float* 
                                int64_t rows, int64_t n, float* y, float* mean, float* rstd,
                                void* stream) {
   return ln_common("moss_layer_norm", x, MOSS_F32, nullptr, MOSS_F32, nullptr, gamma, beta, eps,
-                   rows, n, nullptr, y, mean, rstd, stream);
+                   rows, n, nullptr, y, MOSS_F32, mean, rstd, stream);
 }
 
 extern "C" int moss_residual_layer_norm(const void* x, int x_dtype, const void* u, int u_dtype,
@@ -410,7 +425,17 @@ extern "C" int moss_residual_layer_norm(const void* x, int x_dtype, const void* 
                                         float* rstd, void* stream) {
   if (u == nullptr) return fail(MOSS_ERR_VALUE, "moss_residual_layer_norm: update is null");
   return ln_common("moss_residual_layer_norm", x, x_dtype, u, u_dtype, scale, gamma, beta, eps,
-                   rows, n, residual_out, normed_out, mean, rstd, stream);
+                   rows, n, residual_out, normed_out, MOSS_F32, mean, rstd, stream);
+}
+
+extern "C" int moss_residual_layer_norm_out(const void* x, int x_dtype, const void* u,
+                                            int u_dtype, const float* scale, const float* gamma,
+                                            const float* beta, float eps, int64_t rows, int64_t n,
+                                            float* residual_out, void* normed_out,
+                                            int normed_dtype, float* mean, float* rstd,
+                                            void* stream) {
+  return ln_common("moss_residual_layer_norm_out", x, x_dtype, u, u_dtype, scale, gamma, beta,
+                   eps, rows, n, residual_out, normed_out, normed_dtype, mean, rstd, stream);
 }
 
 extern "C" int moss_scale_add(const void* x, int x_dtype, const void* u, int u_dtype,

@@ -287,6 +287,67 @@ __global__ void __launch_bounds__(256) rope_pair_kernel(RopeArgs a) {
   }
 }
 
+// ------------------------------------------------------------------ rope + history
+// RoPE whose rotated keys (and the values) go straight into an attention
+// history ring: one CTA per batch index and time tile (the phase table of
+// the tile shared by all heads, as rope_pair_kernel), one thread per
+// interleaved pair and head.  q -> oq contiguous [b,h,t,d]; k -> k_cache and
+// v -> v_cache at [b, h, slot[b, t], :] of contiguous [b, h, S, d] rings.  A
+// slot outside [0, S) is skipped and recorded in the device error word.
+struct RopeKvArgs {
+  RopeArgs r;
+  const void* v;
+  int64_t vs[4];
+  const int64_t* slots;  // [b, t]
+  void* k_cache;
+  void* v_cache;
+  int64_t cache_slots;
+};
+
+template <int DT>
+__global__ void __launch_bounds__(256) rope_kv_kernel(RopeKvArgs ka) {
+  extern __shared__ float smem[];
+  const RopeArgs& a = ka.r;
+  const int half = static_cast<int>(a.d >> 1);
+  const int64_t ntiles = (a.t + a.tt - 1) / a.tt;
+  const int64_t bi = blockIdx.x / ntiles;
+  const int64_t t0 = (blockIdx.x % ntiles) * a.tt;
+  const int tt = static_cast<int>(a.t - t0 < a.tt ? a.t - t0 : a.tt);
+  float* sc = smem;
+  float* ss = smem + a.tt * half;
+  fill_phase(a, bi, t0, tt, half, sc, ss);
+  __syncthreads();
+  const int items = static_cast<int>(a.h) * tt * half;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int p = it % half;
+    const int rest = it / half;
+    const int tl = rest % tt;
+    const int64_t hi = rest / tt;
+    const int64_t ti = t0 + tl;
+    const float c = sc[tl * half + p];
+    const float s = ss[tl * half + p];
+    const int64_t qb = bi * a.qs[0] + hi * a.qs[1] + ti * a.qs[2] + 2 * p * a.qs[3];
+    const int64_t kb = bi * a.ks[0] + hi * a.ks[1] + ti * a.ks[2] + 2 * p * a.ks[3];
+    const int64_t vb = bi * ka.vs[0] + hi * ka.vs[1] + ti * ka.vs[2] + 2 * p * ka.vs[3];
+    float q0, q1, k0, k1;
+    rotate_pair(load_as_f32<DT>(a.q, qb), load_as_f32<DT>(a.q, qb + a.qs[3]), c, s, q0, q1);
+    rotate_pair(load_as_f32<DT>(a.k, kb), load_as_f32<DT>(a.k, kb + a.ks[3]), c, s, k0, k1);
+    const int64_t o = ((bi * a.h + hi) * a.t + ti) * a.d + 2 * p;
+    store_from_f32<DT>(a.oq, o, q0);
+    store_from_f32<DT>(a.oq, o + 1, q1);
+    const int64_t slot = ka.slots[bi * a.t + ti];
+    if (slot < 0 || slot >= ka.cache_slots) {
+      record_device_error(MOSS_ERR_VALUE);
+      continue;
+    }
+    const int64_t co = ((bi * a.h + hi) * ka.cache_slots + slot) * a.d + 2 * p;
+    store_from_f32<DT>(ka.k_cache, co, k0);
+    store_from_f32<DT>(ka.k_cache, co + 1, k1);
+    store_from_f32<DT>(ka.v_cache, co, load_as_f32<DT>(ka.v, vb));
+    store_from_f32<DT>(ka.v_cache, co + 1, load_as_f32<DT>(ka.v, vb + ka.vs[3]));
+  }
+}
+
 // Streaming path for q and k whose rows are contiguous within each head
 // (innermost stride 1, time stride d): one CTA per SM.  A producer thread
 // streams tiles (one batch index, TT time steps, all heads) of q and k into
@@ -648,4 +709,50 @@ extern "C" int moss_rope(const void* q, const void* k, int dtype, const void* of
   a.b = b; a.h = h; a.t = t; a.d = d;
   for (int i = 0; i < 4; ++i) { a.qs[i] = q_strides[i]; a.ks[i] = k_strides[i]; }
   return rope_common("moss_rope", a, dtype, false, stream);
+}
+
+extern "C" int moss_rope_kv(const void* q, const void* k, const void* v, int dtype,
+                            const void* offset, int offset_dtype, float freq_coef,
+                            const int64_t* slots, void* oq, void* k_cache, void* v_cache,
+                            int64_t b, int64_t h, int64_t t, int64_t d, int64_t cache_slots,
+                            const int64_t* q_strides, const int64_t* k_strides,
+                            const int64_t* v_strides, void* stream) {
+  const char* name = "moss_rope_kv";
+  if (!q_strides || !k_strides || !v_strides) return fail(MOSS_ERR_VALUE, "%s: null strides", name);
+  if (b < 0 || h < 0 || t < 0 || d < 2 || (d & 1) || cache_slots < 1)
+    return fail(MOSS_ERR_VALUE, "%s: expected equal B,H,T,even-D inputs and a non-empty ring", name);
+  if (dtype != MOSS_F32 && dtype != MOSS_BF16)
+    return fail(MOSS_ERR_VALUE, "%s: q/k/v dtype must be float32 or bfloat16", name);
+  if (offset_dtype < 0 || offset_dtype > 2)
+    return fail(MOSS_ERR_VALUE, "%s: offset dtype must be int64, int32 or float32", name);
+  if (d > 1024) return fail(MOSS_ERR_UNSUPPORTED, "%s: head dim above 1024", name);
+  if (b * h * t == 0) return MOSS_OK;
+  if (!q || !k || !v || !offset || !slots || !oq || !k_cache || !v_cache)
+    return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  RopeKvArgs ka{};
+  RopeArgs& a = ka.r;
+  a.q = q; a.k = k; a.offset = offset; a.offset_dtype = offset_dtype; a.coef = freq_coef;
+  a.oq = oq; a.ok = nullptr;
+  a.b = b; a.h = h; a.t = t; a.d = d;
+  for (int i = 0; i < 4; ++i) {
+    a.qs[i] = q_strides[i];
+    a.ks[i] = k_strides[i];
+    ka.vs[i] = v_strides[i];
+  }
+  ka.v = v; ka.slots = slots; ka.k_cache = k_cache; ka.v_cache = v_cache;
+  ka.cache_slots = cache_slots;
+  const int half = static_cast<int>(d / 2);
+  int tt = 256 / half;
+  if (tt < 1) tt = 1;
+  if (tt > t) tt = static_cast<int>(t);
+  a.tt = tt;
+  const int64_t ntiles = (t + tt - 1) / tt;
+  if (b * ntiles > 0x7fffffffLL || h * tt * half > 0x7fffffffLL)
+    return fail(MOSS_ERR_UNSUPPORTED, "%s: grid too large", name);
+  const unsigned grid = static_cast<unsigned>(b * ntiles);
+  const size_t shmem = sizeof(float) * 2 * tt * half;
+  cudaStream_t s = as_stream(stream);
+  if (dtype == MOSS_BF16) rope_kv_kernel<MOSS_BF16><<<grid, 256, shmem, s>>>(ka);
+  else rope_kv_kernel<MOSS_F32><<<grid, 256, shmem, s>>>(ka);
+  return launch_status(name);
 }

@@ -21,6 +21,7 @@ from .v2_pointwise import (
     layer_norm,
     residual_layer_norm,
     rope,
+    rope_kv,
     rotate,
     scale_add,
 )
@@ -33,6 +34,7 @@ from .v2_runtime import V2Runtime, optimized, validate
 __all__ = [
     "rotate",
     "rope",
+    "rope_kv",
     "scale_add",
     "layer_norm",
     "residual_layer_norm",

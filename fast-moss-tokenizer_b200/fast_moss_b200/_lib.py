@@ -46,10 +46,14 @@ _SIGNATURES = {
     "moss_layer_norm": (_i, [_vp, _vp, _vp, _f, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_residual_layer_norm": (
         _i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _f, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "moss_residual_layer_norm_out": (
+        _i, [_vp, _i, _vp, _i, _vp, _vp, _vp, _f, _i64, _i64, _vp, _vp, _i, _vp, _vp, _vp]),
     "moss_rotate": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _pi64, _pi64,
                          _vp]),
     "moss_rope": (_i, [_vp, _vp, _i, _vp, _i, _f, _vp, _vp, _i64, _i64, _i64, _i64, _pi64, _pi64,
                        _vp]),
+    "moss_rope_kv": (_i, [_vp, _vp, _vp, _i, _vp, _i, _f, _vp, _vp, _vp, _vp, _i64, _i64, _i64,
+                          _i64, _i64, _pi64, _pi64, _pi64, _vp]),
     "moss_gated_act": (_i, [_vp, _vp, _vp, _i, _i64, _i64, _i, _i, _vp]),
     "moss_lfq_prepare": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "moss_lfq_select": (_i, [_vp, _vp, _vp, _vp, _vp, _pi64, _i64, _i64, _i64, _i64, _i, _vp, _vp,

@@ -8,11 +8,15 @@ FP32 residual stream and parameters, bf16 GEMMs on cached bf16 weights
 (:77-106, F.linear as in :104).  Per layer the hot-path ops run as the
 native kernels of libfast_moss_b200:
 
-  LayerNorm of the stack input              moss_layer_norm
-  rotary phase + rotation of q and k         moss_rope
-  residual + layer scale 1 + LayerNorm 2     moss_residual_layer_norm (one pass)
+  LayerNorm of the stack input              moss_residual_layer_norm_out
+  rotary phase + rotation of q and k, the    moss_rope_kv
+    rotated keys and the values written
+    straight into the attention history
+  residual + layer scale 1 + LayerNorm 2     moss_residual_layer_norm_out (one pass,
+                                             normed output stored as the next
+                                             GEMM's bf16 input)
   feed-forward bias + activation             moss_gated_act
-  residual + layer scale 2 + next LN 1       moss_residual_layer_norm
+  residual + layer scale 2 + next LN 1       moss_residual_layer_norm_out
                                              (moss_scale_add after the last layer)
 
 GEMMs (cuBLAS) and attention (SDPA) stay library calls, as in the reference;
@@ -37,7 +41,7 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .graphs import GraphedCallable
-from .v2_pointwise import gated_activation, layer_norm, residual_layer_norm, rope, scale_add
+from .v2_pointwise import gated_activation, layer_norm, residual_layer_norm, rope_kv, scale_add
 
 
 @dataclass(frozen=True)
@@ -193,29 +197,30 @@ class StreamingTransformer:
         h, dh = cfg.heads, cfg.head_dim
         offset = hist.pos  # position of the chunk's first token (advanced at the end)
         _, slots, mask = hist.advance(t)
-        index = slots[:, None, :, None].expand(s, h, t, dh)
         first = self.layers[0]
         x = x.contiguous()
-        normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps)
+        bf16 = torch.bfloat16
+        # LayerNorm outputs go straight to the next GEMM as its bf16 input
+        normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps, out_dtype=bf16)
         for i, p in enumerate(self.layers):
-            qkv = F.linear(normed.to(torch.bfloat16), p["qkv_w16"], p["qkv_b16"])
+            qkv = F.linear(normed, p["qkv_w16"], p["qkv_b16"])
             qkv = qkv.view(s, t, 3, h, dh)
-            q, k = rope(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), offset,
-                        cfg.max_period)
-            hist.keys[i].scatter_(2, index, k)
-            hist.values[i].scatter_(2, index, qkv[:, :, 2].transpose(1, 2))
+            q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
+                        qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
+                        hist.keys[i], hist.values[i])
             with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
                 a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
                                                    attn_mask=mask)
             u = F.linear(a.transpose(1, 2).reshape(s, t, d), p["out_w16"], p["out_b16"])
-            x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps)
-            f = F.linear(normed.to(torch.bfloat16), p["ffn1_w16"])
+            x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps,
+                                            out_dtype=bf16)
+            f = F.linear(normed, p["ffn1_w16"])
             f = gated_activation(f, p["ffn1_b16"], cfg.activation, cfg.gated)
             u = F.linear(f, p["ffn2_w16"], p["ffn2_b16"])
             if i + 1 < len(self.layers):
                 nxt = self.layers[i + 1]
                 x, normed = residual_layer_norm(x, u, p["ls2"], nxt["norm1_w"], nxt["norm1_b"],
-                                                cfg.eps)
+                                                cfg.eps, out_dtype=bf16)
             else:
                 x = scale_add(x, u, p["ls2"])
         hist.pos.add_(t)

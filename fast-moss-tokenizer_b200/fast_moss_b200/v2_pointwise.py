@@ -96,6 +96,61 @@ def rope(q, k, offset, max_period):
     return oq, ok
 
 
+def rope_kv(q, k, v, offset, max_period, slots, k_cache, v_cache):
+    """`rope` with the rotated keys and the values written into a history ring.
+
+    q, k, v: [B, H, T, D] (any strides, same dtype); offset: [B] on q's
+    device; slots: int64 [B, T] on q's device, the ring slot of every token;
+    k_cache, v_cache: contiguous [B, H, S, D] of q's dtype.  Returns the
+    rotated q (contiguous); k_cache[b, h, slots[b, t]] receives the rotated
+    key and v_cache the value.  Same bits as `rope` followed by
+    `k_cache.scatter_(2, ...)` / `v_cache.scatter_(2, ...)`.
+    """
+    if q.ndim != 4 or q.shape != k.shape or q.shape != v.shape or q.shape[-1] % 2:
+        raise ValueError("Expected equal B,H,T,even-D q, k and v")
+    b, h, t, d = q.shape
+    if (
+        q.dtype not in _DTYPES
+        or k.dtype != q.dtype
+        or v.dtype != q.dtype
+        or not q.is_cuda
+        or any(x.device != q.device for x in (k, v, offset, slots, k_cache, v_cache))
+        or offset.numel() != b
+        or slots.shape != (b, t)
+        or slots.dtype != torch.int64
+        or k_cache.ndim != 4
+        or k_cache.shape[:2] != (b, h)
+        or k_cache.shape[3] != d
+        or v_cache.shape != k_cache.shape
+        or k_cache.dtype != q.dtype
+        or v_cache.dtype != q.dtype
+        or not k_cache.is_contiguous()
+        or not v_cache.is_contiguous()
+    ):
+        raise ValueError("Expected same-device q/k/v, [B] offset, int64 [B,T] slots and "
+                         "contiguous [B,H,S,D] caches of q's dtype")
+    if offset.dtype == torch.int64:
+        odt = 0
+    elif offset.dtype == torch.int32:
+        odt = 1
+    else:
+        odt = 2
+        offset = offset.float()
+    offset = offset.contiguous()
+    slots = slots.contiguous()
+    coef = -math.log(max_period) * 2 / d
+    oq = torch.empty(q.shape, device=q.device, dtype=q.dtype)
+    if q.numel():
+        with torch.cuda.device(q.device):
+            _lib.call(
+                "moss_rope_kv", q.data_ptr(), k.data_ptr(), v.data_ptr(), _DTYPES[q.dtype],
+                offset.data_ptr(), odt, coef, slots.data_ptr(), oq.data_ptr(),
+                k_cache.data_ptr(), v_cache.data_ptr(), b, h, t, d, k_cache.shape[2],
+                _lib.strides(q.stride()), _lib.strides(k.stride()), _lib.strides(v.stride()),
+                _stream(q.device))
+    return oq
+
+
 def scale_add(x, update, scale):
     """Residual update x + update * scale (FP32 out, no FMA).
 
@@ -137,9 +192,17 @@ def _check_norm_params(x, weight, bias):
             raise ValueError("Expected contiguous same-device FP32 LayerNorm parameters")
 
 
-def layer_norm(x, weight, bias, eps=1e-5, *, return_stats=False):
+def _out_dtype(out_dtype):
+    if out_dtype not in _DTYPES:
+        raise ValueError("out_dtype must be torch.float32 or torch.bfloat16")
+    return _DTYPES[out_dtype]
+
+
+def layer_norm(x, weight, bias, eps=1e-5, *, return_stats=False, out_dtype=torch.float32):
     """FP32 LayerNorm over the last dim, bit-identical to torch's CUDA op.
 
+    out_dtype=torch.bfloat16 stores the result rounded to bf16 (the bits of
+    `layer_norm(...).to(torch.bfloat16)`, without a separate cast kernel).
     Raises _lib.UnsupportedError for widths PyTorch would not vectorise
     (n % 4 != 0) or misaligned buffers.
     """
@@ -149,26 +212,29 @@ def layer_norm(x, weight, bias, eps=1e-5, *, return_stats=False):
     x = x.contiguous()
     n = x.shape[-1]
     rows = x.numel() // n if n else 0
-    y = torch.empty_like(x)
+    odt = _out_dtype(out_dtype)
+    y = torch.empty(x.shape, device=x.device, dtype=out_dtype)
     mean = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
     rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
     if x.numel():
         with torch.cuda.device(x.device):
             _lib.call(
-                "moss_layer_norm", x.data_ptr(), weight.data_ptr() if weight is not None else None,
-                bias.data_ptr() if bias is not None else None, float(eps), rows, n, y.data_ptr(),
-                mean.data_ptr() if mean is not None else None,
+                "moss_residual_layer_norm_out", x.data_ptr(), _lib.F32, None, _lib.F32, None,
+                weight.data_ptr() if weight is not None else None,
+                bias.data_ptr() if bias is not None else None, float(eps), rows, n, None,
+                y.data_ptr(), odt, mean.data_ptr() if mean is not None else None,
                 rstd.data_ptr() if rstd is not None else None, _stream(x.device))
     return (y, mean, rstd) if return_stats else y
 
 
 def residual_layer_norm(x, update, scale, weight, bias, eps=1e-5, *, write_residual=True,
-                        return_stats=False):
+                        return_stats=False, out_dtype=torch.float32):
     """Fused `r = scale_add(x, update, scale)` and `LayerNorm(r)` in one pass.
 
     Returns (r, normed) -- r is None when write_residual is False -- plus
     (mean, rstd) when return_stats.  Same bits as the reference's
-    scale_add followed by torch's CUDA layer norm.
+    scale_add followed by torch's CUDA layer norm; out_dtype=torch.bfloat16
+    stores normed rounded to bf16 (the next Linear's input cast).
     """
     if (
         x.shape != update.shape
@@ -187,18 +253,19 @@ def residual_layer_norm(x, update, scale, weight, bias, eps=1e-5, *, write_resid
     x, update, scale = x.contiguous(), update.contiguous(), scale.contiguous()
     n = x.shape[-1]
     rows = x.numel() // n if n else 0
+    odt = _out_dtype(out_dtype)
     res = torch.empty(x.shape, device=x.device, dtype=torch.float32) if write_residual else None
-    y = torch.empty(x.shape, device=x.device, dtype=torch.float32)
+    y = torch.empty(x.shape, device=x.device, dtype=out_dtype)
     mean = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
     rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if return_stats else None
     if x.numel():
         with torch.cuda.device(x.device):
             _lib.call(
-                "moss_residual_layer_norm", x.data_ptr(), _DTYPES[x.dtype], update.data_ptr(),
+                "moss_residual_layer_norm_out", x.data_ptr(), _DTYPES[x.dtype], update.data_ptr(),
                 _DTYPES[update.dtype], scale.data_ptr(),
                 weight.data_ptr() if weight is not None else None,
                 bias.data_ptr() if bias is not None else None, float(eps), rows, n,
-                res.data_ptr() if res is not None else None, y.data_ptr(),
+                res.data_ptr() if res is not None else None, y.data_ptr(), odt,
                 mean.data_ptr() if mean is not None else None,
                 rstd.data_ptr() if rstd is not None else None, _stream(x.device))
     if return_stats:

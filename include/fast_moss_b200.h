@@ -101,6 +101,21 @@ MOSS_API int moss_residual_layer_norm(const void* x, int x_dtype, const void* u,
                              void* stream);
 
 /* ---------------------------------------------------------------------------
+ * moss_residual_layer_norm (u != NULL) or moss_layer_norm (u == NULL, x
+ * float32) with the normalised output stored in normed_dtype: MOSS_F32, or
+ * MOSS_BF16 rounded to nearest even -- the bits of the bf16 cast that the
+ * patched layer's next Linear applies to norm(x) under autocast
+ * (fast_moss/v2_runtime.py:104, :259), so the cast needs no kernel of its
+ * own.  A bf16 normed_out must be 8-byte aligned.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_residual_layer_norm_out(const void* x, int x_dtype, const void* u,
+                             int u_dtype, const float* scale,
+                             const float* gamma, const float* beta, float eps,
+                             int64_t rows, int64_t n, float* residual_out,
+                             void* normed_out, int normed_dtype, float* mean,
+                             float* rstd, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Rotary embedding on q and k with caller-supplied tables.
  * Replaces fast_moss/v2_pointwise.py:50-89 (`_rotate` / `rotate`):
  *   o[2p]   = q[2p]*cos - q[2p+1]*sin
@@ -128,6 +143,25 @@ MOSS_API int moss_rope(const void* q, const void* k, int dtype, const void* offs
               int offset_dtype, float freq_coef, void* oq, void* ok, int64_t b,
               int64_t h, int64_t t, int64_t d, const int64_t* q_strides,
               const int64_t* k_strides, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * moss_rope whose rotated keys, and the values, go straight into the
+ * attention history instead of new tensors.  Replaces the patched rotary
+ * forward (fast_moss/v2_runtime.py:186-224) followed by the streaming
+ * attention's key/value cache update (the upstream state that
+ * fast_moss/streaming.py:14-26 keeps at stable addresses): oq contiguous
+ * [b,h,t,d]; k rotated into k_cache and v copied into v_cache at
+ * [b, h, slots[b*t + t_i], :], both caches contiguous [b, h, cache_slots, d]
+ * of the input dtype.  slots: device int64 [b, t]; a slot outside
+ * [0, cache_slots) is skipped and reported through moss_check_device_error.
+ * q, k, v: [b,h,t,d] with arbitrary element strides (4 int64 each, host).
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_rope_kv(const void* q, const void* k, const void* v, int dtype,
+              const void* offset, int offset_dtype, float freq_coef,
+              const int64_t* slots, void* oq, void* k_cache, void* v_cache,
+              int64_t b, int64_t h, int64_t t, int64_t d, int64_t cache_slots,
+              const int64_t* q_strides, const int64_t* k_strides,
+              const int64_t* v_strides, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Bias + gated activation, bf16 or float32 in and out.

@@ -272,3 +272,74 @@ def torch_gated_nobias(x, act):
     else:
         a = torch.nn.functional.gelu(gate)
     return a * up
+
+
+def _rope_kv_case(cuda_device, dtype, b=3, h=4, t=5, d=64, slots_n=9, seed=31):
+    g = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(b, t, 3, h, d, generator=g).to(cuda_device, dtype)
+    q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # strided [b,h,t,d] views
+    offset = torch.tensor([0, 7, 123456][:b], device=cuda_device, dtype=torch.int64)
+    pos = offset[:, None] + torch.arange(t, device=cuda_device)
+    slots = torch.remainder(pos, slots_n)
+    k_cache = torch.randn(b, h, slots_n, d, generator=g).to(cuda_device, dtype)
+    v_cache = torch.randn(b, h, slots_n, d, generator=g).to(cuda_device, dtype)
+    return q, k, v, offset, slots, k_cache, v_cache
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rope_kv_matches_rope_and_scatter(moss, cuda_device, dtype):
+    q, k, v, offset, slots, kc, vc = _rope_kv_case(cuda_device, dtype)
+    b, h, t, d = q.shape
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    oq_ref, ok_ref = moss.rope(q, k, offset, 10000.0)
+    index = slots[:, None, :, None].expand(b, h, t, d)
+    kc_ref.scatter_(2, index, ok_ref)
+    vc_ref.scatter_(2, index, v)
+    oq = moss.rope_kv(q, k, v, offset, 10000.0, slots, kc, vc)
+    assert torch.equal(oq, oq_ref)
+    assert torch.equal(kc, kc_ref)
+    assert torch.equal(vc, vc_ref)
+
+
+def test_rope_kv_reports_a_slot_out_of_range(moss, cuda_device):
+    from fast_moss_b200 import _lib
+
+    q, k, v, offset, slots, kc, vc = _rope_kv_case(cuda_device, torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(_lib.load().moss_check_device_error(stream), "clear")
+    slots[1, 2] = kc.shape[2]  # one past the ring
+    before_k, before_v = kc.clone(), vc.clone()
+    moss.rope_kv(q, k, v, offset, 10000.0, slots, kc, vc)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.load().moss_check_device_error(stream), "device error word")
+    # the bad token wrote nothing; every other token landed in its slot
+    b, h, t, d = q.shape
+    _, ok_ref = moss.rope(q, k, offset, 10000.0)
+    for bi in range(b):
+        for ti in range(t):
+            sl = int(slots[bi, ti])
+            if sl >= kc.shape[2]:
+                continue
+            assert torch.equal(kc[bi, :, sl], ok_ref[bi, :, ti])
+            assert torch.equal(vc[bi, :, sl], v[bi, :, ti])
+    untouched = [s for s in range(kc.shape[2]) if s not in set(slots[1].tolist())]
+    assert torch.equal(kc[1, :, untouched], before_k[1, :, untouched])
+    assert torch.equal(vc[1, :, untouched], before_v[1, :, untouched])
+
+
+@pytest.mark.parametrize("rows,n", [(4, 1280), (300, 1024), (4096, 1024), (7, 100)])
+def test_layer_norm_bf16_output_is_the_cast(moss, cuda_device, rows, n):
+    g = torch.Generator().manual_seed(rows + n)
+    x = (torch.randn(rows, n, generator=g) * 2 + 1).to(cuda_device)
+    u = torch.randn(rows, n, generator=g).to(cuda_device, torch.bfloat16)
+    ls = (0.02 * torch.randn(n, generator=g)).to(cuda_device)
+    w = torch.randn(n, generator=g).to(cuda_device)
+    bias = torch.randn(n, generator=g).to(cuda_device)
+    r, y = moss.residual_layer_norm(x, u, ls, w, bias, 1e-5, out_dtype=torch.bfloat16)
+    r_ref = x + u.float() * ls
+    y_ref = torch.nn.functional.layer_norm(r_ref, (n,), w, bias, 1e-5).to(torch.bfloat16)
+    assert y.dtype == torch.bfloat16
+    assert torch.equal(r, r_ref)
+    assert torch.equal(y, y_ref)
+    y2 = moss.layer_norm(x, w, bias, 1e-5, out_dtype=torch.bfloat16)
+    assert torch.equal(y2, torch.nn.functional.layer_norm(x, (n,), w, bias, 1e-5).to(torch.bfloat16))
