@@ -587,6 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           tmem_load32(tcol + 32u, vb);
           tmem_wait_ld(va);
           tmem_wait_ld(vb);
+          // The accumulator is in registers: hand it back to the MMA warp
+          // now, so that the tile after next is computed while this one is
+          // screened.
+          tc_fence_before();
+          mbar_arrive(&sm.t_empty[abuf]);
           const float ca = max32(va), cb = max32(vb);
           amax = fmaxf(amax, fmaxf(ca, cb));
           const float athr = amax - window;
@@ -624,9 +629,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
             if (ma) nrec = add_record(sm, slot, chunk, ma, sm.cmax[c][slot], athr, nrec);
             if (mb) nrec = add_record(sm, slot, chunk + 1, mb, sm.cmax[c + 1][slot], athr, nrec);
           }
+          tc_fence_before();
+          mbar_arrive(&sm.t_empty[abuf]);
         }
-        tc_fence_before();
-        mbar_arrive(&sm.t_empty[abuf]);
       }
       sm.amax_h[slot] = amax;
       sm.nrec_h[slot] = nrec;
