@@ -23,7 +23,9 @@ path).  The metric is audio seconds per second: each frame is 80 ms of
   kernels    the other hot-path kernels (residual+LayerNorm, RoPE, SiLU
              gate) at their workload sizes vs the measured HBM copy
              bandwidth, launches captured in a CUDA graph with inputs rotated
-             through > L2-sized sets; and the all-FFMA quantizer kernel.
+             through > L2-sized sets; the all-FFMA quantizer kernel; one
+             real-model LFQ stage as the reference's prepare + GEMM + select
+             sequence and as the fused decode.
   stack      the codec's streaming transformer stack (24 x 1280, 20 heads,
              ffn 5120) on the hot-path kernels under the batched CUDA-graph
              scheduler: 125 chunks of 80 ms per stream at 1 and 64 streams,
@@ -368,6 +370,43 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     out["silu_gate"] = {"shape": [4, 2048, 4096], "us": t * 1e6, "bytes": nbytes,
                         "gbs": nbytes / t / 1e9, "frac": nbytes / t / 1e9 / hbm_peak,
                         "traffic": profile_traffic("gated_act_stream_kernel")}
+    del sets
+
+    # one real-model LFQ quantizer stage: 8192 rows of 8-dim latents against
+    # a 1024-entry normalised codebook.  The reference's sequence (prepare,
+    # FP32 GEMM for the [rows, K] dot matrix, select) on these kernels with
+    # cuBLAS in between, beside the fused decode that never writes the dots.
+    b, t, k = 64, 128, 1024
+    weight = torch.randn(k, 8, device=dev, generator=g)
+    book = torch.nn.functional.normalize(weight)
+    cnorm = book.pow(2).sum(1, keepdim=True).T.contiguous()
+    sets = []
+    for _ in range(4):  # 4 x 32 MiB dot matrices: more than L2
+        sets.append((torch.randn(b, 8, t, device=dev, generator=g),
+                     torch.empty(b * t, k, device=dev)))
+    bt = book.T.contiguous()
+    from fast_moss_b200.quantizer import decode_latents, select
+    from fast_moss_b200.quantizer_prepare import prepare
+
+    def unfused(s, sh):
+        _, row_norm, twice, _ = prepare(s[0])
+        torch.matmul(twice, bt, out=s[1])
+        select(s[1], row_norm, cnorm, weight, s[0])
+
+    def fused(s, sh):
+        decode_latents(s[0], book, cnorm, weight)
+
+    t_unfused = time_launches(torch, unfused, sets)
+    t_fused = time_launches(torch, fused, sets)
+    _, rn, tw, _ = prepare(sets[0][0])
+    same = bool(torch.equal(select(tw @ bt, rn, cnorm, weight, sets[0][0])[1],
+                            decode_latents(sets[0][0], book, cnorm, weight)[1]))
+    out["lfq_stage"] = {
+        "shape": {"rows": b * t, "codes": k, "dim": 8},
+        "us_reference_sequence": t_unfused * 1e6, "us_fused": t_fused * 1e6,
+        "dots_bytes_avoided": 2 * b * t * k * 4, "indices_equal": same,
+        "sequence": "moss_lfq_prepare + cuBLAS FP32 GEMM + moss_lfq_select (the reference's order)",
+        "fused": "moss_lfq_decode (prepare, dots and select in one kernel)"}
     del sets
     torch.cuda.synchronize()
     return out
