@@ -99,13 +99,14 @@ struct Pick {
   int64_t nan_i;
 };
 
+// Branch-free: a NaN distance never compares below best; selects instead of
+// data-dependent branches keep the lanes of a warp converged.
 __device__ __forceinline__ void pick_push(Pick& p, float dist, int64_t j) {
-  if (dist != dist) {
-    if (j < p.nan_i) p.nan_i = j;
-  } else if (dist < p.best) {
-    p.best = dist;
-    p.best_i = j;
-  }
+  const bool is_nan = dist != dist;
+  const bool better = dist < p.best;
+  p.nan_i = (is_nan && j < p.nan_i) ? j : p.nan_i;
+  p.best_i = better ? j : p.best_i;
+  p.best = better ? dist : p.best;
 }
 
 // Warp-wide reduction; every lane returns the selected index.
@@ -184,6 +185,104 @@ __global__ void __launch_bounds__(256) lfq_decode_kernel(
   if (lane < 8) out[row * 8 + lane] = weight[idx * 8 + lane];
 }
 
+// The same decode for many rows: the normalised codebook and its norms are
+// staged in shared memory once per block, each warp takes kDecRows rows,
+// and every codeword read serves all of them.  Per row the arithmetic is
+// lfq_decode_kernel's (prepare_row, the sequential 8-channel dot, the
+// distance rounding and the first-NaN / first-minimum pick), so the results
+// are the same bits.  Rows past the end are computed on the last row and
+// discarded, so that every warp reaches the block barrier.
+constexpr int kDecRows = 8;
+constexpr int kDecMaxCodes = 4096;  // 36 bytes per code of shared memory
+
+struct Pick32 {
+  float best;
+  int best_i;
+  int nan_i;
+};
+
+// pick_push with 32-bit indices.
+__device__ __forceinline__ void pick32_push(Pick32& p, float dist, int j) {
+  const bool is_nan = dist != dist;
+  const bool better = dist < p.best;
+  p.nan_i = (is_nan && j < p.nan_i) ? j : p.nan_i;
+  p.best_i = better ? j : p.best_i;
+  p.best = better ? dist : p.best;
+}
+
+__device__ __forceinline__ int pick32_reduce(Pick32 p) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, p.best, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, p.best_i, m);
+    const int on = __shfl_xor_sync(0xffffffffu, p.nan_i, m);
+    if (ob < p.best || (ob == p.best && oi < p.best_i)) {
+      p.best = ob;
+      p.best_i = oi;
+    }
+    if (on < p.nan_i) p.nan_i = on;
+  }
+  return p.nan_i != INT_MAX ? p.nan_i : p.best_i;
+}
+
+__global__ void __launch_bounds__(128) lfq_decode_tile_kernel(
+    const float* __restrict__ x, const float* __restrict__ book_normed,
+    const float* __restrict__ code_norm, const float* __restrict__ weight, int64_t b, int64_t t,
+    int k, float* __restrict__ out, int64_t* __restrict__ indices) {
+  extern __shared__ float4 dec_smem[];
+  float4* sbook = dec_smem;                                 // [k][2]
+  float* scn = reinterpret_cast<float*>(dec_smem + 2 * k);  // [k]
+  for (int i = threadIdx.x; i < 2 * k; i += blockDim.x)
+    sbook[i] = reinterpret_cast<const float4*>(book_normed)[i];
+  for (int i = threadIdx.x; i < k; i += blockDim.x) scn[i] = code_norm[i];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t rows = b * t;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp) * kDecRows;
+  const bool transposed = (b == 1 && t > 1);
+  // lane r prepares row r of the warp's group (all lanes run one
+  // preparation in parallel), then every lane receives the group's values
+  float tw[kDecRows][8], nrm[kDecRows];
+  {
+    const int64_t mine = row0 + (lane % kDecRows);
+    const Prepared p = prepare_row(x, mine < rows ? mine : rows - 1, t, transposed);
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) {
+#pragma unroll
+      for (int d = 0; d < 8; ++d) tw[r][d] = __shfl_sync(0xffffffffu, p.twice[d], r);
+      nrm[r] = __shfl_sync(0xffffffffu, p.norm, r);
+    }
+  }
+  __syncthreads();
+  Pick32 pk[kDecRows];
+#pragma unroll
+  for (int r = 0; r < kDecRows; ++r) pk[r] = Pick32{CUDART_INF_F, lane, INT_MAX};
+  for (int j = lane; j < k; j += 32) {
+    const float4 c0 = sbook[2 * j], c1 = sbook[2 * j + 1];
+    const float cn = scn[j];
+#pragma unroll
+    for (int r = 0; r < kDecRows; ++r) {
+      float dot = __fmul_rn(tw[r][0], c0.x);
+      dot = __fmaf_rn(tw[r][1], c0.y, dot);
+      dot = __fmaf_rn(tw[r][2], c0.z, dot);
+      dot = __fmaf_rn(tw[r][3], c0.w, dot);
+      dot = __fmaf_rn(tw[r][4], c1.x, dot);
+      dot = __fmaf_rn(tw[r][5], c1.y, dot);
+      dot = __fmaf_rn(tw[r][6], c1.z, dot);
+      dot = __fmaf_rn(tw[r][7], c1.w, dot);
+      pick32_push(pk[r], __fadd_rn(__fsub_rn(nrm[r], dot), cn), j);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kDecRows; ++r) {
+    const int idx = pick32_reduce(pk[r]);
+    const int64_t row = row0 + r;
+    if (row < rows) {
+      if (lane == 0) indices[row] = idx;
+      if (lane < 8) out[row * 8 + lane] = weight[static_cast<int64_t>(idx) * 8 + lane];
+    }
+  }
+}
+
 }  // namespace moss
 
 using namespace moss;
@@ -233,6 +332,16 @@ extern "C" int moss_lfq_decode(const float* x, const float* book_normed, const f
     return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
   if (!aligned16(book_normed)) return fail(MOSS_ERR_VALUE, "%s: normalised book must be 16-byte aligned", name);
   const int64_t rows = b * t;
+  if (rows >= 256 && k <= kDecMaxCodes && rows / (4 * kDecRows) < 0x7fffffffLL) {
+    // many rows: the codebook staged once per block of 4 warps x kDecRows rows
+    const size_t smem = static_cast<size_t>(k) * 36;
+    static bool configured[kMaxDevices] = {};
+    allow_dynamic_smem(lfq_decode_tile_kernel, kDecMaxCodes * 36, configured);
+    lfq_decode_tile_kernel<<<static_cast<unsigned>((rows + 4 * kDecRows - 1) / (4 * kDecRows)), 128,
+                             smem, as_stream(stream)>>>(x, book_normed, code_norm, weight, b, t,
+                                                        static_cast<int>(k), out, indices);
+    return launch_status(name);
+  }
   lfq_decode_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, as_stream(stream)>>>(
       x, book_normed, code_norm, weight, b, t, k, out, indices);
   return launch_status(name);

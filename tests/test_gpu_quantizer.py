@@ -218,3 +218,22 @@ def test_rvq_host_batches_pipeline(moss, cuda_device, depth):
         q.encode_host_batches(xs[:2], codes[:1], recon[:2])
     with pytest.raises(ValueError):
         q.encode_host_batches([xs[0].to(cuda_device)], codes[:1], recon[:1])
+
+
+@pytest.mark.parametrize("b,t,k", [(1, 1000, 1024), (3, 111, 1000), (64, 128, 4096), (2, 200, 37)])
+def test_lfq_decode_many_rows_staged_codebook(moss, cuda_device, b, t, k):
+    """Hundreds of rows take the kernel that stages the codebook in shared
+    memory; both summation orders (b == 1 with t > 1 is the transposed one),
+    codebooks that are not a multiple of 32, NaN and all-zero latent rows."""
+    rng = np.random.default_rng(b * 1000 + t + k)
+    weight = rng.standard_normal((k, 8)).astype(np.float32)
+    book = (weight / np.linalg.norm(weight, axis=1, keepdims=True)).astype(np.float32)
+    cnorm = (book * book).sum(1).astype(np.float32)
+    x = rng.standard_normal((b, 8, t)).astype(np.float32)
+    x[0, 3, 5] = np.nan
+    x[-1, :, t - 1] = 0.0
+    values, idx = moss.decode_latents(dev(x, cuda_device), dev(book, cuda_device),
+                                      dev(cnorm, cuda_device), dev(weight, cuda_device))
+    ov, oi = O.lfq_decode(x, book, cnorm, weight)
+    assert np.array_equal(idx.cpu().numpy().reshape(-1), oi)
+    assert same_bits(values.transpose(1, 2).contiguous().cpu().numpy().reshape(-1, 8), ov)
