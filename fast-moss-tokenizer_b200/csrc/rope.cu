@@ -9,17 +9,20 @@
 // given: freq[j] = expf(j * coef), ts = float(offset[b]) + t,
 // phase = freq[j] * ts, c = cosf(phase), s = sinf(phase).
 //
-// Work decomposition: a tile is one batch index and TT time steps for ALL
-// heads, so the phase table of a tile (TT x d/2 (c, s) pairs, evaluated once
-// into shared memory -- the phase does not depend on the head) serves every
-// head.  Three kernels share that decomposition:
+// Work decomposition: the phase does not depend on the head, so each
+// kernel evaluates a time step's d/2 (c, s) pairs once into shared memory
+// and rotates every head's row of that step with them.
 //   * rope_stream_kernel, for q and k whose time rows are contiguous within
-//     each head: bulk copies stage whole tiles in shared memory (one CTA
-//     per SM, producer thread + consumer warps);
+//     each head: one CTA per SM takes an even share of the b*t rows (in
+//     chunks whose phase table it evaluates once); a tile is a group of
+//     heads over a chunk, staged by one bulk copy per head, tensor and
+//     batch run (a producer warp), rotated by 16 consumer warps that write
+//     16-byte vectors straight to global memory;
 //   * rope_vec_kernel, for other layouts with 16-byte rows (innermost
-//     stride 1, e.g. a qkv projection output viewed as [b,h,t,d]):
-//     persistent blocks that issue the next tile's loads and phase table
-//     before rotating the current one;
+//     stride 1, e.g. a qkv projection output viewed as [b,h,t,d]): a tile
+//     is one batch index and TT time steps for all heads; persistent blocks
+//     issue the next tile's loads and phase table before rotating the
+//     current one;
 //   * rope_pair_kernel, one interleaved pair per item, for any strides.
 #include "pipeline.cuh"
 
@@ -361,33 +364,33 @@ namespace rstream {
 constexpr int kConsumers = MOSS_ROPE_CONSUMERS;
 constexpr int kThreads = kConsumers + 32;
 #ifndef MOSS_ROPE_STAGES
-#define MOSS_ROPE_STAGES 3
+#define MOSS_ROPE_STAGES 6
 #endif
 #ifndef MOSS_ROPE_STAGE_BYTES
-#define MOSS_ROPE_STAGE_BYTES 49152
+#define MOSS_ROPE_STAGE_BYTES 32768
 #endif
 constexpr int kStages = MOSS_ROPE_STAGES;
 constexpr int kStageBytes = MOSS_ROPE_STAGE_BYTES;
-#ifndef MOSS_ROPE_MAX_PAIRS
-#define MOSS_ROPE_MAX_PAIRS 2048
-#endif
-constexpr int kMaxPairs = MOSS_ROPE_MAX_PAIRS;  // (c, s) pairs per tile table
+// Most (c, s) pairs of a chunk's phase table: a CTA's rows are walked in
+// chunks whose table is evaluated once, behind one barrier, for all heads.
+constexpr int kWindowPairs = 4096;
 // Items (16 bytes of q and 16 of k) per consumer thread and tile.
 constexpr int kSlots = (kStageBytes / 32 + kConsumers - 1) / kConsumers;
 
 struct Args {
   RopeArgs r;
-  uint32_t ntiles;
-  FastDiv tiles_per_b;  // time tiles per batch index
-  FastDiv nvec;         // 16-byte items per row (d / VW)
-  FastDiv tt;           // time steps per tile
-  FastDiv half;         // d / 2
-  uint32_t fpad;        // floats reserved for freq (d/2 rounded up to 4)
+  uint32_t rows;            // b * t flattened (batch-major) time rows
+  FastDiv t;                // time steps per batch index
+  FastDiv nvec;             // 16-byte items per row (d / VW)
+  FastDiv crow;             // rows per chunk (a tile's rows; the phase window)
+  uint32_t heads_per_tile;  // heads of a tile
+  FastDiv half;             // d / 2
+  uint32_t fpad;            // floats reserved for freq (d/2 rounded up to 4)
 };
 
-inline size_t smem_bytes(int tt, int half, bool tables) {
+inline size_t smem_bytes(int chunk_rows, int half, bool tables) {
   size_t b = static_cast<size_t>(kStages) * kStageBytes;
-  if (!tables) b += sizeof(float) * (((half + 3) & ~3) + 4 * static_cast<size_t>(tt) * half);
+  if (!tables) b += sizeof(float) * (((half + 3) & ~3) + 2 * static_cast<size_t>(chunk_rows) * half);
   return b + (2 * kStages + 2) * 8;
 }
 }  // namespace rstream
@@ -400,17 +403,25 @@ __global__ void __launch_bounds__(rstream::kThreads, 1) rope_stream_kernel(const
   const RopeArgs& a = sa.r;
   extern __shared__ __align__(128) unsigned char sbuf[];
   const int half = static_cast<int>(sa.half.d);
-  const int tt_full = static_cast<int>(sa.tt.d);
-  const int tbl = tt_full * half;
+  const uint32_t R = sa.crow.d;             // rows per chunk
+  const uint32_t G = sa.heads_per_tile;     // heads per tile
+  const uint32_t H = static_cast<uint32_t>(a.h);
+  const uint32_t T = sa.t.d;
+  const uint32_t win_pairs = R * sa.half.d;
   float* freq = reinterpret_cast<float*>(sbuf + kStages * kStageBytes);
-  float* tabs = freq + sa.fpad;
+  float* tab_c = freq + sa.fpad;  // [R][half] cosines of the chunk's rows, then sines
+  float* tab_s = tab_c + win_pairs;
   unsigned long long* full = reinterpret_cast<unsigned long long*>(
-      sbuf + kStages * kStageBytes + (TABLES ? 0 : sizeof(float) * (sa.fpad + 4 * tbl)));
+      sbuf + kStages * kStageBytes + (TABLES ? 0 : sizeof(float) * (sa.fpad + 2 * win_pairs)));
   unsigned long long* empty = full + kStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + 2 * kStages);
   const int tid = threadIdx.x;
-  const uint32_t head_bytes = static_cast<uint32_t>(tt_full * a.d * kEs);  // per head in a stage
-  const uint32_t k_off = static_cast<uint32_t>(a.h) * head_bytes;
+  const uint32_t row_bytes = static_cast<uint32_t>(a.d * kEs);
+  const uint32_t slab = R * row_bytes;  // one head's chunk rows in a stage
+  const uint32_t k_off = G * slab;      // k slabs follow the q slabs
+  // This CTA's rows: an even share of the b * t rows, in order.
+  const uint32_t lo = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * sa.rows / gridDim.x);
+  const uint32_t hi = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * sa.rows / gridDim.x);
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       pipe::mbar_init(&full[s], 1);
@@ -424,140 +435,171 @@ __global__ void __launch_bounds__(rstream::kThreads, 1) rope_stream_kernel(const
   }
   __syncthreads();
 
-  if (tid >= kConsumers) {  // producer warp: one thread issues every copy
-    if (tid != kConsumers) return;
+  // Tiles, in the same order on both sides: for each chunk of R rows, the
+  // heads in groups of G; a tile is q and k of its heads over the chunk.
+  if (tid >= kConsumers) {  // producer warp: lane j copies heads j, j+32, ... of a tile
+    const int pl = tid - kConsumers;
     uint32_t i = 0;
-    for (uint32_t tile = blockIdx.x; tile < sa.ntiles; tile += gridDim.x, ++i) {
-      const int s = static_cast<int>(i % kStages);
-      if (i >= kStages && !pipe::mbar_wait(&empty[s], ((i / kStages) - 1) & 1)) {
-        *abort_flag = 1;
-        break;
-      }
-      if (*abort_flag) break;
-      const uint32_t bi = fast_div(tile, sa.tiles_per_b);
-      const int64_t t0 = static_cast<int64_t>(tile - bi * sa.tiles_per_b.d) * tt_full;
-      const int ttc = static_cast<int>(a.t - t0 < tt_full ? a.t - t0 : tt_full);
-      const uint32_t run = static_cast<uint32_t>(ttc * a.d * kEs);
-      pipe::mbar_arrive_expect_tx(&full[s], 2u * static_cast<uint32_t>(a.h) * run);
-      unsigned char* st = sbuf + s * kStageBytes;
-      const char* q = static_cast<const char*>(a.q) + (bi * a.qs[0] + t0 * a.qs[2]) * kEs;
-      const char* k = static_cast<const char*>(a.k) + (bi * a.ks[0] + t0 * a.ks[2]) * kEs;
-      for (int64_t hi = 0; hi < a.h; ++hi) {
-        pipe::bulk_g2s(st + hi * head_bytes, q + hi * a.qs[1] * kEs, run, &full[s]);
-        pipe::bulk_g2s(st + k_off + hi * head_bytes, k + hi * a.ks[1] * kEs, run, &full[s]);
+    bool stop = false;
+    for (uint32_t c0 = lo; c0 < hi && !stop; c0 += R) {
+      const uint32_t nr = hi - c0 < R ? hi - c0 : R;
+      for (uint32_t h0 = 0; h0 < H; h0 += G, ++i) {
+        const uint32_t ng = H - h0 < G ? H - h0 : G;
+        const int s = static_cast<int>(i % kStages);
+        int go = 1;
+        if (pl == 0) {
+          if (i >= kStages && !pipe::mbar_wait(&empty[s], ((i / kStages) - 1) & 1)) *abort_flag = 1;
+          go = !*abort_flag;
+        }
+        if (!__shfl_sync(0xffffffffu, go, 0)) {
+          stop = true;
+          break;
+        }
+        if (pl == 0) pipe::mbar_arrive_expect_tx(&full[s], 2u * ng * nr * row_bytes);
+        __syncwarp();
+        unsigned char* st = sbuf + s * kStageBytes;
+        for (uint32_t g = pl; g < ng; g += 32) {
+          const int64_t hh = h0 + g;
+          for (uint32_t r0 = 0; r0 < nr;) {  // runs of rows, cut at batch boundaries
+            const uint32_t row = c0 + r0;
+            const uint32_t bi = fast_div(row, sa.t);
+            const uint32_t t0 = row - bi * T;
+            const uint32_t n = T - t0 < nr - r0 ? T - t0 : nr - r0;
+            const char* q = static_cast<const char*>(a.q) + (bi * a.qs[0] + hh * a.qs[1] + t0 * a.qs[2]) * kEs;
+            const char* k = static_cast<const char*>(a.k) + (bi * a.ks[0] + hh * a.ks[1] + t0 * a.ks[2]) * kEs;
+            pipe::bulk_g2s(st + g * slab + r0 * row_bytes, q, n * row_bytes, &full[s]);
+            pipe::bulk_g2s(st + k_off + g * slab + r0 * row_bytes, k, n * row_bytes, &full[s]);
+            r0 += n;
+          }
+        }
       }
     }
     // Drain: the copies of the last issued tiles must land before exit.
-    for (uint32_t j = i > kStages ? i - kStages : 0; j < i; ++j)
-      pipe::mbar_wait(&full[j % kStages], (j / kStages) & 1);
+    if (pl == 0) {
+      for (uint32_t j = i > kStages ? i - kStages : 0; j < i; ++j)
+        pipe::mbar_wait(&full[j % kStages], (j / kStages) & 1);
+    }
+    __syncwarp();
     return;
   }
 
   // Consumer warps.  Every consumer runs the same tiles and barriers; after
   // a timeout (anywhere) the remaining tiles are skipped.  A thread's items
-  // sit at the same place in every tile, so their offsets are computed once.
+  // (head g of the tile, row r of the chunk, 16-byte vector) sit at the same
+  // place in every tile.
   const int lane = tid & 31;
-  const uint32_t items_full = static_cast<uint32_t>(a.h) * tt_full * sa.nvec.d;
+  const uint32_t items_full = G * R * sa.nvec.d;
   uint32_t so[kSlots];   // byte offset of the q item in a stage
-  int tlv[kSlots];       // time step within the tile (large: no item)
-  int toff[kSlots];      // first (c, s) pair of the item in the tile table
-  int64_t orel[kSlots];  // output element offset from the tile's base
+  uint32_t rv[kSlots];   // row within the chunk
+  uint32_t gv[kSlots];   // head within the tile (large: no item)
+  uint32_t vo[kSlots];   // element offset of the vector within the row
 #pragma unroll
   for (int m = 0; m < kSlots; ++m) {
     const uint32_t it = tid + m * kConsumers;
-    so[m] = 0;
-    toff[m] = 0;
-    orel[m] = 0;
-    tlv[m] = 0x3fffffff;
-    if (it < items_full) {
-      const uint32_t rest = fast_div(it, sa.nvec);
-      const uint32_t vec = it - rest * sa.nvec.d;
-      const uint32_t hi = fast_div(rest, sa.tt);
-      const int tl = static_cast<int>(rest - hi * sa.tt.d);
-      so[m] = hi * head_bytes + static_cast<uint32_t>((tl * a.d + vec * VW) * kEs);
-      tlv[m] = tl;
-      toff[m] = tl * half + static_cast<int>(vec) * (VW / 2);
-      orel[m] = (static_cast<int64_t>(hi) * a.t + tl) * a.d + vec * VW;
-    }
+    const uint32_t rest = fast_div(it, sa.nvec);
+    const uint32_t vec = it - rest * sa.nvec.d;
+    const uint32_t g = fast_div(rest, sa.crow);
+    rv[m] = rest - g * R;
+    gv[m] = it < items_full ? g : 0x7fffffffu;
+    vo[m] = vec * VW;
+    so[m] = g * slab + rv[m] * row_bytes + vec * VW * kEs;
   }
   bool alive = true;
   uint32_t i = 0;
-  for (uint32_t tile = blockIdx.x; tile < sa.ntiles; tile += gridDim.x, ++i) {
-    const int s = static_cast<int>(i % kStages);
-    const uint32_t bi = fast_div(tile, sa.tiles_per_b);
-    const int64_t t0 = static_cast<int64_t>(tile - bi * sa.tiles_per_b.d) * tt_full;
-    const int ttc = static_cast<int>(a.t - t0 < tt_full ? a.t - t0 : tt_full);
-    float* sc = tabs + (i & 1) * 2 * tbl;
-    float* ss = sc + tbl;
+  for (uint32_t c0 = lo; c0 < hi; c0 += R) {
+    const uint32_t nr = hi - c0 < R ? hi - c0 : R;
     if (alive && *abort_flag) alive = false;
-    if constexpr (!TABLES) {
+    if constexpr (!TABLES) {  // the chunk's (c, s) pairs; the same decision in every consumer
+      if (c0 != lo) pipe::consumer_sync(kConsumers);  // all reads of the previous chunk done
       if (alive) {
-        const float off = offset_as_float(a.offset, a.offset_dtype, bi);
-        for (int e = tid; e < ttc * half; e += kConsumers) {
-          const int tl = static_cast<int>(fast_div(static_cast<uint32_t>(e), sa.half));
-          const int j = e - tl * half;
-          const float ts = __fadd_rn(off, static_cast<float>(t0 + tl));
+        const uint32_t n = nr * sa.half.d;
+        for (uint32_t e = tid; e < n; e += kConsumers) {
+          const uint32_t r = fast_div(e, sa.half);
+          const uint32_t j = e - r * sa.half.d;
+          const uint32_t row = c0 + r;
+          const uint32_t bi = fast_div(row, sa.t);
+          const float off = offset_as_float(a.offset, a.offset_dtype, bi);
+          const float ts = __fadd_rn(off, static_cast<float>(row - bi * T));
           const float phase = __fmul_rn(freq[j], ts);
-          sc[e] = cosf(phase);
-          ss[e] = sinf(phase);
+          tab_c[e] = cosf(phase);
+          tab_s[e] = sinf(phase);
         }
       }
       pipe::consumer_sync(kConsumers);
     }
-    if (alive && !pipe::mbar_wait(&full[s], (i / kStages) & 1)) {
-      alive = false;
-      *abort_flag = 1;
+    // Output element offset of each item without its head term, and its
+    // first (c, s) pair (in the window, or in the given tables).
+    int64_t ob[kSlots];
+    int64_t tb[kSlots];
+#pragma unroll
+    for (int m = 0; m < kSlots; ++m) {
+      const uint32_t row = c0 + rv[m];
+      const uint32_t bi = fast_div(row, sa.t);
+      ob[m] = (static_cast<int64_t>(bi) * H * T + (row - bi * T)) * a.d + vo[m];
+      tb[m] = TABLES ? static_cast<int64_t>(row) * half + vo[m] / 2
+                     : static_cast<int64_t>(rv[m]) * half + vo[m] / 2;
     }
-    if (alive) {
-      const unsigned char* st = sbuf + s * kStageBytes;
-      const int64_t ob = (static_cast<int64_t>(bi) * a.h * a.t + t0) * a.d;
-      const int64_t tb = (static_cast<int64_t>(bi) * a.t + t0) * half;
+    for (uint32_t h0 = 0; h0 < H; h0 += G, ++i) {
+      const uint32_t ng = H - h0 < G ? H - h0 : G;
+      const int s = static_cast<int>(i % kStages);
+      if (alive && *abort_flag) alive = false;
+      if (alive && !pipe::mbar_wait(&full[s], (i / kStages) & 1)) {
+        alive = false;
+        *abort_flag = 1;
+      }
+      if (alive) {
+        const unsigned char* st = sbuf + s * kStageBytes;
 #pragma unroll
-      for (int m = 0; m < kSlots; ++m) {
-        if (tlv[m] >= ttc) continue;
-        const uint4 qraw = *reinterpret_cast<const uint4*>(st + so[m]);
-        const uint4 kraw = *reinterpret_cast<const uint4*>(st + k_off + so[m]);
-        float c[VW / 2], sn[VW / 2];
-        if constexpr (TABLES) {
+        for (int m = 0; m < kSlots; ++m) {
+          if (gv[m] >= ng || rv[m] >= nr) continue;
+          const uint4 qraw = *reinterpret_cast<const uint4*>(st + so[m]);
+          const uint4 kraw = *reinterpret_cast<const uint4*>(st + k_off + so[m]);
+          float c[VW / 2], sn[VW / 2];
+          if constexpr (TABLES) {
+#pragma unroll
+            for (int p = 0; p < VW / 2; ++p) {
+              c[p] = a.cos_t[tb[m] + p];
+              sn[p] = a.sin_t[tb[m] + p];
+            }
+          } else if constexpr (VW == 8) {  // 16-byte aligned: half is a multiple of 4
+            const float4 cv = *reinterpret_cast<const float4*>(tab_c + tb[m]);
+            const float4 sv = *reinterpret_cast<const float4*>(tab_s + tb[m]);
+            c[0] = cv.x; c[1] = cv.y; c[2] = cv.z; c[3] = cv.w;
+            sn[0] = sv.x; sn[1] = sv.y; sn[2] = sv.z; sn[3] = sv.w;
+          } else {  // 8-byte aligned: half is even
+            const float2 cv = *reinterpret_cast<const float2*>(tab_c + tb[m]);
+            const float2 sv = *reinterpret_cast<const float2*>(tab_s + tb[m]);
+            c[0] = cv.x; c[1] = cv.y;
+            sn[0] = sv.x; sn[1] = sv.y;
+          }
+          float qv[VW], kv[VW], qo[VW], ko[VW];
+          if constexpr (DT == MOSS_BF16) {
+            unpack_bf16x8(qraw, qv);
+            unpack_bf16x8(kraw, kv);
+          } else {
+            qv[0] = __uint_as_float(qraw.x); qv[1] = __uint_as_float(qraw.y);
+            qv[2] = __uint_as_float(qraw.z); qv[3] = __uint_as_float(qraw.w);
+            kv[0] = __uint_as_float(kraw.x); kv[1] = __uint_as_float(kraw.y);
+            kv[2] = __uint_as_float(kraw.z); kv[3] = __uint_as_float(kraw.w);
+          }
 #pragma unroll
           for (int p = 0; p < VW / 2; ++p) {
-            c[p] = a.cos_t[tb + toff[m] + p];
-            sn[p] = a.sin_t[tb + toff[m] + p];
+            rotate_pair(qv[2 * p], qv[2 * p + 1], c[p], sn[p], qo[2 * p], qo[2 * p + 1]);
+            rotate_pair(kv[2 * p], kv[2 * p + 1], c[p], sn[p], ko[2 * p], ko[2 * p + 1]);
           }
-        } else {
-#pragma unroll
-          for (int p = 0; p < VW / 2; ++p) {
-            c[p] = sc[toff[m] + p];
-            sn[p] = ss[toff[m] + p];
+          const int64_t o = ob[m] + static_cast<int64_t>(h0 + gv[m]) * T * a.d;
+          if constexpr (DT == MOSS_BF16) {
+            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.oq) + o) = pack_bf16x8(qo);
+            *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.ok) + o) = pack_bf16x8(ko);
+          } else {
+            *reinterpret_cast<float4*>(static_cast<float*>(a.oq) + o) = make_float4(qo[0], qo[1], qo[2], qo[3]);
+            *reinterpret_cast<float4*>(static_cast<float*>(a.ok) + o) = make_float4(ko[0], ko[1], ko[2], ko[3]);
           }
-        }
-        float qv[VW], kv[VW], qo[VW], ko[VW];
-        if constexpr (DT == MOSS_BF16) {
-          unpack_bf16x8(qraw, qv);
-          unpack_bf16x8(kraw, kv);
-        } else {
-          qv[0] = __uint_as_float(qraw.x); qv[1] = __uint_as_float(qraw.y);
-          qv[2] = __uint_as_float(qraw.z); qv[3] = __uint_as_float(qraw.w);
-          kv[0] = __uint_as_float(kraw.x); kv[1] = __uint_as_float(kraw.y);
-          kv[2] = __uint_as_float(kraw.z); kv[3] = __uint_as_float(kraw.w);
-        }
-#pragma unroll
-        for (int p = 0; p < VW / 2; ++p) {
-          rotate_pair(qv[2 * p], qv[2 * p + 1], c[p], sn[p], qo[2 * p], qo[2 * p + 1]);
-          rotate_pair(kv[2 * p], kv[2 * p + 1], c[p], sn[p], ko[2 * p], ko[2 * p + 1]);
-        }
-        const int64_t o = ob + orel[m];
-        if constexpr (DT == MOSS_BF16) {
-          *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.oq) + o) = pack_bf16x8(qo);
-          *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.ok) + o) = pack_bf16x8(ko);
-        } else {
-          *reinterpret_cast<float4*>(static_cast<float*>(a.oq) + o) = make_float4(qo[0], qo[1], qo[2], qo[3]);
-          *reinterpret_cast<float4*>(static_cast<float*>(a.ok) + o) = make_float4(ko[0], ko[1], ko[2], ko[3]);
         }
       }
+      __syncwarp();
+      if (lane == 0 && alive) pipe::mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0 && alive) pipe::mbar_arrive(&empty[s]);
   }
 }
 
@@ -567,32 +609,44 @@ static bool rope_stream(RopeArgs a, int dtype, bool tables, cudaStream_t s) {
   const int esize = dtype == MOSS_F32 ? 4 : 2;
   const int half = static_cast<int>(a.d / 2);
   if (a.qs[2] != a.d || a.ks[2] != a.d) return false;
-  const int64_t per_t = 2 * a.h * a.d * esize;  // stage bytes per time step
-  int64_t tt = kStageBytes / per_t;
-  if (!tables && tt * half > kMaxPairs) tt = kMaxPairs / half;
-  if (tt > a.t) tt = a.t;
-  if (tt < 1) return false;
-  const int64_t tiles_per_b = (a.t + tt - 1) / tt;
-  const int64_t ntiles = a.b * tiles_per_b;
-  if (ntiles > 0x7fffffffLL || a.h * tt * (a.d / (16 / esize)) > 0x7fffffffLL) return false;
+  const int64_t row_head = 2 * a.d * esize;  // q and k bytes of one head and row
+  const int64_t rows = a.b * a.t;
+  if (row_head > kStageBytes || rows > 0x7fffffffLL || a.h > 0x7fffffffLL) return false;
+  // An even share of the rows per CTA, at least one stage of work each.
+  int64_t grid = (rows * a.h * row_head + kStageBytes - 1) / kStageBytes;
+  if (grid > sm_count()) grid = sm_count();
+  if (grid > rows) grid = rows;
+  const int64_t share = (rows + grid - 1) / grid;  // most rows of one CTA
+  // Chunk rows R: the share in the fewest chunks with R * row_head within a
+  // stage and R * d/2 within the phase window (fewer chunks = fewer, longer
+  // bulk copies: one per head, tensor and batch run of a chunk).  Heads per
+  // tile G: as many as fit a stage with R rows, in even groups.
+  int64_t rmax = kStageBytes / row_head;
+  if (rmax > kWindowPairs / half) rmax = kWindowPairs / half;
+  const int64_t chunks = (share + rmax - 1) / rmax;
+  const int64_t chunk_rows = (share + chunks - 1) / chunks;
+  int64_t head_group = kStageBytes / (chunk_rows * row_head);
+  if (head_group > a.h) head_group = a.h;
+  const int64_t groups = (a.h + head_group - 1) / head_group;
+  head_group = (a.h + groups - 1) / groups;
   Args sa{};
-  a.tt = static_cast<int>(tt);
   sa.r = a;
-  sa.ntiles = static_cast<uint32_t>(ntiles);
-  sa.tiles_per_b = make_fastdiv(static_cast<uint32_t>(tiles_per_b));
+  sa.rows = static_cast<uint32_t>(rows);
+  sa.t = make_fastdiv(static_cast<uint32_t>(a.t));
   sa.nvec = make_fastdiv(static_cast<uint32_t>(a.d / (16 / esize)));
-  sa.tt = make_fastdiv(static_cast<uint32_t>(tt));
+  sa.crow = make_fastdiv(static_cast<uint32_t>(chunk_rows));
+  sa.heads_per_tile = static_cast<uint32_t>(head_group);
   sa.half = make_fastdiv(static_cast<uint32_t>(half));
   sa.fpad = static_cast<uint32_t>((half + 3) & ~3);
-  const size_t shmem = smem_bytes(static_cast<int>(tt), half, tables);
-  const uint32_t grid = sa.ntiles < static_cast<uint32_t>(sm_count()) ? sa.ntiles
-                                                                      : static_cast<uint32_t>(sm_count());
-  const size_t smax = smem_bytes(kMaxPairs, 1, false) + 1024 * sizeof(float);
+  const size_t shmem = smem_bytes(static_cast<int>(chunk_rows), half, tables);
+  // largest request: d = 1024 (512 freq floats) and a full window
+  const size_t smax = static_cast<size_t>(kStages) * kStageBytes +
+                      sizeof(float) * (512 + 2 * static_cast<size_t>(kWindowPairs)) + (2 * kStages + 2) * 8;
 #define MOSS_ROPE_S(DT, TB)                                                    \
   do {                                                                         \
     static bool attr_done[kMaxDevices] = {};                                   \
     allow_dynamic_smem(rope_stream_kernel<DT, TB>, smax, attr_done);           \
-    rope_stream_kernel<DT, TB><<<grid, kThreads, shmem, s>>>(sa);              \
+    rope_stream_kernel<DT, TB><<<static_cast<unsigned>(grid), kThreads, shmem, s>>>(sa); \
   } while (0)
   if (dtype == MOSS_BF16) {
     if (tables) MOSS_ROPE_S(MOSS_BF16, true);

@@ -250,6 +250,35 @@ def test_rope_streaming_and_register_paths_agree(moss, cuda_device, dtype, shape
     assert same_bits(rk[:, sl].float().cpu().numpy(), ok)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(4, 16, 2048, 64), (1, 1, 4000, 1024), (3, 1, 1500, 1024),
+                                   (5, 2, 33, 256)])
+def test_rope_streaming_row_shares(moss, cuda_device, dtype, shape):
+    """The streaming kernel gives each CTA an even share of the b * t rows:
+    shares that cross batch boundaries (a different offset on each side),
+    shares longer than one phase-table window (head dim 1024: 16 rows per
+    window), and the benchmark shape.  In-kernel phase and given
+    tables must both give the bits of the reference's tables."""
+    b, h, t, d = shape
+    g = torch.Generator().manual_seed(17)
+    q = torch.randn(b, h, t, d, generator=g).to(cuda_device, dtype)
+    k = torch.randn(b, h, t, d, generator=g).to(cuda_device, dtype)
+    offset = torch.arange(b, device=cuda_device) * 977 + 11
+    bits = torch.int16 if dtype == torch.bfloat16 else torch.int32
+    cos, sin = reference_tables(offset, t, d, 10000.0, cuda_device)
+    fq, fk = moss.rope(q, k, offset, 10000.0)
+    rq, rk = moss.rotate(q, k, cos, sin)
+    assert torch.equal(fq.view(bits), rq.view(bits)) and torch.equal(fk.view(bits), rk.view(bits))
+    # the same rotation in torch, with the reference's op order
+    qf, kf = q.float(), k.float()
+    c, s = cos[:, None], sin[:, None]
+    for src, got in ((qf, rq), (kf, rk)):
+        want = torch.empty_like(src)
+        want[..., 0::2] = src[..., 0::2] * c - src[..., 1::2] * s
+        want[..., 1::2] = src[..., 0::2] * s + src[..., 1::2] * c
+        assert torch.equal(got.view(bits), want.to(dtype).view(bits))
+
+
 @pytest.mark.parametrize("act", ["silu", "gelu"])
 def test_gate_rows_wider_than_a_stage(moss, cuda_device, act):
     """Rows of 40,000 bytes exceed one shared-memory stage and take the
