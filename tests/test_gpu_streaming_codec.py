@@ -288,3 +288,26 @@ def test_encode_fixed_and_codec(moss, model, cuda_device):
         with model.streaming(batch_size=1):
             with pytest.raises(RuntimeError):
                 encode_fixed(model, audio[:1])
+
+
+def test_command_line_reconstructs_a_wav(moss, model, cuda_device, tmp_path, monkeypatch):
+    """`python -m fast_moss_b200 in.wav out.wav` (fast_moss/__main__.py:13-36)
+    on the stand-in model: the FP32 output file holds the bits of the
+    streaming codec's reconstruction of the file's samples."""
+    import numpy as np
+
+    from fast_moss_b200 import __main__ as cli
+    from fast_moss_b200 import wav
+    from fast_moss_b200.streaming import StreamingCodec
+    from fast_moss_b200.v2_runtime import optimized
+
+    monkeypatch.setattr(cli, "load_model", lambda: model)
+    audio = _audio(cuda_device, 2 * FRAME + 777, seed=5)
+    src, dst = tmp_path / "in.wav", tmp_path / "out.wav"
+    wav.write_wav(src, audio[0].T.cpu().numpy(), 48000)
+    cli.main([str(src), str(dst)])
+    got, rate = wav.read_wav(dst)
+    assert rate == 48000 and got.shape == (audio.shape[-1], 2)
+    with torch.inference_mode(), optimized(model), StreamingCodec(model) as sc:
+        want = sc(audio)[2][0].float().cpu().T.numpy()
+    assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(want).view(np.uint32))
