@@ -23,7 +23,9 @@ path).  The metric is audio seconds per second: each frame is 80 ms of
   kernels    the other hot-path kernels (residual+LayerNorm, RoPE, SiLU
              gate) at their workload sizes vs the measured HBM copy
              bandwidth, launches captured in a CUDA graph with inputs rotated
-             through > L2-sized sets; the all-FFMA quantizer kernel; one
+             through > L2-sized sets; the all-FFMA quantizer kernel; the
+             reference's per-stage quantizer sequence (GEMM + select +
+             update, 32 stages in one graph) on the same GPU; one
              real-model LFQ stage as the reference's prepare + GEMM + select
              sequence and as the fused decode.
   stack      the codec's streaming transformer stack (24 x 1280, 20 heads,
@@ -412,6 +414,55 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     return out
 
 
+def rvq_sequence_line(torch, x, books, codes_fused, fused_s):
+    """The reference's per-stage RVQ algorithm on the same GPU: per stage 2r,
+    the row norm, the FP32 dot-product GEMM with TF32 off (cuBLAS; the
+    reference's `dots = (2e) @ book.T`, fast_moss/v2_runtime.py:179), the
+    selection kernel with the reference's distance, first-NaN and first-min
+    rules (fast_moss/quantizer.py:8-49; `moss_lfq_select`), then r -= c and
+    recon += c.  All 32 stages are captured in one CUDA graph and timed like
+    the kernel lines.  The GEMM's summation order is cuBLAS's, so codes may
+    differ from the pinned-order kernels on near ties; the fraction that
+    agrees is reported."""
+    from fast_moss_b200.quantizer import select
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        stages, k, _ = books.shape
+        bt = books.transpose(1, 2).contiguous()
+        cnorm = books.pow(2).sum(-1).unsqueeze(1).contiguous()
+        r = torch.empty_like(x)
+        recon = torch.empty_like(x)
+        twice = torch.empty_like(x)
+        norm = torch.empty(x.shape[0], 1, device=x.device)
+        dots = torch.empty(x.shape[0], k, device=x.device)
+        codes = torch.empty(stages, x.shape[0], dtype=torch.long, device=x.device)
+
+        def run(_set, _handle):
+            r.copy_(x)
+            recon.zero_()
+            for s in range(stages):
+                torch.mul(r, 2.0, out=twice)
+                torch.sum(r * r, dim=1, keepdim=True, out=norm)
+                torch.mm(twice, bt[s], out=dots)
+                values, idx = select(dots, norm, cnorm[s], books[s], r.t().unsqueeze(0))
+                picked = values.transpose(1, 2)[0]
+                r.sub_(picked)
+                recon.add_(picked)
+                codes[s].copy_(idx[0])
+
+        t = time_launches(torch, run, [None], launches=4, replays=3)
+        agree = float((codes == codes_fused.long()).float().mean())
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return {"ms": t * 1e3, "fused_ms": fused_s * 1e3, "fused_speedup": t / fused_s,
+            "codes_equal_frac": agree, "kernels_per_step": stages * 8 + 2,
+            "sequence": "per stage: 2r, row norm, cuBLAS FP32 GEMM [8192,64]x[64,1024] (TF32 "
+                        "off), moss_lfq_select (the reference's selection rules), r -= c, "
+                        "recon += c; one CUDA graph per step"}
+
+
 def stack_lines(torch, dev, cpu=True):
     """The codec's streaming transformer stack (24 layers, hidden 1280, 20
     heads, feed-forward 5120, FP32 weights seeded 2, bf16 GEMMs) over 125
@@ -617,6 +668,8 @@ def run_b200(args):
     kernels = None
     if rank == 0 and not args.no_kernels:
         kernels = kernel_lines(torch, fm, dev, peaks["hbm_gbs"])
+        kernels["rvq_reference_sequence"] = rvq_sequence_line(torch, x, rvq.books, codes,
+                                                              kernel_s / args.steps)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         rate, threads, rows, dt = cpu_rvq_rate(x_np, books_np, seconds=10.0)
