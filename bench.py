@@ -463,6 +463,85 @@ def rvq_sequence_line(torch, x, books, codes_fused, fused_s):
                         "recon += c; one CUDA graph per step"}
 
 
+def _stack_rate(torch, dev, cfg, stack, streams, chunks):
+    from fast_moss_b200.transformer import BatchedStreams
+
+    sched = BatchedStreams(stack, streams=streams, chunks_per_graph=1)
+    g = torch.Generator().manual_seed(4)
+    host = torch.randn(streams, cfg.chunk_tokens * chunks, cfg.dim, generator=g).pin_memory()
+    host_out = torch.empty_like(host).pin_memory()
+    x_dev = torch.empty(streams, cfg.chunk_tokens, cfg.dim, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def run(copies):
+        sched.reset()
+        for c in range(chunks):
+            sl = slice(c * cfg.chunk_tokens, (c + 1) * cfg.chunk_tokens)
+            if copies:
+                x_dev.copy_(host[:, sl], non_blocking=True)
+            y = sched.push(x_dev)
+            if copies:
+                host_out[:, sl].copy_(y, non_blocking=True)
+
+    times = {}
+    for copies in (False, True):
+        run(copies)
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        run(copies)
+        s1.record(stream)
+        s1.synchronize()
+        times[copies] = s0.elapsed_time(s1) * 1e-3
+    sched.release()
+    torch.cuda.synchronize()
+    audio = streams * chunks * 0.08
+    return {"e2e": audio / times[True], "device": audio / times[False],
+            "ms_per_chunk_e2e": times[True] / chunks * 1e3,
+            "ms_per_chunk_device": times[False] / chunks * 1e3,
+            "h2d_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4,
+            "d2h_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4}
+
+
+def _qkv_kernel_line(torch, dev, cfg, weights):
+    """The stack's qkv projection + rotary + history writes, per layer: the
+    fused tcgen05 kernel against F.linear (cuBLAS) + moss_rope_kv, over the
+    24 layers' weights in turn (236 MB of bf16 weights: more than L2, as in
+    the stack), graph-timed."""
+    import torch.nn.functional as F
+    from fast_moss_b200.v2_pointwise import pack_qkv_weight, qkv_rope, rope_kv
+
+    h, t = cfg.heads, cfg.chunk_tokens
+    layers = []
+    for w in weights:
+        w16 = w["qkv_w"].to(dev, torch.bfloat16)
+        layers.append((w16, pack_qkv_weight(w16), w["qkv_b"].to(dev, torch.bfloat16)))
+    res = {"weight_bytes_per_layer": layers[0][0].numel() * 2}
+    for streams in (1, 64):
+        g = torch.Generator(device=dev).manual_seed(5)
+        x = torch.randn(streams, t, cfg.dim, device=dev, generator=g).to(torch.bfloat16)
+        offset = torch.full((streams,), 100, dtype=torch.long, device=dev)
+        slots = (offset[:, None] + torch.arange(t, device=dev)) % cfg.history_slots
+        kc = torch.zeros(streams, h, cfg.history_slots, 64, device=dev, dtype=torch.bfloat16)
+        vc = torch.zeros_like(kc)
+
+        def fused(layer, _handle):
+            qkv_rope(x, layer[1], layer[2], h, offset, cfg.max_period, slots, kc, vc)
+
+        def unfused(layer, _handle):
+            qkv = F.linear(x, layer[0], layer[2]).view(streams, t, 3, h, 64)
+            rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
+                    qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots, kc, vc)
+
+        tf = time_launches(torch, fused, layers, launches=48, replays=5)
+        tu = time_launches(torch, unfused, layers, launches=48, replays=5)
+        res[f"streams_{streams}"] = {
+            "us_fused": tf * 1e6, "us_linear_plus_rope_kv": tu * 1e6,
+            "fused_weight_gbs": res["weight_bytes_per_layer"] / tf / 1e9}
+    return res
+
+
 def stack_lines(torch, dev, cpu=True):
     """The codec's streaming transformer stack (24 layers, hidden 1280, 20
     heads, feed-forward 5120, FP32 weights seeded 2, bf16 GEMMs) over 125
@@ -472,54 +551,22 @@ def stack_lines(torch, dev, cpu=True):
     reference's StreamingCodec shape, 64 streams the batched scheduler.
     The CPU baseline is the eager oracle stack on the host cores (bf16
     GEMMs, a bounded sample of chunks)."""
-    from fast_moss_b200.transformer import (BatchedStreams, StackConfig, StreamingTransformer,
-                                            init_weights)
+    from fast_moss_b200.transformer import StackConfig, StreamingTransformer, init_weights
 
     cfg = StackConfig()
     chunks = 125
     weights = init_weights(cfg, seed=2)
-    stack = StreamingTransformer(cfg, weights, dev)
     out = {"workload": "streaming stack: 24 layers, hidden 1280, 20 heads, ffn 5120, "
                        "context 250 tokens, 4 tokens per 80 ms chunk, 125 chunks per stream",
            "metric": "audio-sec/sec (RTF x streams)", "dtype": "bf16 GEMMs, f32 residual"}
-    for streams in (1, 64):
-        sched = BatchedStreams(stack, streams=streams, chunks_per_graph=1)
-        g = torch.Generator().manual_seed(4)
-        host = torch.randn(streams, cfg.chunk_tokens * chunks, cfg.dim, generator=g).pin_memory()
-        host_out = torch.empty_like(host).pin_memory()
-        x_dev = torch.empty(streams, cfg.chunk_tokens, cfg.dim, device=dev)
-        stream = torch.cuda.current_stream(dev)
-
-        def run(copies):
-            sched.reset()
-            for c in range(chunks):
-                sl = slice(c * cfg.chunk_tokens, (c + 1) * cfg.chunk_tokens)
-                if copies:
-                    x_dev.copy_(host[:, sl], non_blocking=True)
-                y = sched.push(x_dev)
-                if copies:
-                    host_out[:, sl].copy_(y, non_blocking=True)
-
-        times = {}
-        for copies in (False, True):
-            run(copies)
-            torch.cuda.synchronize()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            run(copies)
-            s1.record(stream)
-            s1.synchronize()
-            times[copies] = s0.elapsed_time(s1) * 1e-3
-        audio = streams * chunks * 0.08
-        out[f"streams_{streams}"] = {
-            "e2e": audio / times[True], "device": audio / times[False],
-            "ms_per_chunk_e2e": times[True] / chunks * 1e3,
-            "ms_per_chunk_device": times[False] / chunks * 1e3,
-            "h2d_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4,
-            "d2h_bytes_per_chunk": streams * cfg.chunk_tokens * cfg.dim * 4}
-        sched.release()
-        del sched
+    for fused in (False, True):
+        stack = StreamingTransformer(cfg, weights, dev, fused_qkv=fused)
+        dst = out if not fused else out.setdefault("fused_qkv", {
+            "what": "qkv Linear + rotary + history writes as one tcgen05 kernel (moss_qkv_rope)"})
+        for streams in (1, 64):
+            dst[f"streams_{streams}"] = _stack_rate(torch, dev, cfg, stack, streams, chunks)
+        del stack
+    out["qkv_kernel"] = _qkv_kernel_line(torch, dev, cfg, weights)
     torch.cuda.synchronize()
     if cpu:
         from oracle.stack import EagerStack

@@ -25,6 +25,7 @@
 //     current one;
 //   * rope_pair_kernel, one interleaved pair per item, for any strides.
 #include "pipeline.cuh"
+#include "rotary.cuh"
 
 namespace moss {
 
@@ -43,18 +44,6 @@ struct RopeArgs {
   int64_t ks[4];
   int tt;  // time steps per CTA
 };
-
-__device__ __forceinline__ float offset_as_float(const void* p, int dtype, int64_t b) {
-  if (dtype == 0) return static_cast<float>(static_cast<const int64_t*>(p)[b]);
-  if (dtype == 1) return static_cast<float>(static_cast<const int32_t*>(p)[b]);
-  return static_cast<const float*>(p)[b];
-}
-
-__device__ __forceinline__ void rotate_pair(float qr, float qj, float c, float s, float& o0,
-                                            float& o1) {
-  o0 = __fsub_rn(__fmul_rn(qr, c), __fmul_rn(qj, s));
-  o1 = __fadd_rn(__fmul_rn(qr, s), __fmul_rn(qj, c));
-}
 
 // Fills the (c, s) pairs of this CTA's tile: [tt][half] each.
 __device__ __forceinline__ void fill_phase(const RopeArgs& a, int64_t bi, int64_t t0, int tt,

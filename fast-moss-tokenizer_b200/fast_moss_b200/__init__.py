@@ -19,6 +19,8 @@ from .rvq import ResidualVectorQuantizer
 from .v2_pointwise import (
     gated_activation,
     layer_norm,
+    pack_qkv_weight,
+    qkv_rope,
     residual_layer_norm,
     rope,
     rope_kv,
@@ -35,6 +37,8 @@ __all__ = [
     "rotate",
     "rope",
     "rope_kv",
+    "pack_qkv_weight",
+    "qkv_rope",
     "scale_add",
     "layer_norm",
     "residual_layer_norm",

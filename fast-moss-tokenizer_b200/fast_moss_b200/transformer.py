@@ -19,7 +19,11 @@ native kernels of libfast_moss_b200:
   residual + layer scale 2 + next LN 1       moss_residual_layer_norm_out
                                              (moss_scale_add after the last layer)
 
-GEMMs (cuBLAS) and attention (SDPA) stay library calls, as in the reference;
+With `fused_qkv=True` the qkv Linear, the rotary embedding and the history
+writes are one tcgen05 kernel (moss_qkv_rope: bf16 tensor-core GEMM whose
+epilogue rounds, rotates and stores into the ring; its dot products are
+summed in its own order, not cuBLAS's).  The other GEMMs (cuBLAS) and
+attention (SDPA) stay library calls, as in the reference;
 attention is pinned to SDPA's memory-efficient backend, which runs these
 few-query, masked shapes about twice as fast as the backend chosen by
 default on B200 (66 us against 121 us per layer at 64 streams).
@@ -41,7 +45,15 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .graphs import GraphedCallable
-from .v2_pointwise import gated_activation, layer_norm, residual_layer_norm, rope_kv, scale_add
+from .v2_pointwise import (
+    gated_activation,
+    layer_norm,
+    pack_qkv_weight,
+    qkv_rope,
+    residual_layer_norm,
+    rope_kv,
+    scale_add,
+)
 
 
 @dataclass(frozen=True)
@@ -168,7 +180,7 @@ class StreamingTransformer:
     """The stack: FP32 parameters on one CUDA device, bf16 GEMM weights cached
     once (the reference's cached Linear, fast_moss/v2_runtime.py:77-106)."""
 
-    def __init__(self, cfg, weights, device):
+    def __init__(self, cfg, weights, device, *, fused_qkv=False):
         device = torch.device(device)
         if device.type != "cuda":
             raise ValueError("StreamingTransformer runs on a CUDA device")
@@ -181,7 +193,12 @@ class StreamingTransformer:
             p = {k: w[k].to(device=device, dtype=torch.float32).contiguous() for k in WEIGHT_NAMES}
             for k in ("qkv_w", "qkv_b", "out_w", "out_b", "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b"):
                 p[k + "16"] = p[k].to(torch.bfloat16)
+            if fused_qkv:
+                p["qkv_image"] = pack_qkv_weight(p["qkv_w16"])
             self.layers.append(p)
+        self.fused_qkv = bool(fused_qkv)
+        if self.fused_qkv and cfg.head_dim != 64:
+            raise ValueError("the fused qkv projection needs heads of 64")
 
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
@@ -203,11 +220,15 @@ class StreamingTransformer:
         # LayerNorm outputs go straight to the next GEMM as its bf16 input
         normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps, out_dtype=bf16)
         for i, p in enumerate(self.layers):
-            qkv = F.linear(normed, p["qkv_w16"], p["qkv_b16"])
-            qkv = qkv.view(s, t, 3, h, dh)
-            q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
-                        qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
-                        hist.keys[i], hist.values[i])
+            if self.fused_qkv:
+                q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
+                             slots, hist.keys[i], hist.values[i])
+            else:
+                qkv = F.linear(normed, p["qkv_w16"], p["qkv_b16"])
+                qkv = qkv.view(s, t, 3, h, dh)
+                q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
+                            qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
+                            hist.keys[i], hist.values[i])
             with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
                 a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
                                                    attn_mask=mask)

@@ -151,6 +151,79 @@ def rope_kv(q, k, v, offset, max_period, slots, k_cache, v_cache):
     return oq
 
 
+def pack_qkv_weight(weight):
+    """Packs a bf16 qkv Linear weight [3*H*64, K] (K a multiple of 64) for
+    `qkv_rope`: blocks of 32 rows x 64 columns in the tensor cores'
+    no-swizzle K-major core-matrix order, block (row tile, column chunk) at
+    [n // 32][k // 64], inside a block [row group][k core][row][element] of
+    8 each (4 row groups).  Done once per weight, like the reference's
+    cached bf16 Linear weight (fast_moss/v2_runtime.py:77-106)."""
+    if weight.ndim != 2 or weight.shape[0] % 192 or weight.shape[1] % 64 or not weight.shape[1]:
+        raise ValueError("Expected a [3*H*64, K] weight with K a multiple of 64")
+    n, k = weight.shape
+    w = weight.to(torch.bfloat16).contiguous()
+    return w.view(n // 32, 4, 8, k // 64, 8, 8).permute(0, 3, 1, 4, 2, 5).contiguous()
+
+
+def qkv_rope(x, w_image, bias, heads, offset, max_period, slots, k_cache, v_cache):
+    """The qkv Linear with the rotary embedding and the history-ring writes
+    in its epilogue (one tcgen05 kernel).
+
+    x: bf16 [B, T, K] (the LayerNorm output); w_image: `pack_qkv_weight` of
+    the [3*heads*64, K] weight; bias: bf16 [3*heads*64] or None; offset [B]
+    and int64 slots [B, T] as in `rope_kv`; k_cache, v_cache: contiguous
+    bf16 [B, heads, S, 64].  Returns the rotated q [B, heads, T, 64].  The
+    same bits as F.linear followed by `rope_kv` whenever the projection's
+    FP32 sums round to the same bf16 value (the summation order differs
+    from cuBLAS's).
+    """
+    if x.ndim != 3 or x.dtype != torch.bfloat16 or not x.is_cuda:
+        raise ValueError("Expected bf16 CUDA x [B, T, K]")
+    b, t, k = x.shape
+    n = 3 * heads * 64
+    if (
+        w_image.dtype != torch.bfloat16
+        or w_image.numel() != n * k
+        or not w_image.is_contiguous()
+        or (bias is not None and (bias.dtype != torch.bfloat16 or bias.shape != (n,)))
+        or offset.numel() != b
+        or slots.shape != (b, t)
+        or slots.dtype != torch.int64
+        or k_cache.dtype != torch.bfloat16
+        or k_cache.ndim != 4
+        or k_cache.shape[:2] != (b, heads)
+        or k_cache.shape[3] != 64
+        or v_cache.shape != k_cache.shape
+        or v_cache.dtype != torch.bfloat16
+        or not k_cache.is_contiguous()
+        or not v_cache.is_contiguous()
+        or any(v.device != x.device for v in (w_image, offset, slots, k_cache, v_cache))
+        or (bias is not None and bias.device != x.device)
+    ):
+        raise ValueError("Incompatible qkv_rope inputs")
+    if offset.dtype == torch.int64:
+        odt = 0
+    elif offset.dtype == torch.int32:
+        odt = 1
+    else:
+        odt = 2
+        offset = offset.float()
+    x = x.contiguous()
+    offset = offset.contiguous()
+    slots = slots.contiguous()
+    bias = bias.contiguous() if bias is not None else None
+    q = torch.empty((b, heads, t, 64), device=x.device, dtype=torch.bfloat16)
+    if x.numel():
+        with torch.cuda.device(x.device):
+            _lib.call(
+                "moss_qkv_rope", x.data_ptr(), w_image.data_ptr(),
+                bias.data_ptr() if bias is not None else None, b, t, heads, k,
+                offset.data_ptr(), odt, -math.log(max_period) * 2 / 64, slots.data_ptr(),
+                q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
+                _stream(x.device))
+    return q
+
+
 def scale_add(x, update, scale):
     """Residual update x + update * scale (FP32 out, no FMA).
 

@@ -164,6 +164,32 @@ MOSS_API int moss_rope_kv(const void* q, const void* k, const void* v, int dtype
               const int64_t* v_strides, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Fused qkv projection with the rotary embedding in its epilogue (bf16).
+ * Replaces the cached bf16 Linear of the attention input
+ * (fast_moss/v2_runtime.py:77-106, F.linear at :104) followed by the
+ * patched rotary forward (fast_moss/v2_runtime.py:186-224) and the
+ * streaming attention's key/value cache update, i.e. the Linear followed by
+ * moss_rope_kv:
+ *   y = bf16(x W^T + bias)   x [b*t, k] bf16 rows (row = b_i*t + t_i),
+ *                            W [3*h*64, k] bf16, FP32 accumulation on the
+ *                            tensor cores (tcgen05), one bf16 rounding
+ *   q = y[:, :64h], k = y[:, 64h:128h], v = y[:, 128h:], heads of 64
+ *   q, k rotated with the in-kernel phase of moss_rope (offset[b_i] + t_i)
+ *   oq [b, h, t, 64]; k_cache / v_cache [b, h, cache_slots, 64] at slot
+ *   slots[b_i*t + t_i] (a slot out of range is skipped and reported).
+ * w_image: W pre-packed by the host into blocks of 32 rows x 64 columns in
+ * the MMA's no-swizzle K-major core-matrix order ([3h*2][k/64][4][8][8][8]
+ * bf16: row group, k core, row, element).  bias: [3*h*64] bf16 or NULL.
+ * k must be a multiple of 64; buffers 16-byte aligned.  The dot products
+ * are summed in this kernel's order, not cuBLAS's, so a projection output
+ * can differ from F.linear's by the rounding of a different sum.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_qkv_rope(const void* x, const void* w_image, const void* bias, int64_t b,
+              int64_t t, int64_t h, int64_t k, const void* offset, int offset_dtype,
+              float freq_coef, const int64_t* slots, void* oq, void* k_cache,
+              void* v_cache, int64_t cache_slots, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Bias + gated activation, bf16 or float32 in and out.
  * No kernel in the reference (its FFN activation is upstream model code);
  * this is the eager-PyTorch chain it replaces, one rounding per torch op:

@@ -103,3 +103,28 @@ def test_eager_step_equals_graph_replay(moss, cuda_device):
     sched = BatchedStreams(stack, streams=2, chunks_per_graph=3)
     assert torch.equal(sched(feats), eager)
     sched.release()
+
+
+def test_fused_qkv_stack(moss, cuda_device):
+    """The stack with the fused qkv projection (tcgen05 GEMM + rotary
+    epilogue + history writes in one kernel): its graph replays equal its
+    own eager steps bit for bit, and it tracks the cuBLAS-projection stack
+    to bf16 noise (the projection's sums are ordered differently)."""
+    from fast_moss_b200.transformer import (BatchedStreams, StackConfig, StreamingTransformer,
+                                            init_weights)
+
+    cfg = StackConfig()
+    weights = init_weights(cfg, seed=2)
+    plain = StreamingTransformer(cfg, weights, cuda_device)
+    fused = StreamingTransformer(cfg, weights, cuda_device, fused_qkv=True)
+    feats = _features(2, 4 * 6, cfg.dim, 3).to(cuda_device)
+    sp = BatchedStreams(plain, streams=2)
+    sf = BatchedStreams(fused, streams=2)
+    a, b = sp(feats), sf(feats)
+    hist = fused.history(2)
+    eager = torch.cat([fused.step(feats[:, c * 4:(c + 1) * 4], hist) for c in range(6)], 1)
+    assert torch.equal(b, eager)
+    rel = float((a - b).norm() / a.norm())
+    assert rel < 2e-2, rel
+    sp.release()
+    sf.release()
