@@ -22,7 +22,9 @@ native kernels of libfast_moss_b200:
 With `fused_qkv=True` the qkv Linear, the rotary embedding and the history
 writes are one tcgen05 kernel (moss_qkv_rope: bf16 tensor-core GEMM whose
 epilogue rounds, rotates and stores into the ring; its dot products are
-summed in its own order, not cuBLAS's).  The other GEMMs (cuBLAS) and
+summed in its own order, not cuBLAS's) for chunks of at most
+FUSED_QKV_MAX_ROWS token rows (all streams together), where it is faster;
+larger chunks keep the cuBLAS GEMM + moss_rope_kv.  The other GEMMs (cuBLAS) and
 attention (SDPA) stay library calls, as in the reference;
 attention is pinned to SDPA's memory-efficient backend, which runs these
 few-query, masked shapes about twice as fast as the backend chosen by
@@ -54,6 +56,13 @@ from .v2_pointwise import (
     rope_kv,
     scale_add,
 )
+
+
+# Token rows (streams x chunk tokens) up to which the fused qkv projection
+# runs: one 32-row tile of moss_qkv_rope.  Measured per layer on B200 at
+# the configured shape: 9.2 us fused against 16.5 us for the cuBLAS GEMM +
+# moss_rope_kv at 4 rows; 70 us against 21 us at 256 rows.
+FUSED_QKV_MAX_ROWS = 32
 
 
 @dataclass(frozen=True)
@@ -220,7 +229,7 @@ class StreamingTransformer:
         # LayerNorm outputs go straight to the next GEMM as its bf16 input
         normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps, out_dtype=bf16)
         for i, p in enumerate(self.layers):
-            if self.fused_qkv:
+            if self.fused_qkv and s * t <= FUSED_QKV_MAX_ROWS:
                 q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
                              slots, hist.keys[i], hist.values[i])
             else:

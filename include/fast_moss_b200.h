@@ -180,9 +180,12 @@ MOSS_API int moss_rope_kv(const void* q, const void* k, const void* v, int dtype
  * w_image: W pre-packed by the host into blocks of 32 rows x 64 columns in
  * the MMA's no-swizzle K-major core-matrix order ([3h*2][k/64][4][8][8][8]
  * bf16: row group, k core, row, element).  bias: [3*h*64] bf16 or NULL.
- * k must be a multiple of 64; buffers 16-byte aligned.  The dot products
- * are summed in this kernel's order, not cuBLAS's, so a projection output
- * can differ from F.linear's by the rounding of a different sum.
+ * k must be a multiple of 64 and at most 1792; buffers 16-byte aligned.
+ * The dot products are summed in this kernel's order, not cuBLAS's, so a
+ * projection output can differ from F.linear's by the rounding of a
+ * different sum.  Built for skinny inputs (one 32-row tile of tokens per
+ * CTA, all operands resident): on B200 it beats the cuBLAS GEMM + the
+ * rotary kernel up to about 32 rows and loses to them well above.
  * ------------------------------------------------------------------------- */
 MOSS_API int moss_qkv_rope(const void* x, const void* w_image, const void* bias, int64_t b,
               int64_t t, int64_t h, int64_t k, const void* offset, int offset_dtype,
