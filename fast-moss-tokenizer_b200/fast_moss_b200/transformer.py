@@ -185,6 +185,21 @@ class StreamHistory:
         return positions, slots, mask[:, None]
 
 
+def additive_mask(mask, dtype):
+    """The boolean attention mask as the additive mask (0 where attended,
+    -inf elsewhere) that SDPA builds from a boolean one, in a buffer whose
+    key dimension is padded to a multiple of 16 (the memory-efficient
+    kernel's alignment; the returned tensor is a view of the real keys).
+    Built once per chunk, so the 24 layers' attention calls skip SDPA's
+    own conversion and padding (four small kernels per layer)."""
+    n = mask.shape[-1]
+    padded = torch.zeros(mask.shape[:-1] + ((n + 15) // 16 * 16,), device=mask.device,
+                         dtype=dtype)
+    out = padded[..., :n]
+    out.masked_fill_(~mask, float("-inf"))
+    return out
+
+
 class StreamingTransformer:
     """The stack: FP32 parameters on one CUDA device, bf16 GEMM weights cached
     once (the reference's cached Linear, fast_moss/v2_runtime.py:77-106)."""
@@ -223,6 +238,7 @@ class StreamingTransformer:
         h, dh = cfg.heads, cfg.head_dim
         offset = hist.pos  # position of the chunk's first token (advanced at the end)
         _, slots, mask = hist.advance(t)
+        mask = additive_mask(mask, torch.bfloat16)
         first = self.layers[0]
         x = x.contiguous()
         bf16 = torch.bfloat16
