@@ -33,7 +33,7 @@
 //              slots; they evaluate the rows' (c, s) table while the loads
 //              fly; then warp 0 is the epilogue, one row per thread (TMEM
 //              lane = row), with no global load left;
-//   warp 5     allocates 32 TMEM columns and issues 4 MMAs per chunk
+//   warp 4     allocates 32 TMEM columns and issues 4 MMAs per chunk
 //              (kind::f16, bf16 operands, M=128, N=32, K=16).  The MMA reads
 //              128 operand rows; rows 32-127 fall on the next chunks' bytes
 //              (in bounds: 12 KB of slack follow the last chunk) and land in
@@ -54,7 +54,7 @@ constexpr int kMaxChunks = 24;  // K <= 1536
 constexpr uint32_t kAChunk = kRows * kChunk * 2;               // 4 KB of token rows per chunk
 constexpr uint32_t kASlack = (kMmaRows - kRows) * kChunk * 2;  // rows 32-127 of the last chunk
 constexpr uint32_t kBBytes = kCols * kChunk * 2;               // 4 KB weight block
-constexpr int kThreads = 192;
+constexpr int kThreads = 160;  // warps 0-3 loads and epilogue, warp 4 MMA
 constexpr int kLoaderThreads = 128;
 constexpr uint32_t kTmemCols = 32;
 
@@ -155,13 +155,13 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
     pipe::fence_mbar_init();
   }
   if (tid < kCols / 2) freq[tid] = expf(__fmul_rn(static_cast<float>(pair0 + tid), a.coef));
-  if (warp == 5) tc::alloc(tmem_slot, kTmemCols);
+  if (warp == 4) tc::alloc(tmem_slot, kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 4) {
     // ---------------------------------------------------------- MMA
     if (lane == 0) {
       const bool ok = pipe::mbar_wait(a_full, 0);
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
       }
     }
     __syncwarp();
-  } else if (warp < 4) {
+  } else {
     // ---------------------------------------------------------- loads, then the epilogue
     {
       const uint32_t ab = pipe::smem_u32(sb + L.a), bb = pipe::smem_u32(sb + L.b);
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  if (warp == 5) tc::dealloc(tmem, kTmemCols);
+  if (warp == 4) tc::dealloc(tmem, kTmemCols);
 }
 
 }  // namespace qkvr
