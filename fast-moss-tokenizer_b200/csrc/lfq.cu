@@ -186,13 +186,30 @@ __global__ void __launch_bounds__(256) lfq_decode_kernel(
 }
 
 // The same decode for many rows: the normalised codebook and its norms are
-// staged in shared memory once per block, each warp takes kDecRows rows,
-// and every codeword read serves all of them.  Per row the arithmetic is
-// lfq_decode_kernel's (prepare_row, the sequential 8-channel dot, the
-// distance rounding and the first-NaN / first-minimum pick), so the results
-// are the same bits.  Rows past the end are computed on the last row and
-// discarded, so that every warp reaches the block barrier.
-constexpr int kDecRows = 8;
+// staged in shared memory once per block of 8 warps, each warp takes
+// ROWS rows and a 1/SPLIT share of the codes, and every codeword read
+// serves all of its rows; the SPLIT warps of a row group then merge their
+// picks through shared memory (smallest distance, lowest index among equal
+// distances, lowest NaN index: the first-NaN / first-minimum rule over the
+// whole codebook, since each warp's share is a contiguous code range).  Per
+// row and code the arithmetic is lfq_decode_kernel's (prepare_row, the
+// sequential 8-channel dot, the distance rounding), so the results are the
+// same bits.  Rows past the end are computed on the last row and
+// discarded, so that every warp reaches the block barriers.
+#ifndef MOSS_DEC_ROWS
+#define MOSS_DEC_ROWS 8
+#endif
+// Codes per warp: all of them.  Splitting them across two or four warps
+// of a row group (with the merge below) measured slower on B200: 12.1 and
+// 13.0 us against 11.7 us at 8192 rows x 1024 codes, 47 and 66 us against
+// 38 us at 4096 codes.
+#ifndef MOSS_DEC_SPLIT
+#define MOSS_DEC_SPLIT 1
+#endif
+constexpr int kDecRows = MOSS_DEC_ROWS;
+constexpr int kDecSplit = MOSS_DEC_SPLIT;
+constexpr int kDecWarps = 8;
+constexpr int kDecRowsPerBlock = kDecRows * kDecWarps / kDecSplit;
 constexpr int kDecMaxCodes = 4096;  // 36 bytes per code of shared memory
 
 struct Pick32 {
@@ -210,6 +227,22 @@ __device__ __forceinline__ void pick32_push(Pick32& p, float dist, int j) {
   p.best = better ? dist : p.best;
 }
 
+// The warp's pick over all of its lanes (every lane gets it).
+__device__ __forceinline__ Pick32 pick32_allreduce(Pick32 p) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, p.best, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, p.best_i, m);
+    const int on = __shfl_xor_sync(0xffffffffu, p.nan_i, m);
+    if (ob < p.best || (ob == p.best && oi < p.best_i)) {
+      p.best = ob;
+      p.best_i = oi;
+    }
+    if (on < p.nan_i) p.nan_i = on;
+  }
+  return p;
+}
+
 __device__ __forceinline__ int pick32_reduce(Pick32 p) {
 #pragma unroll
   for (int m = 16; m > 0; m >>= 1) {
@@ -225,19 +258,24 @@ __device__ __forceinline__ int pick32_reduce(Pick32 p) {
   return p.nan_i != INT_MAX ? p.nan_i : p.best_i;
 }
 
-__global__ void __launch_bounds__(128) lfq_decode_tile_kernel(
+__global__ void __launch_bounds__(kDecWarps * 32) lfq_decode_tile_kernel(
     const float* __restrict__ x, const float* __restrict__ book_normed,
     const float* __restrict__ code_norm, const float* __restrict__ weight, int64_t b, int64_t t,
     int k, float* __restrict__ out, int64_t* __restrict__ indices) {
   extern __shared__ float4 dec_smem[];
   float4* sbook = dec_smem;                                 // [k][2]
   float* scn = reinterpret_cast<float*>(dec_smem + 2 * k);  // [k]
+  __shared__ Pick32 part[kDecSplit][kDecWarps / kDecSplit][kDecRows];
   for (int i = threadIdx.x; i < 2 * k; i += blockDim.x)
     sbook[i] = reinterpret_cast<const float4*>(book_normed)[i];
   for (int i = threadIdx.x; i < k; i += blockDim.x) scn[i] = code_norm[i];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  constexpr int kGroups = kDecWarps / kDecSplit;
+  const int group = warp % kGroups, share = warp / kGroups;
   const int64_t rows = b * t;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp) * kDecRows;
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kGroups + group) * kDecRows;
+  const int j_begin = static_cast<int>(static_cast<int64_t>(k) * share / kDecSplit);
+  const int j_end = static_cast<int>(static_cast<int64_t>(k) * (share + 1) / kDecSplit);
   const bool transposed = (b == 1 && t > 1);
   // lane r prepares row r of the warp's group (all lanes run one
   // preparation in parallel), then every lane receives the group's values
@@ -255,8 +293,8 @@ __global__ void __launch_bounds__(128) lfq_decode_tile_kernel(
   __syncthreads();
   Pick32 pk[kDecRows];
 #pragma unroll
-  for (int r = 0; r < kDecRows; ++r) pk[r] = Pick32{CUDART_INF_F, lane, INT_MAX};
-  for (int j = lane; j < k; j += 32) {
+  for (int r = 0; r < kDecRows; ++r) pk[r] = Pick32{CUDART_INF_F, j_begin + lane, INT_MAX};
+  for (int j = j_begin + lane; j < j_end; j += 32) {
     const float4 c0 = sbook[2 * j], c1 = sbook[2 * j + 1];
     const float cn = scn[j];
 #pragma unroll
@@ -274,11 +312,32 @@ __global__ void __launch_bounds__(128) lfq_decode_tile_kernel(
   }
 #pragma unroll
   for (int r = 0; r < kDecRows; ++r) {
-    const int idx = pick32_reduce(pk[r]);
+    const Pick32 w = pick32_allreduce(pk[r]);
+    if (lane == 0) part[share][group][r] = w;
+  }
+  __syncthreads();
+  if (share == 0 && lane < kDecRows) {
+    const int r = lane;
+    Pick32 m = part[0][group][r];
+    // later shares hold higher codes: a strictly smaller distance wins, an
+    // equal one keeps the earlier (lower) index
+#pragma unroll
+    for (int q = 1; q < kDecSplit; ++q) {
+      const Pick32 o = part[q][group][r];
+      if (o.best < m.best) {
+        m.best = o.best;
+        m.best_i = o.best_i;
+      }
+      if (o.nan_i < m.nan_i) m.nan_i = o.nan_i;
+    }
+    const int idx = m.nan_i != INT_MAX ? m.nan_i : m.best_i;
     const int64_t row = row0 + r;
     if (row < rows) {
-      if (lane == 0) indices[row] = idx;
-      if (lane < 8) out[row * 8 + lane] = weight[static_cast<int64_t>(idx) * 8 + lane];
+      indices[row] = idx;
+      const float4* src = reinterpret_cast<const float4*>(weight + static_cast<int64_t>(idx) * 8);
+      float4* dst = reinterpret_cast<float4*>(out + row * 8);
+      dst[0] = src[0];
+      dst[1] = src[1];
     }
   }
 }
@@ -332,14 +391,15 @@ extern "C" int moss_lfq_decode(const float* x, const float* book_normed, const f
     return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
   if (!aligned16(book_normed)) return fail(MOSS_ERR_VALUE, "%s: normalised book must be 16-byte aligned", name);
   const int64_t rows = b * t;
-  if (rows >= 256 && k <= kDecMaxCodes && rows / (4 * kDecRows) < 0x7fffffffLL) {
-    // many rows: the codebook staged once per block of 4 warps x kDecRows rows
+  if (rows >= 256 && k <= kDecMaxCodes && rows / kDecRowsPerBlock < 0x7fffffffLL &&
+      aligned16(weight) && aligned16(out)) {
+    // many rows: the codebook staged once per block of kDecRowsPerBlock rows
     const size_t smem = static_cast<size_t>(k) * 36;
     static bool configured[kMaxDevices] = {};
     allow_dynamic_smem(lfq_decode_tile_kernel, kDecMaxCodes * 36, configured);
-    lfq_decode_tile_kernel<<<static_cast<unsigned>((rows + 4 * kDecRows - 1) / (4 * kDecRows)), 128,
-                             smem, as_stream(stream)>>>(x, book_normed, code_norm, weight, b, t,
-                                                        static_cast<int>(k), out, indices);
+    lfq_decode_tile_kernel<<<static_cast<unsigned>((rows + kDecRowsPerBlock - 1) / kDecRowsPerBlock),
+                             kDecWarps * 32, smem, as_stream(stream)>>>(
+        x, book_normed, code_norm, weight, b, t, static_cast<int>(k), out, indices);
     return launch_status(name);
   }
   lfq_decode_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, as_stream(stream)>>>(
