@@ -54,8 +54,15 @@ constexpr int kMaxChunks = 24;  // K <= 1536
 constexpr uint32_t kAChunk = kRows * kChunk * 2;               // 4 KB of token rows per chunk
 constexpr uint32_t kASlack = (kMmaRows - kRows) * kChunk * 2;  // rows 32-127 of the last chunk
 constexpr uint32_t kBBytes = kCols * kChunk * 2;               // 4 KB weight block
-constexpr int kThreads = 160;  // warps 0-3 loads and epilogue, warp 4 MMA
-constexpr int kLoaderThreads = 128;
+// Loader warps: 4.  With 8 or 12 the one-stream launch takes the same time
+// (8.9-9.0 us on B200): what limits a CTA is its SM's rate of outstanding
+// global loads, not the number of warps issuing them.
+#ifndef MOSS_QKV_LOADER_WARPS
+#define MOSS_QKV_LOADER_WARPS 4
+#endif
+constexpr int kLoaderWarps = MOSS_QKV_LOADER_WARPS;
+constexpr int kLoaderThreads = kLoaderWarps * 32;
+constexpr int kThreads = kLoaderThreads + 32;  // loader warps (warp 0 also the epilogue), then MMA
 constexpr uint32_t kTmemCols = 32;
 
 // Shared-memory layout (offsets from a 128-byte aligned base).
@@ -155,13 +162,13 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
     pipe::fence_mbar_init();
   }
   if (tid < kCols / 2) freq[tid] = expf(__fmul_rn(static_cast<float>(pair0 + tid), a.coef));
-  if (warp == 4) tc::alloc(tmem_slot, kTmemCols);
+  if (warp == kLoaderWarps) tc::alloc(tmem_slot, kTmemCols);
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kLoaderWarps) {
     // ---------------------------------------------------------- MMA
     if (lane == 0) {
       const bool ok = pipe::mbar_wait(a_full, 0);
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
       tc::fence_async_shared();
       pipe::mbar_arrive(a_full);
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(kLoaderThreads) : "memory");
     if (warp == 0) {
       const bool ok = pipe::mbar_wait(acc_full, 0);
       tc::fence_after();
@@ -267,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) qkv_rope_kernel(const Args a) {
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  if (warp == 4) tc::dealloc(tmem, kTmemCols);
+  if (warp == kLoaderWarps) tc::dealloc(tmem, kTmemCols);
 }
 
 }  // namespace qkvr
