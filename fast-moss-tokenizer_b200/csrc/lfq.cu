@@ -187,35 +187,27 @@ __global__ void __launch_bounds__(256) lfq_decode_kernel(
 
 // The same decode for many rows: the normalised codebook and its norms are
 // staged in shared memory once per block of kDecWarps warps, each warp takes
-// kDecRows rows and a 1/kDecSplit share of the codes, and every codeword read
-// serves all of its rows; the kDecSplit warps of a row group then merge their
-// picks through shared memory (smallest distance, lowest index among equal
-// distances, lowest NaN index: the first-NaN / first-minimum rule over the
-// whole codebook, since each warp's share is a contiguous code range).  Per
-// row and code the arithmetic is lfq_decode_kernel's (prepare_row, the
-// sequential 8-channel dot, the distance rounding), so the results are the
-// same bits.  Rows past the end are computed on the last row and
-// discarded, so that every warp reaches the block barriers.
+// kDecRows rows against the whole codebook, and every codeword read serves
+// all of its rows.  Per row and code the arithmetic is lfq_decode_kernel's
+// (prepare_row, the sequential 8-channel dot, the distance rounding, the
+// first-NaN / first-minimum pick), so the results are the same bits.  Rows
+// past the end are computed on the last row and discarded, so that every
+// warp reaches the block barrier.
+//
+// Measured on B200 at 8192 rows x 1024 / 4096 codes: 16 warps x 4 rows
+// (64 rows per staged codebook) 10.3 / 31.5 us; 8 x 8 11.8 / 37.6 us,
+// 16 x 8 17.0 / 55.3 us, 32 x 2 13.7 / 42.3 us; splitting a row group's
+// codes across 2 or 4 warps with a shared-memory merge of the picks
+// 12.1-13.0 / 47-66 us.
 #ifndef MOSS_DEC_ROWS
 #define MOSS_DEC_ROWS 4
 #endif
-// Codes per warp: all of them.  Splitting them across two or four warps
-// of a row group (with the merge below) measured slower on B200: 12.1 and
-// 13.0 us against 11.7 us at 8192 rows x 1024 codes, 47 and 66 us against
-// 38 us at 4096 codes.
-#ifndef MOSS_DEC_SPLIT
-#define MOSS_DEC_SPLIT 1
-#endif
-constexpr int kDecRows = MOSS_DEC_ROWS;
-constexpr int kDecSplit = MOSS_DEC_SPLIT;
-// 16 warps x 4 rows: 64 rows per staged codebook.  Measured on B200 at
-// 8192 rows x 1024 / 4096 codes: 10.3 / 31.5 us; 8 warps x 8 rows 11.8 /
-// 37.6 us, 16 x 8 17.0 / 55.3 us, 32 x 2 13.7 / 42.3 us.
 #ifndef MOSS_DEC_WARPS
 #define MOSS_DEC_WARPS 16
 #endif
+constexpr int kDecRows = MOSS_DEC_ROWS;
 constexpr int kDecWarps = MOSS_DEC_WARPS;
-constexpr int kDecRowsPerBlock = kDecRows * kDecWarps / kDecSplit;
+constexpr int kDecRowsPerBlock = kDecRows * kDecWarps;
 constexpr int kDecMaxCodes = 4096;  // 36 bytes per code of shared memory
 
 struct Pick32 {
@@ -231,22 +223,6 @@ __device__ __forceinline__ void pick32_push(Pick32& p, float dist, int j) {
   p.nan_i = (is_nan && j < p.nan_i) ? j : p.nan_i;
   p.best_i = better ? j : p.best_i;
   p.best = better ? dist : p.best;
-}
-
-// The warp's pick over all of its lanes (every lane gets it).
-__device__ __forceinline__ Pick32 pick32_allreduce(Pick32 p) {
-#pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, p.best, m);
-    const int oi = __shfl_xor_sync(0xffffffffu, p.best_i, m);
-    const int on = __shfl_xor_sync(0xffffffffu, p.nan_i, m);
-    if (ob < p.best || (ob == p.best && oi < p.best_i)) {
-      p.best = ob;
-      p.best_i = oi;
-    }
-    if (on < p.nan_i) p.nan_i = on;
-  }
-  return p;
 }
 
 __device__ __forceinline__ int pick32_reduce(Pick32 p) {
@@ -271,17 +247,12 @@ __global__ void __launch_bounds__(kDecWarps * 32) lfq_decode_tile_kernel(
   extern __shared__ float4 dec_smem[];
   float4* sbook = dec_smem;                                 // [k][2]
   float* scn = reinterpret_cast<float*>(dec_smem + 2 * k);  // [k]
-  __shared__ Pick32 part[kDecSplit][kDecWarps / kDecSplit][kDecRows];
   for (int i = threadIdx.x; i < 2 * k; i += blockDim.x)
     sbook[i] = reinterpret_cast<const float4*>(book_normed)[i];
   for (int i = threadIdx.x; i < k; i += blockDim.x) scn[i] = code_norm[i];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int kGroups = kDecWarps / kDecSplit;
-  const int group = warp % kGroups, share = warp / kGroups;
   const int64_t rows = b * t;
-  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kGroups + group) * kDecRows;
-  const int j_begin = static_cast<int>(static_cast<int64_t>(k) * share / kDecSplit);
-  const int j_end = static_cast<int>(static_cast<int64_t>(k) * (share + 1) / kDecSplit);
+  const int64_t row0 = (static_cast<int64_t>(blockIdx.x) * kDecWarps + warp) * kDecRows;
   const bool transposed = (b == 1 && t > 1);
   // lane r prepares row r of the warp's group (all lanes run one
   // preparation in parallel), then every lane receives the group's values
@@ -299,8 +270,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) lfq_decode_tile_kernel(
   __syncthreads();
   Pick32 pk[kDecRows];
 #pragma unroll
-  for (int r = 0; r < kDecRows; ++r) pk[r] = Pick32{CUDART_INF_F, j_begin + lane, INT_MAX};
-  for (int j = j_begin + lane; j < j_end; j += 32) {
+  for (int r = 0; r < kDecRows; ++r) pk[r] = Pick32{CUDART_INF_F, lane, INT_MAX};
+  for (int j = lane; j < k; j += 32) {
     const float4 c0 = sbook[2 * j], c1 = sbook[2 * j + 1];
     const float cn = scn[j];
 #pragma unroll
@@ -316,35 +287,20 @@ __global__ void __launch_bounds__(kDecWarps * 32) lfq_decode_tile_kernel(
       pick32_push(pk[r], __fadd_rn(__fsub_rn(nrm[r], dot), cn), j);
     }
   }
+  // every lane gets each row's index; lane r writes row r
+  int mine = 0;
 #pragma unroll
   for (int r = 0; r < kDecRows; ++r) {
-    const Pick32 w = pick32_allreduce(pk[r]);
-    if (lane == 0) part[share][group][r] = w;
+    const int idx = pick32_reduce(pk[r]);
+    mine = lane == r ? idx : mine;
   }
-  __syncthreads();
-  if (share == 0 && lane < kDecRows) {
-    const int r = lane;
-    Pick32 m = part[0][group][r];
-    // later shares hold higher codes: a strictly smaller distance wins, an
-    // equal one keeps the earlier (lower) index
-#pragma unroll
-    for (int q = 1; q < kDecSplit; ++q) {
-      const Pick32 o = part[q][group][r];
-      if (o.best < m.best) {
-        m.best = o.best;
-        m.best_i = o.best_i;
-      }
-      if (o.nan_i < m.nan_i) m.nan_i = o.nan_i;
-    }
-    const int idx = m.nan_i != INT_MAX ? m.nan_i : m.best_i;
-    const int64_t row = row0 + r;
-    if (row < rows) {
-      indices[row] = idx;
-      const float4* src = reinterpret_cast<const float4*>(weight + static_cast<int64_t>(idx) * 8);
-      float4* dst = reinterpret_cast<float4*>(out + row * 8);
-      dst[0] = src[0];
-      dst[1] = src[1];
-    }
+  const int64_t row = row0 + lane;
+  if (lane < kDecRows && row < rows) {
+    indices[row] = mine;
+    const float4* src = reinterpret_cast<const float4*>(weight + static_cast<int64_t>(mine) * 8);
+    float4* dst = reinterpret_cast<float4*>(out + row * 8);
+    dst[0] = src[0];
+    dst[1] = src[1];
   }
 }
 
