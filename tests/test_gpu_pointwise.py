@@ -166,12 +166,15 @@ def test_silu_gate_config3(moss, cuda_device):
     assert bf16_ulp_diff(y[:, sub].float().cpu().numpy(), oy) <= 1
 
 
+@pytest.mark.parametrize("copies", [1, 64])
 @pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
-def test_activation_exhaustive_bf16(moss, cuda_device, act):
-    """Every one of the 65,536 bf16 bit patterns as the gate input (up = 1 and
-    up = a random bf16), with and without a bias: bit-exact against torch."""
+def test_activation_exhaustive_bf16(moss, cuda_device, act, copies):
+    """Every one of the 65,536 bf16 bit patterns as the gate input (up = a
+    random bf16), with and without a bias: bit-exact against torch.  One
+    copy (65,536 outputs) takes the register kernel; 64 copies (2^22
+    outputs) the shared-memory table kernel."""
     bits = torch.arange(65536, dtype=torch.int32).to(torch.int16)
-    gate = bits.view(torch.bfloat16).reshape(-1, 128).to(cuda_device)
+    gate = bits.view(torch.bfloat16).reshape(-1, 128).repeat(copies, 1).to(cuda_device)
     g = torch.Generator().manual_seed(31)
     up = torch.randn(gate.shape, generator=g).to(cuda_device, torch.bfloat16)
     x = torch.cat([gate, up], dim=1)
