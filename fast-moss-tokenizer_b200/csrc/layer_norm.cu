@@ -123,6 +123,17 @@ __device__ __forceinline__ float scale_add1(float x, float u, float s) {
   return __fadd_rn(x, __fmul_rn(u, s));
 }
 
+// gamma * (rstd * (x - mean)) + beta with gamma and beta already loaded
+// (the same operations as ln_out's first case).
+__device__ __forceinline__ float4 ln_out_gb(float4 v, float mean, float rstd, float4 g, float4 b) {
+  float4 o;
+  o.x = __fmaf_rn(g.x, __fmul_rn(rstd, __fsub_rn(v.x, mean)), b.x);
+  o.y = __fmaf_rn(g.y, __fmul_rn(rstd, __fsub_rn(v.y, mean)), b.y);
+  o.z = __fmaf_rn(g.z, __fmul_rn(rstd, __fsub_rn(v.z, mean)), b.z);
+  o.w = __fmaf_rn(g.w, __fmul_rn(rstd, __fsub_rn(v.w, mean)), b.w);
+  return o;
+}
+
 __device__ __forceinline__ float4 ln_out(float4 v, float mean, float rstd, const float* gamma,
                                          const float* beta, int i) {
   float4 o;
@@ -173,14 +184,23 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
   const int nvec = n >> 2;
   const int64_t base4 = row * nvec;
 
-  // Issue every load of the row before any arithmetic.
-  float4 val[NVT], upd[NVT];
+  // Issue every load of the row, and of the affine parameters, before any
+  // arithmetic.
+  const bool gb = gamma != nullptr && beta != nullptr;
+  float4 val[NVT], upd[NVT], sv[NVT], gv[NVT], bv[NVT];
 #pragma unroll
   for (int m = 0; m < NVT; ++m) {
     const int i = tid + 128 * m;
     if (i < nvec) {
       val[m] = load4<XDT>(x, base4 + i, x_vec);
-      if constexpr (HAS_U) upd[m] = load4<UDT>(u, base4 + i, u_vec);
+      if constexpr (HAS_U) {
+        upd[m] = load4<UDT>(u, base4 + i, u_vec);
+        sv[m] = reinterpret_cast<const float4*>(scale)[i];
+      }
+      if (gb) {
+        gv[m] = reinterpret_cast<const float4*>(gamma)[i];
+        bv[m] = reinterpret_cast<const float4*>(beta)[i];
+      }
     }
   }
   Welford w = {0.0f, 0.0f, 0.0f};
@@ -189,7 +209,7 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
     const int i = tid + 128 * m;
     if (i < nvec) {
       if constexpr (HAS_U) {
-        const float4 s = reinterpret_cast<const float4*>(scale)[i];
+        const float4 s = sv[m];
         val[m].x = scale_add1(val[m].x, upd[m].x, s.x);
         val[m].y = scale_add1(val[m].y, upd[m].y, s.y);
         val[m].z = scale_add1(val[m].z, upd[m].z, s.z);
@@ -252,7 +272,8 @@ __global__ void __launch_bounds__(128) residual_ln_kernel(
   for (int m = 0; m < NVT; ++m) {
     const int i = tid + 128 * m;
     if (i < nvec) {
-      const float4 o = ln_out(val[m], mean, rstd, gamma, beta, i);
+      const float4 o = gb ? ln_out_gb(val[m], mean, rstd, gv[m], bv[m])
+                          : ln_out(val[m], mean, rstd, gamma, beta, i);
       if (out_bf16) {
         // the consumer's cast: round to nearest even, as torch's .to(bfloat16)
         reinterpret_cast<uint2*>(normed_out)[base4 + i] = make_uint2(
