@@ -180,7 +180,7 @@ MOSS_API int moss_rope_kv(const void* q, const void* k, const void* v, int dtype
  * w_image: W pre-packed by the host into blocks of 32 rows x 64 columns in
  * the MMA's no-swizzle K-major core-matrix order ([3h*2][k/64][4][8][8][8]
  * bf16: row group, k core, row, element).  bias: [3*h*64] bf16 or NULL.
- * k must be a multiple of 64 and at most 1792; buffers 16-byte aligned.
+ * k must be a multiple of 64 and at most 1536; buffers 16-byte aligned.
  * The dot products are summed in this kernel's order, not cuBLAS's, so a
  * projection output can differ from F.linear's by the rounding of a
  * different sum.  Built for skinny inputs (one 32-row tile of tokens per
