@@ -13,6 +13,9 @@
 // outputs from 16-byte loads of the gate half, the up half and the bias;
 // the bias adds and the gating product run as packed bf16 operations,
 // which give the same bits as the float32 op followed by the bf16 rounding.
+#include <atomic>
+#include <mutex>
+
 #include "pipeline.cuh"
 
 namespace moss {
@@ -261,16 +264,27 @@ __global__ void act_lut_kernel() {
   g_act_lut[2 * 65536 + h] = f32_to_bf16_bits(activation_exact<MOSS_ACT_GELU_TANH>(v));
 }
 
-// Builds the tables on the current device at its first use, on `s` (stream
-// order makes them visible to the kernels launched after it).
-static void ensure_act_lut(cudaStream_t s) {
-  static bool ready[kMaxDevices] = {};
+// True once the tables of the current device are built.  The first call
+// outside a graph capture builds them on `s` and waits for the build, so
+// kernels on every stream (and in graphs captured later) find them written.
+// While `s` is being captured nothing may be waited for, and a build
+// recorded into the graph would run only at its replay: the caller then
+// takes the register kernel, which gives the same bits.
+static bool act_lut_ready(cudaStream_t s) {
+  static std::atomic<bool> ready[kMaxDevices];
+  static std::mutex build;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) dev = 0;
-  if (!ready[dev]) {
-    act_lut_kernel<<<65536 / 256, 256, 0, s>>>();
-    ready[dev] = true;
-  }
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+  if (ready[dev].load(std::memory_order_acquire)) return true;
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &capture) != cudaSuccess || capture != cudaStreamCaptureStatusNone)
+    return false;
+  std::lock_guard<std::mutex> lock(build);
+  if (ready[dev].load(std::memory_order_acquire)) return true;
+  act_lut_kernel<<<65536 / 256, 256, 0, s>>>();
+  if (cudaPeekAtLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) return false;
+  ready[dev].store(true, std::memory_order_release);
+  return true;
 }
 
 // Streaming path (bf16, rows of at most kStageBytes): one CTA per SM.  A
@@ -476,8 +490,7 @@ static void launch_gated(const void* x, const void* bias, void* y, int dtype, in
                          int64_t width, int64_t out_w, bool vec, cudaStream_t s) {
   const int sms = sm_count();
   if (vec && width * 2 <= gstream::kStageBytes && rows < 0x7fffffffLL &&
-      rows * out_w >= kStreamMinOutputs) {
-    ensure_act_lut(s);
+      rows * out_w >= kStreamMinOutputs && act_lut_ready(s)) {
     gstream::Args a{};
     a.x = static_cast<const uint16_t*>(x);
     a.bias = static_cast<const uint16_t*>(bias);
