@@ -16,8 +16,11 @@
  *     -> RuntimeError, the same exception classes the reference raises.
  *   - Calls on distinct streams are independent.  The only state shared
  *     between calls is read-only after its first use on a device: the SM
- *     count and the bf16 activation tables of moss_gated_act (built by one
- *     kernel on the caller's stream at the first bf16 call on a device).
+ *     count and the bf16 activation tables of moss_gated_act.  The tables
+ *     are built by one kernel at the first moss_gated_act call on a device
+ *     that is large enough to use them (2^22 outputs) and is not inside a
+ *     stream capture; that call waits for the caller's stream once.  Calls
+ *     captured before then use a kernel without the tables (same results).
  *
  * Dtype codes: MOSS_F32 = float32, MOSS_BF16 = bfloat16 (stored as uint16).
  *
