@@ -96,7 +96,9 @@ class ResidualVectorQuantizer:
         `depth` device buffer sets in rotation (events order every reuse).
         Work is queued on the current stream's device; on return the current
         stream waits for the last copy out (synchronize before reading the
-        host outputs).
+        host outputs).  The copies overlap the quantizer only when every
+        host tensor is pinned and contiguous: torch stages any other copy
+        through pageable memory, which serialises it with the host.
         """
         if not len(xs) == len(codes_out) == len(recon_out):
             raise ValueError("xs, codes_out and recon_out must have the same length")
