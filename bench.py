@@ -549,6 +549,51 @@ def _qkv_kernel_line(torch, dev, cfg, weights):
     return res
 
 
+def _attention_kernel_line(torch, dev, cfg):
+    """The stack's attention over its history ring, per layer: the owned
+    kernel (moss_history_attention) against the SDPA call it replaces
+    (memory-efficient backend, additive mask built once per chunk), over 24
+    layers' rings in turn, graph-timed.  `gbs` counts the bytes the kernel
+    must move: keys and values of every slot, queries, slot positions and
+    the output."""
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    from fast_moss_b200.transformer import StreamHistory, additive_mask
+    from fast_moss_b200.v2_pointwise import history_attention
+
+    h, t, dh = cfg.heads, cfg.chunk_tokens, cfg.head_dim
+    res = {}
+    for streams in (1, 64):
+        hist = StreamHistory(cfg, streams, dev)
+        g = torch.Generator(device=dev).manual_seed(6)
+        for kc, vc in zip(hist.keys, hist.values):
+            kc.normal_(generator=g)
+            vc.normal_(generator=g)
+        for _ in range(cfg.history_slots // t + 2):  # every slot holds a token
+            offset = hist.pos.clone()
+            _, _, mask = hist.advance(t)
+            hist.pos.add_(t)
+        amask = additive_mask(mask, torch.bfloat16)
+        q = torch.randn(streams, h, t, dh, device=dev, generator=g).to(torch.bfloat16)
+        layers = list(zip(hist.keys, hist.values))
+
+        def owned(layer, _handle):
+            history_attention(q, layer[0], layer[1], hist.slot_pos, offset, cfg.context)
+
+        def sdpa(layer, _handle):
+            with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
+                torch.nn.functional.scaled_dot_product_attention(q, layer[0], layer[1],
+                                                                 attn_mask=amask)
+
+        to = time_launches(torch, owned, layers, launches=48, replays=5)
+        ts = time_launches(torch, sdpa, layers, launches=48, replays=5)
+        n = cfg.history_slots
+        nbytes = streams * (h * n * dh * 2 * 2 + 2 * h * t * dh * 2 + n * 8 + 8)
+        res[f"streams_{streams}"] = {"us_owned": to * 1e6, "us_sdpa": ts * 1e6,
+                                     "owned_gbs": nbytes / to / 1e9, "bytes": nbytes}
+        del hist, layers
+    return res
+
+
 def stack_lines(torch, dev, cpu=True):
     """The codec's streaming transformer stack (24 layers, hidden 1280, 20
     heads, feed-forward 5120, FP32 weights seeded 2, bf16 GEMMs) over 125
@@ -566,14 +611,22 @@ def stack_lines(torch, dev, cpu=True):
     out = {"workload": "streaming stack: 24 layers, hidden 1280, 20 heads, ffn 5120, "
                        "context 250 tokens, 4 tokens per 80 ms chunk, 125 chunks per stream",
            "metric": "audio-sec/sec (RTF x streams)", "dtype": "bf16 GEMMs, f32 residual"}
-    for fused in (False, True):
-        stack = StreamingTransformer(cfg, weights, dev, fused_qkv=fused)
-        dst = out if not fused else out.setdefault("fused_qkv", {
-            "what": "qkv Linear + rotary + history writes as one tcgen05 kernel (moss_qkv_rope)"})
+    variants = (
+        (None, {}),
+        ("fused_qkv", {"fused_qkv": True}),
+        ("fused_qkv_history_attention", {"fused_qkv": True, "history_attention": True}))
+    for key, opts in variants:
+        stack = StreamingTransformer(cfg, weights, dev, **opts)
+        dst = out if key is None else out.setdefault(key, {"what": {
+            "fused_qkv": "qkv Linear + rotary + history writes as one tcgen05 kernel "
+                         "(moss_qkv_rope; up to 32 token rows)",
+            "fused_qkv_history_attention": "moss_qkv_rope, and the attention over the history "
+                                           "ring as moss_history_attention instead of SDPA"}[key]})
         for streams in (1, 64):
             dst[f"streams_{streams}"] = _stack_rate(torch, dev, cfg, stack, streams, chunks)
         del stack
     out["qkv_kernel"] = _qkv_kernel_line(torch, dev, cfg, weights)
+    out["attention_kernel"] = _attention_kernel_line(torch, dev, cfg)
     torch.cuda.synchronize()
     if cpu:
         from oracle.stack import EagerStack

@@ -1,0 +1,246 @@
+// Attention of a chunk's queries over a streaming history ring (bf16 in and
+// out, FP32 arithmetic).
+//
+// The reference's streaming layer calls the upstream attention module with
+// SDPA (the only validated backend, fast_moss/v2_runtime.py:40-41) over a
+// bounded history that its StreamingCodec keeps at stable addresses
+// (fast_moss/streaming.py:68-79); the patched layer calls it at
+// fast_moss/v2_runtime.py:254-262.  Per stream s, head h and query t of the
+// chunk (absolute position pos[s] + t), the keys are the ring's slots j with
+//   0 <= slot_pos[s, j] <= pos[s] + t   and   slot_pos[s, j] > pos[s] + t - context
+// (the boolean mask the history builds), and
+//   out[s, t, h, :] = sum_j softmax_j(scale * q[s, h, t, :] . k[s, h, j, :]) v[s, h, j, :]
+// with the softmax over the attended keys.
+//
+// One CTA per (stream, head).  All threads issue 16-byte cp.async loads of
+// the head's whole K and V blocks at once (contiguous in the [S, H, N, 64]
+// ring), K first: K rows land XOR-swizzled by 16-byte chunk so that the
+// per-key dot products read shared memory without bank conflicts.  Thread j
+// scores key j for every query; the softmax is a block reduction in a fixed
+// order; for P.V each warp takes a strided eighth of the keys with lane l
+// holding dims 2l and 2l+1, and the eight partial sums are added in warp
+// order.  Everything is FP32 (expf, IEEE division), rounded once to bf16.
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace moss {
+namespace hattn {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kDim = 64;
+constexpr int kMaxQueries = 8;
+constexpr int kMaxKeys = 512;
+constexpr int kKeysPerThread = kMaxKeys / kThreads;
+
+struct Args {
+  const uint16_t* q;         // [S, H, T, 64]
+  const uint16_t* k;         // [S, H, N, 64]
+  const uint16_t* v;         // [S, H, N, 64]
+  const int64_t* slot_pos;   // [S, N]
+  const int64_t* pos;        // [S]
+  uint16_t* out;             // [S, T, H, 64]
+  int64_t context;
+  float scale;
+  int h, t, n;
+};
+
+// Rows of the weight array are padded to 4 floats (16 bytes).
+__host__ __device__ constexpr int padded_keys(int n) { return (n + 3) & ~3; }
+
+__host__ __device__ constexpr size_t smem_bytes(int t, int n) {
+  return static_cast<size_t>(n) * kDim * 2 * 2            // K and V
+         + static_cast<size_t>(t) * kDim * 4              // q (float)
+         + static_cast<size_t>(t) * padded_keys(n) * 4    // weights
+         + static_cast<size_t>(kWarps) * t * kDim * 4     // P.V partial sums
+         + static_cast<size_t>(kWarps) * kMaxQueries * 4;  // reductions
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+template <int T>
+__global__ void __launch_bounds__(kThreads) history_attn_kernel(const Args a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  const int n = a.n;
+  unsigned char* ks = sm;                                        // [n][128 B], swizzled
+  unsigned char* vs = ks + static_cast<size_t>(n) * kDim * 2;    // [n][128 B]
+  float* qs = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [T][64]
+  const int np = padded_keys(n);
+  float* ps = qs + T * kDim;                                     // [T][np]
+  float* part = ps + T * np;                                     // [warps][T][64]
+  float* red = part + kWarps * T * kDim;                         // [warps][kMaxQueries]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t sh = blockIdx.x;           // s * H + h
+  const int64_t s = sh / a.h;
+  const int hh = static_cast<int>(sh - s * a.h);
+  const char* kg = reinterpret_cast<const char*>(a.k + sh * n * kDim);
+  const char* vg = reinterpret_cast<const char*>(a.v + sh * n * kDim);
+  const int chunks = n * (kDim * 2 / 16);  // 8 chunks of 16 bytes per row
+  for (int c = tid; c < chunks; c += kThreads) {
+    const int row = c >> 3, col = c & 7;
+    cp_async16(smem_u32(ks + row * 128 + ((col ^ (row & 7)) << 4)), kg + static_cast<size_t>(c) * 16);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int c = tid; c < chunks; c += kThreads) cp_async16(smem_u32(vs + c * 16), vg + static_cast<size_t>(c) * 16);
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const uint16_t* qg = a.q + sh * T * kDim;
+  for (int i = tid; i < T * kDim; i += kThreads) qs[i] = bf16_bits_to_f32(qg[i]);
+  const int64_t p0 = a.pos[s];
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();
+
+  // ---- scores: thread tid takes keys tid and tid + 256
+  float sc[kKeysPerThread][T];
+#pragma unroll
+  for (int m = 0; m < kKeysPerThread; ++m) {
+    const int j = tid + m * kThreads;
+#pragma unroll
+    for (int t = 0; t < T; ++t) sc[m][t] = -CUDART_INF_F;
+    if (j < n) {
+      float acc[T];
+#pragma unroll
+      for (int t = 0; t < T; ++t) acc[t] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(ks + j * 128 + ((c ^ (j & 7)) << 4));
+        float kv[8];
+        unpack_bf16x8(raw, kv);
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[t] = __fmaf_rn(qs[t * kDim + c * 8 + e], kv[e], acc[t]);
+        }
+      }
+      const int64_t held = a.slot_pos[s * n + j];
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const int64_t qp = p0 + t;
+        const bool on = held >= 0 && held <= qp && held > qp - a.context;
+        sc[m][t] = on ? __fmul_rn(acc[t], a.scale) : -CUDART_INF_F;
+      }
+    }
+  }
+  // ---- softmax: block maxima, then exponentials and block sums
+  float mx[T];
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    float v = sc[0][t];
+#pragma unroll
+    for (int m = 1; m < kKeysPerThread; ++m) v = fmaxf(v, sc[m][t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[warp * kMaxQueries + t] = v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    float v = red[t];
+    for (int w = 1; w < kWarps; ++w) v = fmaxf(v, red[w * kMaxQueries + t]);
+    mx[t] = v;
+  }
+  __syncthreads();  // every thread has read the maxima before the sums reuse `red`
+  float l[T];
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) {
+      const int j = tid + m * kThreads;
+      // a query with no attended key keeps weights 0 (its output is NaN, as SDPA's)
+      const float e = (j < n && mx[t] != -CUDART_INF_F) ? expf(__fsub_rn(sc[m][t], mx[t])) : 0.0f;
+      if (j < n) ps[t * np + j] = e;
+      sum = __fadd_rn(sum, e);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    if (lane == 0) red[warp * kMaxQueries + t] = sum;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // V, the weights and the partial sums are visible
+#pragma unroll
+  for (int t = 0; t < T; ++t) {
+    float v = red[t];
+    for (int w = 1; w < kWarps; ++w) v = __fadd_rn(v, red[w * kMaxQueries + t]);
+    l[t] = v;
+  }
+
+  // ---- P.V: warp w takes keys w, w + 8, ...; lane l dims 2l, 2l + 1
+  float o0[T], o1[T];
+#pragma unroll
+  for (int t = 0; t < T; ++t) o0[t] = o1[t] = 0.0f;
+  for (int j = warp; j < n; j += kWarps) {
+    const uint32_t raw = *reinterpret_cast<const uint32_t*>(vs + j * 128 + lane * 4);
+    const float v0 = __uint_as_float(raw << 16), v1 = __uint_as_float(raw & 0xffff0000u);
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      const float p = ps[t * np + j];
+      o0[t] = __fmaf_rn(p, v0, o0[t]);
+      o1[t] = __fmaf_rn(p, v1, o1[t]);
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < T; ++t)
+    *reinterpret_cast<float2*>(part + (warp * T + t) * kDim + 2 * lane) = make_float2(o0[t], o1[t]);
+  __syncthreads();
+  for (int i = tid; i < T * kDim; i += kThreads) {
+    const int t = i / kDim, d = i - t * kDim;
+    float acc = part[t * kDim + d];
+    for (int w = 1; w < kWarps; ++w) acc = __fadd_rn(acc, part[(w * T + t) * kDim + d]);
+    float lt = l[0];
+#pragma unroll
+    for (int u = 1; u < T; ++u) lt = t == u ? l[u] : lt;
+    a.out[((s * T + t) * a.h + hh) * kDim + d] = f32_to_bf16_bits(__fdiv_rn(acc, lt));
+  }
+}
+
+}  // namespace hattn
+}  // namespace moss
+
+using namespace moss;
+
+extern "C" int moss_history_attention(const void* q, const void* k_cache, const void* v_cache,
+                                      const int64_t* slot_pos, const int64_t* pos, int64_t s,
+                                      int64_t h, int64_t t, int64_t n, int64_t d, int64_t context,
+                                      float scale, void* out, void* stream) {
+  using namespace hattn;
+  const char* name = "moss_history_attention";
+  if (s < 0 || h < 1 || t < 1 || n < 1 || context < 1)
+    return fail(MOSS_ERR_VALUE, "%s: need streams >= 0, heads, queries, slots and context >= 1", name);
+  if (d != kDim) return fail(MOSS_ERR_UNSUPPORTED, "%s: only heads of 64 are supported", name);
+  if (t > kMaxQueries) return fail(MOSS_ERR_UNSUPPORTED, "%s: at most %d queries per stream", name, kMaxQueries);
+  if (n > kMaxKeys) return fail(MOSS_ERR_UNSUPPORTED, "%s: at most %d history slots", name, kMaxKeys);
+  if (s * h > 0x7fffffffLL) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many streams x heads", name);
+  if (s == 0) return MOSS_OK;
+  if (!q || !k_cache || !v_cache || !slot_pos || !pos || !out)
+    return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  if (!aligned16(k_cache) || !aligned16(v_cache))
+    return fail(MOSS_ERR_VALUE, "%s: the history rings must be 16-byte aligned", name);
+  Args a{static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
+         static_cast<const uint16_t*>(v_cache), slot_pos, pos, static_cast<uint16_t*>(out),
+         context, scale, static_cast<int>(h), static_cast<int>(t), static_cast<int>(n)};
+  const size_t shmem = smem_bytes(static_cast<int>(t), static_cast<int>(n));
+  const unsigned grid = static_cast<unsigned>(s * h);
+  cudaStream_t st = as_stream(stream);
+#define MOSS_HATTN(T)                                                                   \
+  case T: {                                                                             \
+    static bool attr_done[kMaxDevices] = {};                                            \
+    allow_dynamic_smem(history_attn_kernel<T>, shmem_max, attr_done);                   \
+    history_attn_kernel<T><<<grid, kThreads, shmem, st>>>(a);                           \
+    break;                                                                              \
+  }
+  const size_t shmem_max = smem_bytes(kMaxQueries, kMaxKeys);
+  switch (t) {
+    MOSS_HATTN(1) MOSS_HATTN(2) MOSS_HATTN(3) MOSS_HATTN(4)
+    MOSS_HATTN(5) MOSS_HATTN(6) MOSS_HATTN(7) MOSS_HATTN(8)
+    default: break;
+  }
+#undef MOSS_HATTN
+  return launch_status(name);
+}

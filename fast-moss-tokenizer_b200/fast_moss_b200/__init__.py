@@ -18,6 +18,7 @@ from .quantizer_prepare import prepare
 from .rvq import ResidualVectorQuantizer
 from .v2_pointwise import (
     gated_activation,
+    history_attention,
     layer_norm,
     pack_qkv_weight,
     qkv_rope,
@@ -43,6 +44,7 @@ __all__ = [
     "layer_norm",
     "residual_layer_norm",
     "gated_activation",
+    "history_attention",
     "select",
     "decode_latents",
     "prepare",

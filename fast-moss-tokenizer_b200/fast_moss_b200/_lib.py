@@ -56,6 +56,8 @@ _SIGNATURES = {
                           _i64, _i64, _pi64, _pi64, _pi64, _vp]),
     "moss_qkv_rope": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i, _f, _vp, _vp, _vp, _vp,
                            _i64, _vp]),
+    "moss_history_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
+                                    _f, _vp, _vp]),
     "moss_gated_act": (_i, [_vp, _vp, _vp, _i, _i64, _i64, _i, _i, _vp]),
     "moss_lfq_prepare": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "moss_lfq_select": (_i, [_vp, _vp, _vp, _vp, _vp, _pi64, _i64, _i64, _i64, _i64, _i, _vp, _vp,

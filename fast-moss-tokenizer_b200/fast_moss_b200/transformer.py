@@ -49,6 +49,7 @@ from torch.nn.attention import SDPBackend, sdpa_kernel
 from .graphs import GraphedCallable
 from .v2_pointwise import (
     gated_activation,
+    history_attention,
     layer_norm,
     pack_qkv_weight,
     qkv_rope,
@@ -204,7 +205,7 @@ class StreamingTransformer:
     """The stack: FP32 parameters on one CUDA device, bf16 GEMM weights cached
     once (the reference's cached Linear, fast_moss/v2_runtime.py:77-106)."""
 
-    def __init__(self, cfg, weights, device, *, fused_qkv=False):
+    def __init__(self, cfg, weights, device, *, fused_qkv=False, history_attention=False):
         device = torch.device(device)
         if device.type != "cuda":
             raise ValueError("StreamingTransformer runs on a CUDA device")
@@ -223,6 +224,13 @@ class StreamingTransformer:
         self.fused_qkv = bool(fused_qkv)
         if self.fused_qkv and cfg.head_dim != 64:
             raise ValueError("the fused qkv projection needs heads of 64")
+        # the attention as moss_history_attention (FP32 softmax and P.V over
+        # the ring, mask from the slot positions) instead of SDPA
+        self.history_attention = bool(history_attention)
+        if self.history_attention and (cfg.head_dim != 64 or cfg.chunk_tokens > 8
+                                       or cfg.history_slots > 512):
+            raise ValueError("the history attention kernel needs heads of 64, at most 8 "
+                             "tokens per chunk and at most 512 history slots")
 
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
@@ -238,7 +246,8 @@ class StreamingTransformer:
         h, dh = cfg.heads, cfg.head_dim
         offset = hist.pos  # position of the chunk's first token (advanced at the end)
         _, slots, mask = hist.advance(t)
-        mask = additive_mask(mask, torch.bfloat16)
+        if not self.history_attention:
+            mask = additive_mask(mask, torch.bfloat16)
         first = self.layers[0]
         x = x.contiguous()
         bf16 = torch.bfloat16
@@ -254,10 +263,15 @@ class StreamingTransformer:
                 q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
                             qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
                             hist.keys[i], hist.values[i])
-            with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
-                a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
-                                                   attn_mask=mask)
-            u = F.linear(a.transpose(1, 2).reshape(s, t, d), p["out_w16"], p["out_b16"])
+            if self.history_attention:
+                a = history_attention(q, hist.keys[i], hist.values[i], hist.slot_pos, offset,
+                                      cfg.context).view(s, t, d)
+            else:
+                with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
+                    a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
+                                                       attn_mask=mask)
+                a = a.transpose(1, 2).reshape(s, t, d)
+            u = F.linear(a, p["out_w16"], p["out_b16"])
             x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps,
                                             out_dtype=bf16)
             f = F.linear(normed, p["ffn1_w16"])

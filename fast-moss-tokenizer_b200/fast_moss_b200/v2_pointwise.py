@@ -151,6 +151,57 @@ def rope_kv(q, k, v, offset, max_period, slots, k_cache, v_cache):
     return oq
 
 
+def history_attention(q, k_cache, v_cache, slot_pos, pos, context, scale=None, out=None):
+    """Attention of a chunk's queries over a streaming history ring.
+
+    q: bf16 [S, H, T, 64] (T <= 8); k_cache, v_cache: contiguous bf16
+    [S, H, N, 64] rings (N <= 512); slot_pos: int64 [S, N], the position held
+    by each slot (-1 = empty); pos: int64 [S], the position of the chunk's
+    first token.  Query t attends to the slots holding positions in
+    (pos + t - context, pos + t] -- the mask of the streaming history -- with
+    scale 1/sqrt(64) by default.  Returns bf16 [S, T, H, 64] (or fills
+    `out`), the layout the output projection reads.  Replaces the SDPA call
+    over the bounded history (fast_moss/v2_runtime.py:40-41, :254-262;
+    fast_moss/streaming.py:68-79); FP32 arithmetic with one bf16 rounding.
+    """
+    if q.ndim != 4 or k_cache.ndim != 4:
+        raise ValueError("Expected q [S, H, T, D] and caches [S, H, N, D]")
+    s, h, t, d = q.shape
+    n = k_cache.shape[2]
+    if (
+        q.dtype != torch.bfloat16
+        or k_cache.dtype != torch.bfloat16
+        or v_cache.dtype != torch.bfloat16
+        or not q.is_cuda
+        or any(x.device != q.device for x in (k_cache, v_cache, slot_pos, pos))
+        or k_cache.shape[:2] != (s, h)
+        or k_cache.shape[3] != d
+        or v_cache.shape != k_cache.shape
+        or not k_cache.is_contiguous()
+        or not v_cache.is_contiguous()
+        or slot_pos.shape != (s, n)
+        or slot_pos.dtype != torch.int64
+        or pos.shape != (s,)
+        or pos.dtype != torch.int64
+    ):
+        raise ValueError("Expected same-device bf16 q and contiguous [S,H,N,D] bf16 caches, "
+                         "int64 [S,N] slot positions and int64 [S] chunk positions")
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((s, t, h, d), device=q.device, dtype=torch.bfloat16)
+    elif out.shape != (s, t, h, d) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [S, T, H, D] tensor")
+    q = q.contiguous()
+    slot_pos = slot_pos.contiguous()
+    pos = pos.contiguous()
+    with torch.cuda.device(q.device):
+        _lib.call("moss_history_attention", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                  slot_pos.data_ptr(), pos.data_ptr(), s, h, t, n, d, int(context), float(scale),
+                  out.data_ptr(), _stream(q.device))
+    return out
+
+
 def pack_qkv_weight(weight):
     """Packs a bf16 qkv Linear weight [3*H*64, K] (K a multiple of 64) for
     `qkv_rope`: blocks of 32 rows x 64 columns in the tensor cores'

@@ -196,6 +196,29 @@ MOSS_API int moss_qkv_rope(const void* x, const void* w_image, const void* bias,
               void* v_cache, int64_t cache_slots, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Attention of a chunk's queries over a streaming history ring.
+ * Replaces the SDPA call of the streaming layer's attention over its
+ * bounded history (fast_moss/v2_runtime.py:40-41 validates SDPA,
+ * :254-262 calls the attention block; fast_moss/streaming.py:68-79 keeps
+ * the history bounded and at stable addresses).
+ *   query t of stream s sits at position pos[s] + t; it attends to ring slot
+ *   j iff 0 <= slot_pos[s, j] <= pos[s] + t and slot_pos[s, j] > pos[s] + t
+ *   - context (slot_pos = -1 marks an empty slot);
+ *   out[s, t, h] = sum_j softmax_j(scale * q[s, h, t] . k[s, h, j]) v[s, h, j]
+ * q [s, h, t, 64] bf16 contiguous; k_cache, v_cache [s, h, n, 64] bf16
+ * contiguous and 16-byte aligned; slot_pos int64 [s, n]; pos int64 [s];
+ * out [s, t, h, 64] bf16 (the layout the output projection reads).
+ * d must be 64, 1 <= t <= 8, 1 <= n <= 512.  FP32 arithmetic throughout,
+ * one bf16 rounding, so results can differ from SDPA's (which rounds the
+ * weights to bf16 before P.V) by a bf16 unit.  A query with no attended
+ * slot gets NaN.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_history_attention(const void* q, const void* k_cache, const void* v_cache,
+              const int64_t* slot_pos, const int64_t* pos, int64_t s, int64_t h,
+              int64_t t, int64_t n, int64_t d, int64_t context, float scale, void* out,
+              void* stream);
+
+/* ---------------------------------------------------------------------------
  * Bias + gated activation, bf16 or float32 in and out.
  * No kernel in the reference (its FFN activation is upstream model code);
  * this is the eager-PyTorch chain it replaces, one rounding per torch op:
