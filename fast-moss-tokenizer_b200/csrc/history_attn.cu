@@ -20,6 +20,9 @@
 // order; for P.V each warp takes a strided eighth of the keys with lane l
 // holding dims 2l and 2l+1, and the eight partial sums are added in warp
 // order.  Everything is FP32 (expf, IEEE division), rounded once to bf16.
+// The weights and the partial sums reuse K's shared memory once the scores
+// are formed, so that three CTAs fit on an SM (registers capped to match):
+// one CTA's loads then overlap the others' arithmetic.
 #include <math_constants.h>
 
 #include "common.cuh"
@@ -49,12 +52,19 @@ struct Args {
 // Rows of the weight array are padded to 4 floats (16 bytes).
 __host__ __device__ constexpr int padded_keys(int n) { return (n + 3) & ~3; }
 
+// Shared memory: region A holds K while the scores are formed, then the
+// weights [t][padded n] and the P.V partial sums [warps][t][64]; then V,
+// q (float) and the reduction slots.
+__host__ __device__ constexpr size_t region_a(int t, int n) {
+  return static_cast<size_t>(n) * kDim * 2 >
+                 static_cast<size_t>(t) * (padded_keys(n) + kWarps * kDim) * 4
+             ? static_cast<size_t>(n) * kDim * 2
+             : static_cast<size_t>(t) * (padded_keys(n) + kWarps * kDim) * 4;
+}
+
 __host__ __device__ constexpr size_t smem_bytes(int t, int n) {
-  return static_cast<size_t>(n) * kDim * 2 * 2            // K and V
-         + static_cast<size_t>(t) * kDim * 4              // q (float)
-         + static_cast<size_t>(t) * padded_keys(n) * 4    // weights
-         + static_cast<size_t>(kWarps) * t * kDim * 4     // P.V partial sums
-         + static_cast<size_t>(kWarps) * kMaxQueries * 4;  // reductions
+  return region_a(t, n) + static_cast<size_t>(n) * kDim * 2 +
+         static_cast<size_t>(t) * kDim * 4 + static_cast<size_t>(kWarps) * kMaxQueries * 4;
 }
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
@@ -66,16 +76,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 template <int T>
-__global__ void __launch_bounds__(kThreads) history_attn_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, 3) history_attn_kernel(const Args a) {
   extern __shared__ __align__(16) unsigned char sm[];
   const int n = a.n;
-  unsigned char* ks = sm;                                        // [n][128 B], swizzled
-  unsigned char* vs = ks + static_cast<size_t>(n) * kDim * 2;    // [n][128 B]
-  float* qs = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [T][64]
   const int np = padded_keys(n);
-  float* ps = qs + T * kDim;                                     // [T][np]
+  unsigned char* ks = sm;                                        // [n][128 B], swizzled
+  float* ps = reinterpret_cast<float*>(sm);                      // [T][np] (after the scores)
   float* part = ps + T * np;                                     // [warps][T][64]
-  float* red = part + kWarps * T * kDim;                         // [warps][kMaxQueries]
+  unsigned char* vs = sm + region_a(T, n);                       // [n][128 B]
+  float* qs = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [T][64]
+  float* red = qs + T * kDim;                                    // [warps][kMaxQueries]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t sh = blockIdx.x;           // s * H + h
   const int64_t s = sh / a.h;
@@ -114,8 +124,16 @@ __global__ void __launch_bounds__(kThreads) history_attn_kernel(const Args a) {
         unpack_bf16x8(raw, kv);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[t] = __fmaf_rn(qs[t * kDim + c * 8 + e], kv[e], acc[t]);
+          const float4 qa = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8 + 4);
+          acc[t] = __fmaf_rn(qa.x, kv[0], acc[t]);
+          acc[t] = __fmaf_rn(qa.y, kv[1], acc[t]);
+          acc[t] = __fmaf_rn(qa.z, kv[2], acc[t]);
+          acc[t] = __fmaf_rn(qa.w, kv[3], acc[t]);
+          acc[t] = __fmaf_rn(qb.x, kv[4], acc[t]);
+          acc[t] = __fmaf_rn(qb.y, kv[5], acc[t]);
+          acc[t] = __fmaf_rn(qb.z, kv[6], acc[t]);
+          acc[t] = __fmaf_rn(qb.w, kv[7], acc[t]);
         }
       }
       const int64_t held = a.slot_pos[s * n + j];
@@ -145,7 +163,9 @@ __global__ void __launch_bounds__(kThreads) history_attn_kernel(const Args a) {
     for (int w = 1; w < kWarps; ++w) v = fmaxf(v, red[w * kMaxQueries + t]);
     mx[t] = v;
   }
-  __syncthreads();  // every thread has read the maxima before the sums reuse `red`
+  // every thread has read the maxima before the sums reuse `red`, and every
+  // read of K is done before the weights overwrite it
+  __syncthreads();
   float l[T];
 #pragma unroll
   for (int t = 0; t < T; ++t) {
