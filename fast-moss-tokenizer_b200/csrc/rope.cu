@@ -340,6 +340,78 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(RopeKvArgs ka) {
   }
 }
 
+// Vector form of rope_kv_kernel for rows that are 16-byte vectors (innermost
+// stride 1, aligned): one thread per 16-byte item of q, k and v (one batch
+// index, head, time step and VW elements), its VW/2 (c, s) pairs evaluated
+// by the thread with fill_phase's arithmetic.  Enough threads to fill the
+// device at a few tokens per batch index, where the tile kernel above has
+// one CTA per batch index.
+template <int DT>
+__global__ void __launch_bounds__(256) rope_kv_vec_kernel(RopeKvArgs ka, int64_t items) {
+  constexpr int VW = DT == MOSS_BF16 ? 8 : 4;
+  constexpr int kEs = DT == MOSS_BF16 ? 2 : 4;
+  const RopeArgs& a = ka.r;
+  const int64_t it = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (it >= items) return;
+  const int64_t nvec = a.d / VW;
+  const int64_t vec = it % nvec;
+  int64_t rest = it / nvec;
+  const int64_t ti = rest % a.t;
+  rest /= a.t;
+  const int64_t hi = rest % a.h;
+  const int64_t bi = rest / a.h;
+  const int64_t slot = ka.slots[bi * a.t + ti];
+  const char* qp = static_cast<const char*>(a.q) + (bi * a.qs[0] + hi * a.qs[1] + ti * a.qs[2] + vec * VW) * kEs;
+  const char* kp = static_cast<const char*>(a.k) + (bi * a.ks[0] + hi * a.ks[1] + ti * a.ks[2] + vec * VW) * kEs;
+  const char* vp = static_cast<const char*>(ka.v) + (bi * ka.vs[0] + hi * ka.vs[1] + ti * ka.vs[2] + vec * VW) * kEs;
+  const uint4 qraw = *reinterpret_cast<const uint4*>(qp);
+  const uint4 kraw = *reinterpret_cast<const uint4*>(kp);
+  const uint4 vraw = *reinterpret_cast<const uint4*>(vp);
+  const float off = offset_as_float(a.offset, a.offset_dtype, bi);
+  const float ts = __fadd_rn(off, static_cast<float>(ti));
+  float c[VW / 2], sn[VW / 2];
+#pragma unroll
+  for (int p = 0; p < VW / 2; ++p) {
+    const int j = static_cast<int>(vec) * (VW / 2) + p;
+    const float freq = expf(__fmul_rn(static_cast<float>(j), a.coef));
+    const float phase = __fmul_rn(freq, ts);
+    c[p] = cosf(phase);
+    sn[p] = sinf(phase);
+  }
+  float qv[VW], kv[VW], qo[VW], ko[VW];
+  if constexpr (DT == MOSS_BF16) {
+    unpack_bf16x8(qraw, qv);
+    unpack_bf16x8(kraw, kv);
+  } else {
+    qv[0] = __uint_as_float(qraw.x); qv[1] = __uint_as_float(qraw.y);
+    qv[2] = __uint_as_float(qraw.z); qv[3] = __uint_as_float(qraw.w);
+    kv[0] = __uint_as_float(kraw.x); kv[1] = __uint_as_float(kraw.y);
+    kv[2] = __uint_as_float(kraw.z); kv[3] = __uint_as_float(kraw.w);
+  }
+#pragma unroll
+  for (int p = 0; p < VW / 2; ++p) {
+    rotate_pair(qv[2 * p], qv[2 * p + 1], c[p], sn[p], qo[2 * p], qo[2 * p + 1]);
+    rotate_pair(kv[2 * p], kv[2 * p + 1], c[p], sn[p], ko[2 * p], ko[2 * p + 1]);
+  }
+  const int64_t o = ((bi * a.h + hi) * a.t + ti) * a.d + vec * VW;
+  uint4 qw, kw;
+  if constexpr (DT == MOSS_BF16) {
+    qw = pack_bf16x8(qo);
+    kw = pack_bf16x8(ko);
+  } else {
+    qw = make_uint4(__float_as_uint(qo[0]), __float_as_uint(qo[1]), __float_as_uint(qo[2]), __float_as_uint(qo[3]));
+    kw = make_uint4(__float_as_uint(ko[0]), __float_as_uint(ko[1]), __float_as_uint(ko[2]), __float_as_uint(ko[3]));
+  }
+  *reinterpret_cast<uint4*>(static_cast<char*>(a.oq) + o * kEs) = qw;
+  if (slot < 0 || slot >= ka.cache_slots) {
+    record_device_error(MOSS_ERR_VALUE);
+    return;
+  }
+  const int64_t co = ((bi * a.h + hi) * ka.cache_slots + slot) * a.d + vec * VW;
+  *reinterpret_cast<uint4*>(static_cast<char*>(ka.k_cache) + co * kEs) = kw;
+  *reinterpret_cast<uint4*>(static_cast<char*>(ka.v_cache) + co * kEs) = vraw;
+}
+
 // Streaming path for q and k whose rows are contiguous within each head
 // (innermost stride 1, time stride d): one CTA per SM.  A producer thread
 // streams tiles (one batch index, TT time steps, all heads) of q and k into
@@ -785,6 +857,24 @@ extern "C" int moss_rope_kv(const void* q, const void* k, const void* v, int dty
   ka.v = v; ka.slots = slots; ka.k_cache = k_cache; ka.v_cache = v_cache;
   ka.cache_slots = cache_slots;
   const int half = static_cast<int>(d / 2);
+  cudaStream_t s = as_stream(stream);
+  {
+    const int esize = dtype == MOSS_F32 ? 4 : 2;
+    const int vw = dtype == MOSS_F32 ? 4 : 8;
+    bool vec = d % vw == 0 && q_strides[3] == 1 && k_strides[3] == 1 && v_strides[3] == 1 &&
+               aligned16(q) && aligned16(k) && aligned16(v) && aligned16(oq) &&
+               aligned16(k_cache) && aligned16(v_cache);
+    for (int i = 0; i < 3 && vec; ++i)
+      vec = (q_strides[i] * esize) % 16 == 0 && (k_strides[i] * esize) % 16 == 0 &&
+            (v_strides[i] * esize) % 16 == 0;
+    const int64_t items = b * h * t * (d / vw);
+    if (vec && (items + 255) / 256 <= 0x7fffffffLL) {
+      const unsigned grid = static_cast<unsigned>((items + 255) / 256);
+      if (dtype == MOSS_BF16) rope_kv_vec_kernel<MOSS_BF16><<<grid, 256, 0, s>>>(ka, items);
+      else rope_kv_vec_kernel<MOSS_F32><<<grid, 256, 0, s>>>(ka, items);
+      return launch_status(name);
+    }
+  }
   int tt = 256 / half;
   if (tt < 1) tt = 1;
   if (tt > t) tt = static_cast<int>(t);
@@ -794,7 +884,6 @@ extern "C" int moss_rope_kv(const void* q, const void* k, const void* v, int dty
     return fail(MOSS_ERR_UNSUPPORTED, "%s: grid too large", name);
   const unsigned grid = static_cast<unsigned>(b * ntiles);
   const size_t shmem = sizeof(float) * 2 * tt * half;
-  cudaStream_t s = as_stream(stream);
   if (dtype == MOSS_BF16) rope_kv_kernel<MOSS_BF16><<<grid, 256, shmem, s>>>(ka);
   else rope_kv_kernel<MOSS_F32><<<grid, 256, shmem, s>>>(ka);
   return launch_status(name);

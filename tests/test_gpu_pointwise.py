@@ -310,7 +310,8 @@ def _rope_kv_case(cuda_device, dtype, b=3, h=4, t=5, d=64, slots_n=9, seed=31):
     g = torch.Generator().manual_seed(seed)
     qkv = torch.randn(b, t, 3, h, d, generator=g).to(cuda_device, dtype)
     q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))  # strided [b,h,t,d] views
-    offset = torch.tensor([0, 7, 123456][:b], device=cuda_device, dtype=torch.int64)
+    offset = torch.tensor(([0, 7, 123456] + [97 * i for i in range(3, b)])[:b], device=cuda_device,
+                          dtype=torch.int64)
     pos = offset[:, None] + torch.arange(t, device=cuda_device)
     slots = torch.remainder(pos, slots_n)
     k_cache = torch.randn(b, h, slots_n, d, generator=g).to(cuda_device, dtype)
@@ -318,9 +319,15 @@ def _rope_kv_case(cuda_device, dtype, b=3, h=4, t=5, d=64, slots_n=9, seed=31):
     return q, k, v, offset, slots, k_cache, v_cache
 
 
+@pytest.mark.parametrize("shape", [
+    (3, 4, 5, 64, 9),      # 16-byte rows: the vector kernel
+    (64, 20, 4, 64, 253),  # the stack's 64 batched streams
+    (3, 4, 5, 6, 9),       # rows that are not 16-byte vectors: the tile kernel
+])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_rope_kv_matches_rope_and_scatter(moss, cuda_device, dtype):
-    q, k, v, offset, slots, kc, vc = _rope_kv_case(cuda_device, dtype)
+def test_rope_kv_matches_rope_and_scatter(moss, cuda_device, dtype, shape):
+    b, h, t, d, slots_n = shape
+    q, k, v, offset, slots, kc, vc = _rope_kv_case(cuda_device, dtype, b, h, t, d, slots_n)
     b, h, t, d = q.shape
     kc_ref, vc_ref = kc.clone(), vc.clone()
     oq_ref, ok_ref = moss.rope(q, k, offset, 10000.0)
