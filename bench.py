@@ -614,12 +614,15 @@ def stack_lines(torch, dev, cpu=True):
     variants = (
         (None, {}),
         ("fused_qkv", {"fused_qkv": True}),
+        ("history_attention", {"history_attention": True}),
         ("fused_qkv_history_attention", {"fused_qkv": True, "history_attention": True}))
     for key, opts in variants:
         stack = StreamingTransformer(cfg, weights, dev, **opts)
         dst = out if key is None else out.setdefault(key, {"what": {
             "fused_qkv": "qkv Linear + rotary + history writes as one tcgen05 kernel "
                          "(moss_qkv_rope; up to 32 token rows)",
+            "history_attention": "the attention over the history ring as "
+                                 "moss_history_attention instead of SDPA",
             "fused_qkv_history_attention": "moss_qkv_rope, and the attention over the history "
                                            "ring as moss_history_attention instead of SDPA"}[key]})
         for streams in (1, 64):
