@@ -218,7 +218,7 @@ def cpu_rvq_rate(x, books, seconds=10.0):
     from oracle import oracle as O
 
     threads = O.max_threads()
-    rows = 512
+    rows = 2048
     t = time.perf_counter()
     O.rvq_encode(x[:rows], books, nthreads=threads)
     dt = time.perf_counter() - t
