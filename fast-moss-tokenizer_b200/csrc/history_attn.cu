@@ -103,6 +103,13 @@ __global__ void __launch_bounds__(kThreads, 3) history_attn_kernel(const Args a)
   const uint16_t* qg = a.q + sh * T * kDim;
   for (int i = tid; i < T * kDim; i += kThreads) qs[i] = bf16_bits_to_f32(qg[i]);
   const int64_t p0 = a.pos[s];
+  // the slot positions of this thread's keys, loaded while K is in flight
+  int64_t held[kKeysPerThread];
+#pragma unroll
+  for (int m = 0; m < kKeysPerThread; ++m) {
+    const int j = tid + m * kThreads;
+    held[m] = j < n ? a.slot_pos[s * n + j] : -1;
+  }
   asm volatile("cp.async.wait_group 1;" ::: "memory");
   __syncthreads();
 
@@ -136,11 +143,10 @@ __global__ void __launch_bounds__(kThreads, 3) history_attn_kernel(const Args a)
           acc[t] = __fmaf_rn(qb.w, kv[7], acc[t]);
         }
       }
-      const int64_t held = a.slot_pos[s * n + j];
 #pragma unroll
       for (int t = 0; t < T; ++t) {
         const int64_t qp = p0 + t;
-        const bool on = held >= 0 && held <= qp && held > qp - a.context;
+        const bool on = held[m] >= 0 && held[m] <= qp && held[m] > qp - a.context;
         sc[m][t] = on ? __fmul_rn(acc[t], a.scale) : -CUDART_INF_F;
       }
     }
