@@ -1,5 +1,7 @@
-// Error reporting, version and device-error plumbing of the C ABI.
+// Error reporting, version and device-error plumbing of the C ABI, and the
+// self-test of the bounded-wait path.
 #include "common.cuh"
+#include "pipeline.cuh"
 
 #include <string.h>
 
@@ -72,4 +74,32 @@ extern "C" int moss_check_device_error(void* stream) {
                       value);
   }
   return MOSS_OK;
+}
+
+namespace moss {
+
+// One warp waits on an mbarrier through the kernels' own bounded wait
+// (pipe::mbar_wait).  With `arrive` thread 0 completes the phase first, so
+// the wait returns at once; without it nothing completes the phase and
+// every thread gives up after limit_ns, recording MOSS_ERR_TIMEOUT.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns, int arrive) {
+  __shared__ unsigned long long bar;
+  if (threadIdx.x == 0) {
+    pipe::mbar_init(&bar, 1);
+    pipe::fence_mbar_init();
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 0) pipe::mbar_arrive(&bar);
+  pipe::mbar_wait(&bar, 0, limit_ns);
+}
+
+}  // namespace moss
+
+extern "C" int moss_test_bounded_wait(int64_t limit_ns, int arrive, void* stream) {
+  const char* name = "moss_test_bounded_wait";
+  if (limit_ns < 1000 || limit_ns > 100000000)
+    return moss::fail(MOSS_ERR_VALUE, "%s: limit must be 1 us to 100 ms", name);
+  moss::bounded_wait_probe_kernel<<<1, 32, 0, moss::as_stream(stream)>>>(
+      static_cast<uint64_t>(limit_ns), arrive ? 1 : 0);
+  return moss::launch_status(name);
 }

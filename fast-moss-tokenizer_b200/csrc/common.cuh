@@ -36,6 +36,34 @@ __device__ __forceinline__ void record_device_error(int code) {
   atomicCAS(&g_device_error, 0, code);
 }
 
+// ---------------------------------------------------------------- bounded waits
+// Every spin in these kernels (on an mbarrier phase, a copy or an MMA) goes
+// through bounded_wait: it polls until `poll()` is true, and after
+// `limit_ns` of %globaltimer time gives up, records MOSS_ERR_TIMEOUT in the
+// device error word and returns false.  The caller then stops issuing work,
+// waits (bounded again) for its own copies in flight, frees what it holds
+// and returns, so no kernel traps or hangs.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // ~2 s
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+template <typename Poll>
+__device__ __forceinline__ bool bounded_wait(Poll poll, uint64_t limit_ns = kWaitLimitNs) {
+  if (poll()) return true;
+  const uint64_t start = global_ns();
+  while (!poll()) {
+    if (global_ns() - start > limit_ns) {
+      record_device_error(MOSS_ERR_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- dtypes
 __device__ __forceinline__ float bf16_bits_to_f32(uint16_t v) {
   return __uint_as_float(static_cast<uint32_t>(v) << 16);

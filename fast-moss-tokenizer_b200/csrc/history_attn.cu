@@ -36,6 +36,10 @@ constexpr int kDim = 64;
 constexpr int kMaxQueries = 8;
 constexpr int kMaxKeys = 512;
 constexpr int kKeysPerThread = kMaxKeys / kThreads;
+// Every slot index j = tid + m * kThreads (m < kKeysPerThread) that a thread
+// holds must cover [0, kMaxKeys) exactly; the host rejects n > kMaxKeys
+// before any launch, so the per-thread arrays are never indexed past it.
+static_assert(kKeysPerThread * kThreads == kMaxKeys, "slots per thread must tile kMaxKeys");
 
 struct Args {
   const uint16_t* q;         // [S, H, T, 64]

@@ -44,23 +44,11 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 // Waits for the phase of the given parity; false (after recording a
-// timeout) when it has not completed within ~2 s.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > 2000000000ull) {
-      record_device_error(MOSS_ERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
+// timeout) when it has not completed within `limit_ns` (~2 s by default).
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  return bounded_wait([&] { return mbar_try_wait(bar, parity); }, limit_ns);
 }
 // Global -> shared bulk copy; dst, src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,

@@ -88,23 +88,9 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
   return ok != 0;
 }
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-
 // Waits for the given phase; gives up after ~2 s and records a timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > 2000000000ull) {
-      record_device_error(MOSS_ERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
+  return bounded_wait([&] { return mbar_try_wait(bar, parity); });
 }
 
 // Local column of a row in the k-major 2r array.
@@ -394,50 +380,98 @@ __device__ __forceinline__ uint32_t tc_extra_offset(int n, int k) {
          static_cast<uint32_t>(n & 7) * 16u + static_cast<uint32_t>(k & 3) * 4u;
 }
 
-// One CTA per stage: code norms, the k-major copy used by the FFMA kernel,
-// the swizzled tile images used by the tensor-core kernel, per-stage stats.
+// Codebook preparation, one CTA per (256-code chunk, stage).  The chunk's
+// codewords are staged in shared memory with coalesced 16-byte loads (row
+// stride 65 floats, so both row-wise and column-wise reads are free of bank
+// conflicts); every output is then written in its own linear order, so all
+// global stores are coalesced: the code norms (sequential FMA, d ascending,
+// from +0; +inf for padding codes), the k-major copy read by the FFMA
+// kernel, and the 128-byte-swizzled tensor-core tile image with its extra
+// K block {-cnorm, 0 x 7} (-inf for padding codes).
+constexpr int kPrepStride = kDim + 1;
+constexpr size_t kPrepSmem = (static_cast<size_t>(kChunk) * kPrepStride + kChunk) * sizeof(float);
+
 __global__ void __launch_bounds__(256) rvq_prepare_kernel(const float* __restrict__ books, int k,
                                                           int kpad, int stages,
                                                           float* __restrict__ code_norm,
-                                                          float* __restrict__ packed,
-                                                          float* __restrict__ stats) {
+                                                          float* __restrict__ packed) {
+  extern __shared__ float prep_smem[];
+  float* rows = prep_smem;                         // [kChunk][kPrepStride]
+  float* norms = prep_smem + kChunk * kPrepStride;  // [kChunk]
+  const int ch = blockIdx.x, s = blockIdx.y;
+  const int nch = kpad / kChunk;
+  const int base = ch * kChunk;
+  const int valid = min(kChunk, k - base);  // >= 1: kpad < k + kChunk
+  const float* book = books + (static_cast<int64_t>(s) * k + base) * kDim;
+  // stage: float4 loads when the chunk's rows are 16-byte aligned (always,
+  // since kDim floats per row, when `books` itself is)
+  if ((reinterpret_cast<uintptr_t>(books) & 15u) == 0) {
+    for (int f = threadIdx.x; f < valid * (kDim / 4); f += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(book)[f];
+      const int n = f / (kDim / 4), d = (f % (kDim / 4)) * 4;
+      float* dst = rows + n * kPrepStride + d;
+      dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    }
+  } else {
+    for (int f = threadIdx.x; f < valid * kDim; f += blockDim.x)
+      rows[(f / kDim) * kPrepStride + f % kDim] = book[f];
+  }
+  for (int f = threadIdx.x + valid * kDim; f < kChunk * kDim; f += blockDim.x)
+    rows[(f / kDim) * kPrepStride + f % kDim] = 0.0f;
+  __syncthreads();
+  {
+    const int n = threadIdx.x;  // blockDim.x == kChunk
+    float nv = CUDART_INF_F;
+    if (n < valid) {
+      nv = 0.0f;
+      for (int d = 0; d < kDim; ++d) {
+        const float v = rows[n * kPrepStride + d];
+        nv = __fmaf_rn(v, v, nv);
+      }
+    }
+    norms[n] = nv;
+    code_norm[static_cast<int64_t>(s) * kpad + base + n] = nv;
+  }
+  __syncthreads();
+  // k-major copy [stage][chunk][d][kChunk]
+  float* kmajor = packed + (static_cast<int64_t>(s) * nch + ch) * kDim * kChunk;
+  for (int f = threadIdx.x; f < kDim * kChunk; f += blockDim.x)
+    kmajor[f] = rows[(f % kChunk) * kPrepStride + f / kChunk];
+  // tensor-core tile image, walked in its byte order (inverse of
+  // tc_image_offset / tc_extra_offset)
+  float* tile = packed + static_cast<int64_t>(stages) * kpad * kDim +
+                (static_cast<int64_t>(s) * nch + ch) * (kTcTileBytes / 4);
+  for (int f = threadIdx.x; f < kTcMainBytes / 4; f += blockDim.x) {
+    const int o = f * 4;
+    const int kb = o >> 15, ng = (o >> 10) & 31, nr = (o >> 7) & 7, c16 = (o >> 4) & 7,
+              w = (o >> 2) & 3;
+    const int n = ng * 8 + nr, kk = kb * 32 + (((c16 ^ nr) << 2) | w);
+    tile[f] = rows[n * kPrepStride + kk];
+  }
+  for (int f = threadIdx.x; f < kChunk * 8; f += blockDim.x) {
+    const int o = f * 4;
+    const int ng = o >> 8, eb = (o >> 7) & 1, nr = (o >> 4) & 7, w = (o >> 2) & 3;
+    const int n = ng * 8 + nr, e = eb * 4 + w;
+    // padding codes screen at -inf, below every real (finite) code
+    tile[kTcMainBytes / 4 + f] = e ? 0.0f : (n < valid ? -norms[n] : -CUDART_INF_F);
+  }
+}
+
+// Per-stage stats from the code norms: {max finite norm (from 0), 1 if any
+// real code's norm is non-finite -- which is the case exactly when one of
+// its values is non-finite or its squares overflow -- , 0, 0}.
+__global__ void __launch_bounds__(256) rvq_stats_kernel(const float* __restrict__ code_norm,
+                                                        int k, int kpad,
+                                                        float* __restrict__ stats) {
   __shared__ float red_max[256];
   __shared__ int red_bad[256];
   const int s = blockIdx.x;
-  const float* book = books + static_cast<int64_t>(s) * k * kDim;
-  const int nch = kpad / kChunk;
-  unsigned char* image = reinterpret_cast<unsigned char*>(
-      packed + static_cast<int64_t>(stages) * kpad * kDim);
   float mx = 0.0f;
   int bad = 0;
-  for (int j = threadIdx.x; j < kpad; j += blockDim.x) {
-    const int ch = j / kChunk, i = j % kChunk;
-    float* dst = packed + ((static_cast<int64_t>(s) * nch + ch) * kDim) * kChunk + i;
-    unsigned char* tile = image + (static_cast<int64_t>(s) * nch + ch) * kTcTileBytes;
-    if (j < k) {
-      float n = 0.0f;
-      for (int d = 0; d < kDim; ++d) {
-        const float v = book[static_cast<int64_t>(j) * kDim + d];
-        n = __fmaf_rn(v, v, n);
-        dst[static_cast<int64_t>(d) * kChunk] = v;
-        *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = v;
-        if (!isfinite(v)) bad = 1;
-      }
-      code_norm[static_cast<int64_t>(s) * kpad + j] = n;
-      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -n;
-      for (int e = 1; e < 8; ++e) *reinterpret_cast<float*>(tile + tc_extra_offset(i, e)) = 0.0f;
-      if (!isfinite(n)) bad = 1;
-      else mx = fmaxf(mx, n);
-    } else {
-      for (int d = 0; d < kDim; ++d) {
-        dst[static_cast<int64_t>(d) * kChunk] = 0.0f;
-        *reinterpret_cast<float*>(tile + tc_image_offset(i, d)) = 0.0f;
-      }
-      code_norm[static_cast<int64_t>(s) * kpad + j] = CUDART_INF_F;
-      // padding codes screen at -inf, below every real (finite) code
-      *reinterpret_cast<float*>(tile + tc_extra_offset(i, 0)) = -CUDART_INF_F;
-      for (int e = 1; e < 8; ++e) *reinterpret_cast<float*>(tile + tc_extra_offset(i, e)) = 0.0f;
-    }
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const float n = code_norm[static_cast<int64_t>(s) * kpad + j];
+    if (!isfinite(n)) bad = 1;
+    else mx = fmaxf(mx, n);
   }
   red_max[threadIdx.x] = mx;
   red_bad[threadIdx.x] = bad;
@@ -501,9 +535,14 @@ extern "C" int moss_rvq_prepare_codebooks(const float* books, int64_t stages, in
   if (k > 65536 || stages > 65535) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many codes or stages", name);
   if (!books || !code_norm || !packed || !stats) return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
   const int64_t kpad = (k + rvq::kChunk - 1) / rvq::kChunk * rvq::kChunk;
-  rvq::rvq_prepare_kernel<<<static_cast<unsigned>(stages), 256, 0, as_stream(stream)>>>(
+  static bool smem_set[kMaxDevices] = {false};
+  allow_dynamic_smem(rvq::rvq_prepare_kernel, rvq::kPrepSmem, smem_set);
+  const dim3 grid(static_cast<unsigned>(kpad / rvq::kChunk), static_cast<unsigned>(stages));
+  rvq::rvq_prepare_kernel<<<grid, rvq::kChunk, rvq::kPrepSmem, as_stream(stream)>>>(
       books, static_cast<int>(k), static_cast<int>(kpad), static_cast<int>(stages), code_norm,
-      packed, stats);
+      packed);
+  rvq::rvq_stats_kernel<<<static_cast<unsigned>(stages), 256, 0, as_stream(stream)>>>(
+      code_norm, static_cast<int>(k), static_cast<int>(kpad), stats);
   return launch_status(name);
 }
 

@@ -9,6 +9,8 @@
 // stream.  Capacity: 32 stages x 1024 codes x 64 dims.
 #include "common.cuh"
 
+#include <atomic>
+
 namespace moss {
 namespace rvq_static {
 
@@ -26,8 +28,10 @@ constexpr int64_t kScratchFloats = kPackedFloats + kNormFloats + kStatsFloats;
 // of it that the encode reads, so nothing here has to start at zero.
 static __device__ __align__(256) float g_scratch[kScratchFloats];
 
-// Device address of g_scratch, looked up once per device.
-static float* g_scratch_ptr[kMaxDevices] = {};
+// Device address of g_scratch, looked up once per device and kept for the
+// life of the process (a lookup by two threads at once stores the same
+// value; calls after cudaDeviceReset are not supported).
+static std::atomic<float*> g_scratch_ptr[kMaxDevices] = {};
 
 }  // namespace rvq_static
 }  // namespace moss
@@ -40,8 +44,10 @@ extern "C" int moss_rvq_encode_static(const float* x, int64_t rows, int64_t d, c
   using namespace rvq_static;
   const char* name = "moss_rvq_encode_static";
   if (rows < 0 || stages < 1 || k < 1 || d < 1) return fail(MOSS_ERR_VALUE, "%s: bad shape", name);
+  // valid sizes this entry point does not cover: MOSS_ERR_UNSUPPORTED, as the
+  // prepared-buffer entry points report sizes they do not cover
   if (d != kDim || stages > kMaxStages || k > kMaxCodes)
-    return fail(MOSS_ERR_VALUE,
+    return fail(MOSS_ERR_UNSUPPORTED,
                 "%s: %lld stages x %lld codes x %lld dims exceed the static scratch "
                 "(at most %lld stages x %lld codes x %lld dims); use moss_rvq_prepare_codebooks "
                 "and moss_rvq_encode with caller buffers",
@@ -49,7 +55,7 @@ extern "C" int moss_rvq_encode_static(const float* x, int64_t rows, int64_t d, c
                 static_cast<long long>(d), static_cast<long long>(kMaxStages),
                 static_cast<long long>(kMaxCodes), static_cast<long long>(kDim));
   if (moss_rvq_packed_floats(stages, k, d) > kPackedFloats)
-    return fail(MOSS_ERR_VALUE, "%s: packed codebooks exceed the static scratch", name);
+    return fail(MOSS_ERR_UNSUPPORTED, "%s: packed codebooks exceed the static scratch", name);
   if (rows == 0) return MOSS_OK;
   if (!x || !books || !codes || !recon) return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
   int dev = 0;
@@ -57,15 +63,16 @@ extern "C" int moss_rvq_encode_static(const float* x, int64_t rows, int64_t d, c
   if (e != cudaSuccess) return fail(MOSS_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return fail(MOSS_ERR_UNSUPPORTED, "%s: device index %d out of range", name, dev);
-  if (g_scratch_ptr[dev] == nullptr) {
+  float* packed = g_scratch_ptr[dev].load(std::memory_order_relaxed);
+  if (packed == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(MOSS_ERR_CUDA, "%s: scratch address lookup failed: %s", name,
                   cudaGetErrorString(e));
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    packed = static_cast<float*>(p);
+    g_scratch_ptr[dev].store(packed, std::memory_order_relaxed);
   }
-  float* packed = g_scratch_ptr[dev];
   float* code_norm = packed + kPackedFloats;
   float* stats = code_norm + kNormFloats;
   int st = moss_rvq_prepare_codebooks(books, stages, k, d, code_norm, packed, stats, stream);

@@ -24,13 +24,19 @@
 // (rare, short) record of {chunk, mask, chunk max} in shared memory; the
 // records are filtered against the final window at the end of the stage.
 //
-// One CTA = 128 rows (the 128 TMEM lanes), all stages:
-//   warps 0-3  epilogue: thread i owns row i (residual in registers), screens
-//              its TMEM lane, resolves, updates, writes the next stage's A
-//              operand (2r, K-major 128B-swizzled) to shared memory;
-//   warp 4     producer: cp.async.bulk of pre-built 256-code codebook tile
+// A CTA owns `rows_per_cta` rows for all stages, 320 threads:
+//   warps 0-7  epilogue (256 threads).  With at most 64 rows per CTA (the
+//              default while the rows fit one CTA per SM: 8192 rows -> 147
+//              CTAs of 56) every row is written into two TMEM lanes (lane i
+//              and 64 + i), so four threads screen its 256 columns per tile
+//              (two lane copies x two column halves); with 128 rows per CTA
+//              each row has one lane and two threads.  The part-0 thread of
+//              a row owns it: residual in registers, the exact resolve of
+//              its warp's candidate queue, the residual update, and the next
+//              stage's A operand (2r, K-major 128B-swizzled) in shared memory;
+//   warp 8     producer: cp.async.bulk of pre-built 256-code codebook tile
 //              images (64 KB swizzled dims + 8 KB norm column) into 2 slots;
-//   warp 5     TMEM allocator + MMA issuer: per tile 9 x tcgen05.mma
+//   warp 9     TMEM allocator + MMA issuer: per tile 9 x tcgen05.mma
 //              (M=128, N=256, K=8) into one of two 256-column accumulators.
 // Every wait is bounded (~2 s) and records MOSS_ERR_TIMEOUT; all roles then
 // meet at the final barrier where the TMEM is released.
@@ -116,22 +122,9 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t 
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 // Bounded wait (~2 s); false after recording a timeout.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - start > 2000000000ull) {
-      record_device_error(MOSS_ERR_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
+  return bounded_wait([&] { return mbar_try_wait(bar, parity); });
 }
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          unsigned long long* bar) {
@@ -387,7 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   const int ntiles = a.kpad / kTileCodes;
   const int total_tiles = a.stages * ntiles;
   const int rpc = a.rows_per_cta;
-  const int copies = kRows / rpc;
+  // rows_per_cta <= 64: every row sits in two TMEM lanes, copy c of local
+  // row i in lane c * 64 + i (lanes i >= rpc of each copy hold no row)
+  const int copies = rpc <= kRows / 2 ? 2 : 1;
+  const int span = kRows / copies;  // lanes per copy
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * rpc;
 
   if (tid == 0) {
@@ -399,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kEpiThreads);
     }
-    mbar_init(&sm.a_full, rpc);
+    mbar_init(&sm.a_full, span);  // every owner thread writes its lane
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.slow_count = 0;
   }
@@ -475,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   } else {
     // ------------------------------------------------------------ epilogue
     // The CTA's rpc rows sit in the 128 TMEM lanes `copies` times (lane L
-    // holds local row L % rpc).  Warp w reads the lanes of quarter w % 4, and
+    // holds local row L % span when that is below rpc).  Warp w reads the lanes of quarter w % 4, and
     // the 2 * copies warps that see a row split every tile's 256 columns
     // into equal parts.  The part-0 thread of a row owns it (residual in
     // registers): it writes the A operand, resolves and updates.
@@ -485,10 +481,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     const int part = (quarter / qpr) * 2 + (warp >> 2);
     const int nparts = 2 * copies;
     const int cpp = 8 / nparts;               // 32-code chunks per part and tile
-    const int slot = part * rpc + lr;
+    const int slot = part * span + lr;
     const bool owner = part == 0;
     const int64_t grow = row0 + lr;
-    const bool valid = grow < a.rows;
+    const bool valid = lr < rpc && grow < a.rows;
     float r[kDim];
     if (owner && valid) {
       const float4* src = reinterpret_cast<const float4*>(a.x + grow * kDim);
@@ -507,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       for (int cp = 0; cp < copies; ++cp) {
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<float*>(e + plain_offset(lr + cp * rpc, k)) = k == 0 ? 1.0f : 0.0f;
+          *reinterpret_cast<float*>(e + plain_offset(lr + cp * span, k)) = k == 0 ? 1.0f : 0.0f;
       }
     }
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -522,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
           const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
           st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
-          st_shared_v4(a_base + sw128_offset(lr + rpc, 4 * c, kRows * 128u), x0, x1, x2, x3);
+          st_shared_v4(a_base + sw128_offset(lr + span, 4 * c, kRows * 128u), x0, x1, x2, x3);
         }
       } else {
 #pragma unroll
@@ -649,8 +645,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         if (p < nparts) {
-          fast = fast && sm.nrec_h[p * rpc + lr] <= kRec;
-          gmax = fmaxf(gmax, sm.amax_h[p * rpc + lr]);
+          fast = fast && sm.nrec_h[p * span + lr] <= kRec;
+          gmax = fmaxf(gmax, sm.amax_h[p * span + lr]);
         }
       }
       const float athr = gmax - window;
@@ -863,9 +859,13 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
       !aligned16(recon) || (residual_out && !aligned16(residual_out)))
     return fail(MOSS_ERR_VALUE, "%s: buffers must be 16-byte aligned", name);
   const int64_t kpad = (k + rvqtc::kTileCodes - 1) / rvqtc::kTileCodes * rvqtc::kTileCodes;
-  // 64 rows per CTA (each in two TMEM lanes, so four threads share a row's
-  // columns) while that fills at most one CTA per SM, else 128.
-  const int rows_per_cta = rows <= static_cast<int64_t>(sm_count()) * 64 ? 64 : rvqtc::kRows;
+  // While the rows fit one CTA per SM at 64 rows per CTA, they are spread
+  // evenly over all SMs (ceil(rows / SMs) rows per CTA, each row in two
+  // TMEM lanes so four threads share its columns: 8192 rows -> 147 CTAs of
+  // 56); above that a CTA takes 128 rows, one lane each.
+  const int64_t sms = sm_count();
+  const int rows_per_cta =
+      rows <= sms * 64 ? static_cast<int>((rows + sms - 1) / sms) : rvqtc::kRows;
   const int64_t grid = (rows + rows_per_cta - 1) / rows_per_cta;
   if (grid > 0x7fffffffLL) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many rows", name);
   const size_t smem = sizeof(rvqtc::Smem) + 1024;

@@ -42,6 +42,7 @@ _SIGNATURES = {
     "moss_version": (_i, []),
     "moss_last_error": (ctypes.c_char_p, []),
     "moss_check_device_error": (_i, [_vp]),
+    "moss_test_bounded_wait": (_i, [_i64, _i, _vp]),
     "moss_scale_add": (_i, [_vp, _i, _vp, _i, _vp, _vp, _i64, _i64, _vp]),
     "moss_layer_norm": (_i, [_vp, _vp, _vp, _f, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_residual_layer_norm": (

@@ -66,6 +66,17 @@ MOSS_API const char* moss_last_error(void);
  * graph capture. */
 MOSS_API int moss_check_device_error(void* stream);
 
+/* Self-test of the failure path -- no counterpart in the reference (its
+ * kernels never wait on the device).  Runs one warp that waits on an
+ * mbarrier through the same bounded wait every kernel here uses, with a
+ * limit of limit_ns (1 us to 100 ms) instead of the kernels' ~2 s.  With
+ * arrive != 0 the phase is completed first and nothing is recorded; with
+ * arrive == 0 nothing completes it, the wait gives up after limit_ns,
+ * records MOSS_ERR_TIMEOUT in the device error word (read and cleared by
+ * moss_check_device_error) and the kernel returns: the context stays
+ * usable.  Stream-ordered; for tests. */
+MOSS_API int moss_test_bounded_wait(int64_t limit_ns, int arrive, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Residual update with per-channel layer scale.
  * Replaces fast_moss/v2_pointwise.py:92-122 (`_scale_add` / `scale_add`):
@@ -330,14 +341,20 @@ MOSS_API int moss_rvq_encode_ffma(const float* x, int64_t rows, int64_t d,
  * moss_rvq_prepare_codebooks into it and then moss_rvq_encode, both on
  * `stream`.  Same arguments and results as moss_rvq_encode minus the
  * prepared buffers.
- *   - Capacity: at most 32 stages x 1024 codes, d == 64; larger sizes return
- *     MOSS_ERR_VALUE.  The array takes 17,957,376 bytes of device memory on
- *     every device the library is used on.
+ *   - Capacity: at most 32 stages x 1024 codes, d == 64; other sizes return
+ *     MOSS_ERR_UNSUPPORTED (bad shapes and null pointers MOSS_ERR_VALUE).
+ *     The array takes 17,957,376 bytes of device memory on every device the
+ *     library is used on.
+ *   - Cost: every call prepares the codebooks again (two small kernels,
+ *     one CTA per 256-code chunk and stage, then one per stage) before the
+ *     encode; callers that quantize many batches against one codebook set
+ *     and can allocate should prepare once and call moss_rvq_encode.
  *   - Nothing in the array has to start at zero: every call rewrites all of
  *     it that the encode reads.
  *   - The first call on each device looks up the array's address
- *     (cudaGetSymbolAddress); make that first call before any stream capture
- *     on the device.
+ *     (cudaGetSymbolAddress) and keeps it for the life of the process (calls
+ *     after cudaDeviceReset are not supported); make that first call before
+ *     any stream capture on the device.
  *   - Calls that overlap in time on one device (other streams or host
  *     threads) race on the shared array; serialise them.
  * ------------------------------------------------------------------------- */

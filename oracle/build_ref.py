@@ -10,6 +10,7 @@ feeding the source through stdin.  The only output is the shared library in
 oracle/_ref/ (git-ignored), used to pin oracle.lfq_prepare.
 
 Usage: python oracle/build_ref.py [--reference /path/to/reference]
+(default: $FAST_MOSS_REFERENCE, else `reference` beside the repository root)
 """
 
 import argparse
@@ -21,7 +22,10 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 OUT = os.path.join(OUT_DIR, "libref_prepare.so")
-DEFAULT_REFERENCE = "/root/reference"
+# The reference checkout: $FAST_MOSS_REFERENCE, else a directory named
+# `reference` beside this repository's root.
+DEFAULT_REFERENCE = os.environ.get(
+    "FAST_MOSS_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 SHIM = r"""
 #include <cmath>

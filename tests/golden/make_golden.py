@@ -1,7 +1,8 @@
 """Generates tests/golden/*.npz from the REFERENCE implementation.
 
-Run in a checkout that has the reference at /root/reference (or
---reference PATH).  The reference's Triton kernels (`_scale_add`,
+Run with the reference checkout at --reference PATH (default:
+$FAST_MOSS_REFERENCE, else a directory `reference` beside the repository
+root).  The reference's Triton kernels (`_scale_add`,
 `_rotate`, `_select`) run on the CPU under TRITON_INTERPRET=1 and its LFQ
 preparation kernel runs as host code compiled by oracle/build_ref.py.  The
 fixtures record inputs and the reference's outputs; the tests compare the

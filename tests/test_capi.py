@@ -78,6 +78,16 @@ def test_bad_arguments_map_to_value_errors(lib):
     assert lib.moss_rvq_packed_floats(32, 1000, 64) == 32 * 1024 * 64 + 32 * 4 * 256 * 72
     assert lib.moss_rvq_encode_ffma(None, 8, 32, None, None, None, None, 1, 4, None, None, None,
                                     None) == _lib.ERR_UNSUPPORTED
+    # the bounded-wait self-test takes limits of 1 us to 100 ms only
+    assert lib.moss_test_bounded_wait(10, 0, None) == _lib.ERR_VALUE
+    assert lib.moss_test_bounded_wait(10**9, 0, None) == _lib.ERR_VALUE
+    # the history attention holds at most 512 slots per thread block: larger
+    # rings are rejected before any launch (null pointers are never read)
+    assert lib.moss_history_attention(None, None, None, None, None, 2, 20, 4, 513, 64, 250,
+                                      0.125, None, None) == _lib.ERR_UNSUPPORTED
+    assert b"512" in lib.moss_last_error()
+    assert lib.moss_history_attention(None, None, None, None, None, 2, 20, 4, 512, 64, 250,
+                                      0.125, None, None) == _lib.ERR_VALUE
 
 
 def test_python_wrappers_raise_reference_exceptions():
@@ -102,5 +112,10 @@ def test_static_quantizer_rejects_sizes_beyond_its_scratch(lib):
 
     for stages, k, d in ((33, 1024, 64), (32, 1025, 64), (4, 16, 32)):
         st = lib.moss_rvq_encode_static(None, 10, d, None, stages, k, None, None, None, None)
-        assert st == _lib.ERR_VALUE
+        assert st == _lib.ERR_UNSUPPORTED
         assert b"static scratch" in lib.moss_last_error()
+    for stages, k, d in ((0, 16, 64), (4, 0, 64), (4, 16, 0)):
+        st = lib.moss_rvq_encode_static(None, 10, d, None, stages, k, None, None, None, None)
+        assert st == _lib.ERR_VALUE
+    st = lib.moss_rvq_encode_static(None, -1, 64, None, 4, 16, None, None, None, None)
+    assert st == _lib.ERR_VALUE

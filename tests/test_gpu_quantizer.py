@@ -132,6 +132,8 @@ def test_rvq_config2_bit_exact(moss, cuda_device, algorithm):
 @pytest.mark.parametrize("algorithm", ALGOS)
 @pytest.mark.parametrize("rows,k,stages", [(1, 1024, 4), (57, 1000, 3), (113, 256, 2),
                                            (300, 37, 5), (56, 2049, 2), (129, 4096, 2),
+                                           (9000, 512, 3),   # 61 rows per CTA, last CTA short
+                                           (9472, 300, 2),   # 148 x 64: exactly 64 per CTA
                                            (10001, 300, 2)])  # > 148 x 64 rows: 128 per CTA
 def test_rvq_ragged_shapes(moss, cuda_device, rows, k, stages, algorithm):
     x, books = rvq_case(rows, k, stages, rows + k, cuda_device)

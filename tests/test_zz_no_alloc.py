@@ -61,3 +61,33 @@ def test_static_scratch_matches_workspace_entry_point(moss, cuda_device):
         for g, w in zip(got, want):
             assert torch.equal(g, w), (rows, stages, k)
         assert lib.moss_check_device_error(None) == 0
+
+
+def test_static_scratch_without_residual_and_with_no_rows(moss, cuda_device):
+    """residual_out may be NULL (the header allows it); rows == 0 is a no-op
+    that returns MOSS_OK and leaves the outputs untouched."""
+    from fast_moss_b200 import _lib
+
+    lib = _lib.load()
+    rng = np.random.default_rng(78)
+    x = torch.from_numpy(rng.standard_normal((513, 64)).astype(np.float32)).to(cuda_device)
+    books = torch.from_numpy(
+        (rng.standard_normal((9, 700, 64)) / 8).astype(np.float32)).to(cuda_device)
+    sh = torch.cuda.current_stream(cuda_device).cuda_stream
+    codes = torch.full((9, 513), -7, dtype=torch.int32, device=cuda_device)
+    recon = torch.full_like(x, float("nan"))
+    _lib.check(lib.moss_rvq_encode_static(x.data_ptr(), 513, 64, books.data_ptr(), 9, 700,
+                                          codes.data_ptr(), recon.data_ptr(), None, sh),
+               "moss_rvq_encode_static")
+    want = _workspace_encode(lib, _lib, x, books)
+    torch.cuda.synchronize()
+    assert torch.equal(codes, want[0]) and torch.equal(recon, want[1])
+
+    codes0 = codes.clone()
+    recon0 = recon.clone()
+    st = lib.moss_rvq_encode_static(x.data_ptr(), 0, 64, books.data_ptr(), 9, 700,
+                                    codes.data_ptr(), recon.data_ptr(), None, sh)
+    torch.cuda.synchronize()
+    assert st == _lib.OK
+    assert torch.equal(codes, codes0) and torch.equal(recon, recon0)
+    assert lib.moss_check_device_error(None) == 0
