@@ -1,45 +1,54 @@
 """Benchmark of the MOSS v2 hot path on B200 (one JSON line on rank 0).
 
-Headline workload: the 32-stage residual vector quantizer (encode + decode)
-over 8192 codec frames x 64 dims with 32 codebooks of 1024 x 64, FP32.  One
-step = one pass of the quantizer over one 8192-frame batch per GPU (weak
-scaling: every rank quantizes its own batch, no collective on the data
-path).  The metric is audio seconds per second: each frame is 80 ms of
-48 kHz audio (3840 samples), so one 8192-frame batch is 655.36 s of audio.
+Headline workload: the codec's streaming transformer stack (24 layers,
+hidden 1280, 20 heads, feed-forward 5120, FP32 residual stream, bf16 GEMMs
+on cached bf16 weights, seeded random weights) serving 64 independent
+batch-1 streams per GPU through the batched CUDA-graph scheduler
+(BatchedStreams): every stream is the streaming configuration of the
+benchmark (chunks of [1, 4, 1280] tokens = 80 ms of audio).  One step = 125
+chunks of every stream, i.e. 10 s of audio per stream, 640 s per GPU.  The
+metric is audio seconds per second (real-time factor x streams), whole job:
+every rank serves its own 64 streams (weak scaling, no collective on the
+data path).
 
-  value      device time of the encode kernel only (inputs resident in HBM),
-             L2 flushed between timed steps; max over ranks.
-  e2e        the same metric through the public API with host buffers: every
-             step copies the frames in from pinned host memory and the codes
-             and reconstruction back out, the copies of one step overlapped
-             with the quantization of its neighbours.
-  roofline   the encode kernel against the tensor-core (TF32) peak: it
-             screens every codeword with tcgen05 TF32 dot products and
-             re-ranks the survivors exactly in FP32.  achieved = algorithmic
-             FLOPs per launch (8192 x 32 x 1024 x 64 x 2) / CUDA-event launch
-             time; peak = half the measured dense bf16 GEMM rate; the FP32
-             FFMA peak (SMs x 128 lanes x 2 x max clock) is given beside it.
-             DRAM traffic per launch comes from the committed ncu summary.
-  kernels    the other hot-path kernels (residual+LayerNorm, RoPE, SiLU
-             gate) at their workload sizes vs the measured HBM copy
-             bandwidth, launches captured in a CUDA graph with inputs rotated
-             through > L2-sized sets; the all-FFMA quantizer kernel; the
-             reference's per-stage quantizer sequence (GEMM + select +
-             update, 32 stages in one graph) on the same GPU; one
-             real-model LFQ stage as the reference's prepare + GEMM + select
-             sequence and as the fused decode.
-  stack      the codec's streaming transformer stack (24 x 1280, 20 heads,
-             ffn 5120) on the hot-path kernels under the batched CUDA-graph
-             scheduler: 125 chunks of 80 ms per stream at 1 and 64 streams,
-             with and without the per-chunk host copies, and the eager torch
-             stack on the host cores beside it.
+  value      device time of the K timed steps with every chunk's features
+             already in HBM (max over ranks).  Each chunk streams the 0.94 GB
+             of bf16 weights and the 2.0 GB of history rings, far more than
+             L2, so no flush is needed.
+  e2e        the same steps through the scheduler's public API with host
+             buffers: each chunk's features are copied in from pinned host
+             memory straight into the graph's input and its output copied
+             back out, inside the timed region.
+  roofline   the dominant kernel of this library in the step, the attention
+             over the history ring (moss_history_attention, one launch per
+             layer and chunk), against the measured HBM copy bandwidth:
+             achieved = its algorithmic bytes (keys and values of every ring
+             slot, queries, slot positions, output) / its CUDA-event launch
+             time at the step's shapes; `step` gives the whole chunk's
+             algorithmic HBM bytes (weights + rings) over the chunk time.
+  cpu_baseline  the eager torch stack (oracle/stack.py) on the host cores,
+             the same 64 streams batched, a bounded sample of chunks.
+  quantizer  the 32-stage residual VQ of the benchmark's quantizer
+             configuration (8192 frames x 64, 32 codebooks x 1024 x 64,
+             FP32): frames/s of the tensor-core kernel, its tensor roofline,
+             the all-FFMA kernel, the reference's per-stage sequence on the
+             same GPU (cuBLAS GEMM + select) with the fraction of equal
+             codes, end to end with host buffers, and the CPU oracle port.
+  kernels    residual+LayerNorm, RoPE, SiLU gate and one real-model LFQ
+             stage at their benchmark sizes, graph-timed over > L2-sized
+             rotating sets, against the measured HBM bandwidth.
+  stack      the stack's variants at 1 stream (the benchmark's batch-1
+             configuration) and 64 streams: the default path (bit-identical
+             to the eager torch stack), the fused qkv projection, the
+             history attention, both; and the per-layer kernel lines of the
+             qkv projection and the attention.
   clocks     SM clock and clock-event reasons sampled during the timed
              region.
-  cpu_baseline  the CPU oracle port of the same quantizer on the host
-             cores (bounded sample).
 
-`--impl reference` times the CPU implementation of the path instead (the
-oracle port, all host threads) on rank 0.
+The extra objects (quantizer, kernels, stack) are measured on rank 0 of a
+one-GPU run only.  `--impl reference` times the reference's computation of
+the headline on the host instead: the eager torch stack of oracle/stack.py,
+64 streams batched, all host threads, rank 0 only.
 """
 
 import argparse
@@ -60,11 +69,18 @@ for _p in (REPO, PKG_DIR):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+# headline: the streaming stack
+STREAMS = 64          # independent batch-1 streams per GPU
+CHUNKS = 125          # 80 ms chunks per stream and step: 10 s of audio
+CHUNK_SEC = 0.08
+HEADLINE_OPTIONS = {"history_attention": True}
+METRIC = "audio-sec/sec (RTF x streams), streaming codec stack"
+
+# the quantizer configuration
 FRAMES = 8192
 DIM = 64
 STAGES = 32
 CODES = 1024
-FRAME_SEC = 3840 / 48000  # 80 ms of audio per codec frame
 FLOP_PER_FRAME = STAGES * CODES * DIM * 2  # dot-product multiply-adds
 L2_FLUSH_BYTES = 256 << 20
 
@@ -72,13 +88,14 @@ L2_FLUSH_BYTES = 256 << 20
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=500)
+    p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["b200", "reference"], default="b200")
     p.add_argument("--no-kernels", action="store_true", help="skip the per-kernel HBM lines")
-    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-quantizer", action="store_true", help="skip the quantizer object")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     p.add_argument("--no-stack", action="store_true",
-                   help="skip the streaming transformer stack lines")
+                   help="skip the stack variants (the headline always runs)")
     return p.parse_args()
 
 
@@ -112,7 +129,6 @@ def profile_traffic(kernel):
         return None
     m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", open(paths[0]).read())
     return float(m.group(1)) if m else None
-
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
@@ -232,43 +248,78 @@ def cpu_rvq_rate(x, books, seconds=10.0):
     return rows * passes / dt, threads, rows, passes, dt
 
 
+
+def _cpu_stack_rate(cfg, weights, streams, seconds):
+    """Audio-sec/s of the eager torch stack (oracle/stack.py) on the host
+    cores for `streams` streams batched: one warm-up chunk, then chunks
+    until about `seconds` have passed (at least 2).  Returns (rate, chunks,
+    threads, seconds)."""
+    import torch
+
+    from oracle.stack import EagerStack
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    ref = EagerStack(cfg, weights, "cpu", streams)
+    g = torch.Generator().manual_seed(4)
+    feats = torch.randn(3, streams, cfg.chunk_tokens, cfg.dim, generator=g)
+    ref.step(feats[0])
+    n = 0
+    t = time.perf_counter()
+    while n < 2 or (time.perf_counter() - t < seconds and n < 16):
+        ref.step(feats[1 + n % 2])
+        n += 1
+    dt = time.perf_counter() - t
+    return streams * n * CHUNK_SEC / dt, n, threads, dt
+
+
 def run_reference(args):
-    rank, _, world = rank_info()
+    """The reference's computation of the headline workload on the host:
+    the eager torch stack (stock LayerNorm, eager residual and rotary, the
+    same GEMM and SDPA calls; oracle/stack.py) with the 64 streams batched,
+    all host threads.  One step = one 80 ms chunk of every stream (a
+    bounded sample of the 125-chunk step)."""
+    rank, _, _ = rank_info()
     if rank != 0:
         return
-    x, books = workload()
-    from oracle import oracle as O
+    import torch
 
-    threads = O.max_threads()
-    # size each step so that the whole warm-up + timed run takes ~2 minutes
-    rate = cpu_rvq_rate(x, books, seconds=2.0)[0]
-    per_step = min(5.0, 120.0 / max(1, args.steps + args.warmup))
-    rows = int(min(FRAMES, max(16, rate * per_step)))
-    for _ in range(args.warmup):
-        O.rvq_encode(x[:rows], books, nthreads=threads)
+    from fast_moss_b200.transformer import StackConfig, init_weights
+    from oracle.stack import EagerStack
+
+    cfg = StackConfig()
+    weights = init_weights(cfg, seed=2)
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    ref = EagerStack(cfg, weights, "cpu", STREAMS)
+    g = torch.Generator().manual_seed(4)
+    feats = torch.randn(2, STREAMS, cfg.chunk_tokens, cfg.dim, generator=g)
+    for i in range(args.warmup):
+        ref.step(feats[i % 2])
     t = time.perf_counter()
-    for _ in range(args.steps):
-        O.rvq_encode(x[:rows], books, nthreads=threads)
+    for i in range(args.steps):
+        ref.step(feats[i % 2])
     dt = time.perf_counter() - t
-    value = rows * args.steps / dt * FRAME_SEC
+    value = STREAMS * args.steps * CHUNK_SEC / dt
     line = {
         "impl": "reference",
-        "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
+        "metric": METRIC,
         "value": value, "unit": "audio-sec/sec", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded N(0,1) frames, N(0,1)/8 codebooks",
-        "config": {"workload": f"rvq{STAGES}_encode_decode: {FRAMES} frames x {DIM}, "
-                               f"{STAGES} codebooks x {CODES} x {DIM}, FP32",
-                   "sample_rows_per_step": rows},
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) features, seeded random weights (std 0.02)",
+        "config": {"workload": f"streaming codec stack 24 x 1280, 20 heads, ffn 5120; "
+                               f"{STREAMS} batch-1 streams batched; one 80 ms chunk of every "
+                               f"stream per step (a sample of the {CHUNKS}-chunk step)",
+                   "streams": STREAMS, "chunks_per_step": 1},
         "cpu_baseline": {"value": value, "unit": "audio-sec/sec", "cores": threads,
                          "kind": "port",
-                         "sample": f"{rows} of {FRAMES} frames x {STAGES} stages per step"},
+                         "sample": f"{args.steps} chunks of {STREAMS} streams, eager torch stack "
+                                   f"(oracle/stack.py) on the host"},
         "e2e": {"value": value, "unit": "audio-sec/sec", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-
 
 # ----------------------------------------------------------------- GPU arms
 def time_launches(torch, fn, sets, launches=40, replays=5):
@@ -478,15 +529,14 @@ def _stack_rate(torch, dev, cfg, stack, streams, chunks):
     # slice would be staged through pageable memory by torch).
     host = torch.randn(chunks, streams, cfg.chunk_tokens, cfg.dim, generator=g).pin_memory()
     host_out = torch.empty_like(host).pin_memory()
-    x_dev = torch.empty(streams, cfg.chunk_tokens, cfg.dim, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def run(copies):
         sched.reset()
         for c in range(chunks):
             if copies:
-                x_dev.copy_(host[c], non_blocking=True)
-            y = sched.push(x_dev)
+                sched.input.copy_(host[c], non_blocking=True)
+            y = sched.advance()
             if copies:
                 host_out[c].copy_(y, non_blocking=True)
 
@@ -594,63 +644,245 @@ def _attention_kernel_line(torch, dev, cfg):
     return res
 
 
-def stack_lines(torch, dev, cpu=True):
-    """The codec's streaming transformer stack (24 layers, hidden 1280, 20
-    heads, feed-forward 5120, FP32 weights seeded 2, bf16 GEMMs) over 125
-    chunks of 80 ms = 10 s of audio per stream, one CUDA graph replay per
-    chunk.  Every chunk is copied in from pinned host memory and its output
-    back out inside the timed region (the streaming use); one stream is the
-    reference's StreamingCodec shape, 64 streams the batched scheduler.
-    The CPU baseline is the eager oracle stack on the host cores (bf16
-    GEMMs, a bounded sample of chunks)."""
+
+def stack_variants(torch, dev):
+    """The stack's variants at 1 stream (the benchmark's batch-1 streaming
+    configuration: 125 chunks of [1, 4, 1280]) and at 64 streams, each with
+    and without the per-chunk host copies; then the per-layer lines of the
+    qkv projection and of the attention."""
     from fast_moss_b200.transformer import StackConfig, StreamingTransformer, init_weights
 
     cfg = StackConfig()
-    chunks = 125
-    weights = init_weights(cfg, seed=2)
+    weights = init_weights(cfg, seed=2, device=dev)
     out = {"workload": "streaming stack: 24 layers, hidden 1280, 20 heads, ffn 5120, "
                        "context 250 tokens, 4 tokens per 80 ms chunk, 125 chunks per stream",
            "metric": "audio-sec/sec (RTF x streams)", "dtype": "bf16 GEMMs, f32 residual"}
     variants = (
-        (None, {}),
-        ("fused_qkv", {"fused_qkv": True}),
-        ("history_attention", {"history_attention": True}),
-        ("fused_qkv_history_attention", {"fused_qkv": True, "history_attention": True}))
-    for key, opts in variants:
+        ("default", {}, "cuBLAS projections, SDPA attention; bit-identical to the eager torch "
+                        "stack"),
+        ("fused_qkv", {"fused_qkv": True}, "qkv Linear + rotary + history writes as one tcgen05 "
+                                           "kernel (moss_qkv_rope; up to 32 token rows)"),
+        ("history_attention", {"history_attention": True},
+         "the attention over the history ring as moss_history_attention instead of SDPA "
+         "(the headline's path)"),
+        ("fused_qkv_history_attention", {"fused_qkv": True, "history_attention": True},
+         "moss_qkv_rope, and moss_history_attention instead of SDPA"))
+    for key, opts, what in variants:
         stack = StreamingTransformer(cfg, weights, dev, **opts)
-        dst = out if key is None else out.setdefault(key, {"what": {
-            "fused_qkv": "qkv Linear + rotary + history writes as one tcgen05 kernel "
-                         "(moss_qkv_rope; up to 32 token rows)",
-            "history_attention": "the attention over the history ring as "
-                                 "moss_history_attention instead of SDPA",
-            "fused_qkv_history_attention": "moss_qkv_rope, and the attention over the history "
-                                           "ring as moss_history_attention instead of SDPA"}[key]})
+        dst = out.setdefault(key, {"what": what})
         for streams in (1, 64):
-            dst[f"streams_{streams}"] = _stack_rate(torch, dev, cfg, stack, streams, chunks)
+            dst[f"streams_{streams}"] = _stack_rate(torch, dev, cfg, stack, streams, CHUNKS)
         del stack
     out["qkv_kernel"] = _qkv_kernel_line(torch, dev, cfg, weights)
     out["attention_kernel"] = _attention_kernel_line(torch, dev, cfg)
     torch.cuda.synchronize()
-    if cpu:
-        from oracle.stack import EagerStack
-
-        torch.set_num_threads(len(os.sched_getaffinity(0)))
-        ref = EagerStack(cfg, weights, "cpu", 1)
-        g = torch.Generator().manual_seed(4)
-        feats = torch.randn(1, cfg.chunk_tokens * 4, cfg.dim, generator=g)
-        ref.step(feats[:, :4])  # warm-up
-        n = 0
-        t = time.perf_counter()
-        while n < 3 or (time.perf_counter() - t < 10.0 and n < 8):
-            c = 1 + n % 3
-            ref.step(feats[:, 4 * c:4 * (c + 1)])
-            n += 1
-        dt = (time.perf_counter() - t) / n
-        out["cpu_baseline"] = {"value": 0.08 / dt, "unit": "audio-sec/sec", "cores":
-                               torch.get_num_threads(), "kind": "port",
-                               "sample": f"{n} chunks of one stream, eager torch stack on the "
-                                         f"host (bf16 GEMMs)"}
     return out
+
+
+def quantizer_lines(torch, dev, peaks, peak_src, steps, warmup, cpu):
+    """The benchmark's quantizer configuration: 8192 frames x 64 through 32
+    codebooks of 1024 x 64 (seed 1), FP32, int32 codes.  Kernel time with L2
+    flushed between launches, end to end through
+    ResidualVectorQuantizer.encode_host_batches with pinned host buffers,
+    the all-FFMA kernel, the reference's per-stage sequence, and the CPU
+    oracle port."""
+    import fast_moss_b200 as fm
+    from fast_moss_b200 import _lib
+
+    lib = _lib.load()
+    x_np, books_np = workload(seed=1)
+    books = torch.from_numpy(books_np).to(dev)
+    rvq = fm.ResidualVectorQuantizer(books)
+    x = torch.from_numpy(x_np).to(dev)
+    codes = torch.empty((STAGES, FRAMES), dtype=torch.int32, device=dev)
+    recon = torch.empty((FRAMES, DIM), device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    def launch(entry, c, r):
+        _lib.check(getattr(lib, entry)(
+            x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(), rvq.packed.data_ptr(),
+            rvq.code_norm.data_ptr(), rvq.stats.data_ptr(), STAGES, CODES, c.data_ptr(),
+            r.data_ptr(), None, sh), entry)
+
+    def timed(entry, n, c, r):
+        for _ in range(max(warmup, 3)):
+            launch(entry, c, r)
+        s = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+        for i in range(n):
+            flush.fill_(float(i))  # evict the previous launch's data from L2 (untimed)
+            s[i].record(stream)
+            launch(entry, c, r)
+            e[i].record(stream)
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in zip(s, e)) * 1e-3 / n
+
+    n = max(steps, 10)
+    tc_s = timed("moss_rvq_encode", n, codes, recon)
+    ok = bool(torch.equal(rvq.decode(codes), recon))
+    codes_f = torch.empty_like(codes)
+    recon_f = torch.empty_like(recon)
+    ffma_s = timed("moss_rvq_encode_ffma", max(3, min(n, 20)), codes_f, recon_f)
+    ok = ok and bool(torch.equal(codes_f, codes))
+    _lib.check(lib.moss_check_device_error(sh), "device error word")
+
+    nhost = 4
+    x_hosts = [torch.from_numpy(x_np).pin_memory() for _ in range(nhost)]
+    codes_hosts = [torch.empty((STAGES, FRAMES), dtype=torch.int32).pin_memory()
+                   for _ in range(nhost)]
+    recon_hosts = [torch.empty((FRAMES, DIM)).pin_memory() for _ in range(nhost)]
+
+    def e2e_run(k):
+        rvq.encode_host_batches([x_hosts[i % nhost] for i in range(k)],
+                                [codes_hosts[i % nhost] for i in range(k)],
+                                [recon_hosts[i % nhost] for i in range(k)])
+
+    e2e_run(3)
+    torch.cuda.synchronize()
+    es = torch.cuda.Event(enable_timing=True)
+    ee = torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    e2e_run(n)
+    ee.record(stream)
+    ee.synchronize()
+    e2e_s = es.elapsed_time(ee) * 1e-3 / n
+    ok = ok and bool(torch.equal(codes_hosts[(n - 1) % nhost], codes.cpu()))
+
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    fp32_peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
+    tf32_peak = float(peaks["bf16_tflops"]) / 2
+    flop = FRAMES * FLOP_PER_FRAME
+    out = {
+        "what": "config-2 quantizer throughput: 32-stage residual VQ encode + decode, "
+                f"{FRAMES} frames x {DIM}, {STAGES} codebooks x {CODES} x {DIM}, FP32, int32 "
+                "codes (a kernel measurement, not a codec RTF)",
+        "unit": "frames/sec",
+        "value": FRAMES / tc_s, "us_per_launch": tc_s * 1e6,
+        "l2": "flushed between launches (256 MiB write, untimed)",
+        "e2e": {"value": FRAMES / e2e_s, "unit": "frames/sec",
+                "h2d_bytes_per_step": FRAMES * DIM * 4,
+                "d2h_bytes_per_step": STAGES * FRAMES * 4 + FRAMES * DIM * 4,
+                "api": "ResidualVectorQuantizer.encode_host_batches (copies overlapped with the "
+                       "neighbouring batches)"},
+        "roofline": {"bound": "tensor", "kernel": "rvq_tc_kernel (TF32 tcgen05 screening + exact "
+                                                  "FP32 rerank)",
+                     "achieved": flop / tc_s / 1e12, "peak": tf32_peak, "unit": "TFLOP/s",
+                     "frac": flop / tc_s / 1e12 / tf32_peak,
+                     "traffic": profile_traffic("rvq_tc_kernel"),
+                     "peak_source": f"TF32 dense = 1/2 of the {peak_src} bf16 dense GEMM rate "
+                                    f"({peaks['bf16_tflops']} TFLOP/s)",
+                     "flop_per_launch": flop, "fp32_ffma_peak": fp32_peak,
+                     "frac_of_fp32_ffma_peak": flop / tc_s / 1e12 / fp32_peak},
+        "ffma": {"kernel": "rvq_encode_kernel (all-FFMA, identical codes)",
+                 "us_per_launch": ffma_s * 1e6, "achieved_tflops": flop / ffma_s / 1e12,
+                 "frac_of_fp32_ffma_peak": flop / ffma_s / 1e12 / fp32_peak},
+        "reference_sequence": rvq_sequence_line(torch, x, rvq.books, codes, tc_s),
+        "outputs_verified": ok,
+    }
+    if cpu:
+        rate, threads, rows, passes, dt = cpu_rvq_rate(x_np, books_np, seconds=10.0)
+        out["cpu_baseline"] = {"value": rate, "unit": "frames/sec", "cores": threads,
+                               "kind": "port",
+                               "sample": f"{passes} x {rows} of {FRAMES} frames x {STAGES} stages "
+                                         f"({dt:.1f} s, oracle C port, OpenMP)"}
+    return out
+
+
+def headline(torch, dist, dev, rank, world, args):
+    """Times the headline steps on this rank: returns (device seconds, e2e
+    seconds, outputs agree, clocks, details)."""
+    from fast_moss_b200.transformer import BatchedStreams, StackConfig, StreamingTransformer
+    from fast_moss_b200.transformer import init_weights
+
+    cfg = StackConfig()
+    weights = init_weights(cfg, seed=2, device=dev)
+    stack = StreamingTransformer(cfg, weights, dev, **HEADLINE_OPTIONS)
+    sched = BatchedStreams(stack, streams=STREAMS, chunks_per_graph=1)
+    g = torch.Generator(device=dev).manual_seed(4 + rank)
+    feats = torch.randn(CHUNKS, STREAMS, cfg.chunk_tokens, cfg.dim, device=dev, generator=g)
+    out_dev = torch.empty_like(feats)
+    host_in = feats.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def step_device():  # features resident in HBM
+        sched.reset()
+        for c in range(CHUNKS):
+            sched.input.copy_(feats[c])
+            out_dev[c].copy_(sched.advance())
+
+    def step_host():  # pinned host buffers, copies inside the step
+        sched.reset()
+        for c in range(CHUNKS):
+            sched.input.copy_(host_in[c], non_blocking=True)
+            host_out[c].copy_(sched.advance(), non_blocking=True)
+
+    def timed(step, k):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(k):
+            step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return s0.elapsed_time(s1) * 1e-3
+
+    sampler = ClockSampler(dev)
+    sampler.start()
+    time.sleep(0.3)
+    t0 = time.time()
+    device_s = timed(step_device, args.steps)
+    t1 = time.time()
+    e2e_s = timed(step_host, args.steps)
+    sampler.stop()
+    clocks = sampler.summary(t0, t1)
+    # the last step of both paths ran the same features from a reset history
+    agree = bool(torch.equal(out_dev.cpu(), host_out)) and bool(torch.isfinite(out_dev).all())
+    details = {"native_launches_per_chunk": stack.native_launches(STREAMS),
+               "h2d_bytes_per_chunk": host_in[0].numel() * 4,
+               "d2h_bytes_per_chunk": host_out[0].numel() * 4}
+    sched.release()
+    del stack, sched, feats, out_dev
+    torch.cuda.synchronize()
+    return device_s, e2e_s, agree, clocks, details, weights, cfg
+
+
+def step_roofline(torch, dev, cfg, peaks, ms_per_chunk):
+    """The dominant kernel of this library in the headline step (the
+    history attention, measured at the step's shapes), and the whole
+    chunk's algorithmic HBM bytes against the chunk time."""
+    att = _attention_kernel_line(torch, dev, cfg)["streams_64"]
+    hbm = float(peaks["hbm_gbs"])
+    d, f, h = cfg.dim, cfg.ffn, cfg.heads
+    weight_bytes = cfg.layers * (3 * d * d + d * d + 2 * d * f) * 2
+    ring_bytes = cfg.layers * STREAMS * h * cfg.history_slots * cfg.head_dim * 2 * 2
+    chunk_bytes = weight_bytes + ring_bytes
+    return {
+        "bound": "hbm",
+        "kernel": "history_attn_kernel (moss_history_attention: 64 streams x 20 heads, 4 queries "
+                  "over 253 ring slots of 64, bf16)",
+        "achieved": att["owned_gbs"], "peak": hbm, "unit": "GB/s", "frac": att["owned_gbs"] / hbm,
+        "traffic": profile_traffic("history_attn_kernel"),
+        "bytes_per_launch": att["bytes"], "us_per_launch": att["us_owned"],
+        "us_per_launch_sdpa": att["us_sdpa"],
+        "step": {"what": "one chunk of all 64 streams: bf16 weights of 24 layers + every layer's "
+                         "key/value ring read once",
+                 "bytes_per_chunk": chunk_bytes, "weight_bytes": weight_bytes,
+                 "ring_bytes": ring_bytes, "ms_per_chunk": ms_per_chunk,
+                 "achieved_gbs": chunk_bytes / (ms_per_chunk * 1e-3) / 1e9,
+                 "frac": chunk_bytes / (ms_per_chunk * 1e-3) / 1e9 / hbm},
+    }
 
 
 def run_b200(args):
@@ -666,202 +898,87 @@ def run_b200(args):
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
 
-    import fast_moss_b200 as fm
     from fast_moss_b200 import _lib
-
-    lib = _lib.load()
-    peaks, peak_src = measured_peaks()
-    x_np, books_np = workload(seed=1 + rank)
-    books = torch.from_numpy(books_np).to(dev)
-    rvq = fm.ResidualVectorQuantizer(books)
-    x = torch.from_numpy(x_np).to(dev)
-    codes = torch.empty((STAGES, FRAMES), dtype=torch.int32, device=dev)
-    recon = torch.empty((FRAMES, DIM), device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
-    stream = torch.cuda.current_stream(dev)
-    sh = stream.cuda_stream
-
-    def step():  # tensor-core kernel: one launch per step
-        st = lib.moss_rvq_encode(x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(),
-                                 rvq.packed.data_ptr(), rvq.code_norm.data_ptr(),
-                                 rvq.stats.data_ptr(), STAGES, CODES, codes.data_ptr(),
-                                 recon.data_ptr(), None, sh)
-        if st:
-            _lib.check(st, "moss_rvq_encode")
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-
-    sampler = ClockSampler(dev)
-    sampler.start()
-    time.sleep(0.3)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.time()
-    for i in range(args.steps):
-        flush.fill_(float(i))  # evict the previous step's data from L2 (untimed)
-        starts[i].record(stream)
-        step()
-        ends[i].record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    t1 = time.time()
-    kernel_s = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) * 1e-3
-    # correctness guard on the timed outputs: decode(codes) must equal recon
-    ok = bool(torch.equal(rvq.decode(codes), recon))
-    _lib.check(lib.moss_check_device_error(sh), "device error word")
-
-    # e2e through the public API with host buffers: every step's frames are
-    # copied in from pinned host memory and its codes and reconstruction
-    # copied back out; ResidualVectorQuantizer.encode_host_batches overlaps
-    # those copies with the neighbouring steps' quantization (the pipeline's
-    # fill and drain are inside the timed region)
-    e2e_steps = max(1, min(args.steps, 200))
-    nhost = 4
-    x_hosts = [torch.from_numpy(x_np).pin_memory() for _ in range(nhost)]
-    codes_hosts = [torch.empty((STAGES, FRAMES), dtype=torch.int32).pin_memory()
-                   for _ in range(nhost)]
-    recon_hosts = [torch.empty((FRAMES, DIM)).pin_memory() for _ in range(nhost)]
-
-    def e2e_run(steps):
-        rvq.encode_host_batches([x_hosts[i % nhost] for i in range(steps)],
-                                [codes_hosts[i % nhost] for i in range(steps)],
-                                [recon_hosts[i % nhost] for i in range(steps)])
-
-    e2e_run(3)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    es = torch.cuda.Event(enable_timing=True)
-    ee = torch.cuda.Event(enable_timing=True)
-    es.record(stream)
-    e2e_run(e2e_steps)
-    ee.record(stream)
-    ee.synchronize()
-    e2e_s = es.elapsed_time(ee) * 1e-3
-    ok = ok and bool(torch.equal(codes_hosts[(e2e_steps - 1) % nhost], codes.cpu()))
-
-    # the all-FFMA kernel (same codes) for comparison, same flush discipline
-    ffma_steps = max(3, min(args.steps, 50))
-    fs = [torch.cuda.Event(enable_timing=True) for _ in range(ffma_steps)]
-    fe = [torch.cuda.Event(enable_timing=True) for _ in range(ffma_steps)]
-    codes_f = torch.empty_like(codes)
-    recon_f = torch.empty_like(recon)
-    for i in range(ffma_steps + 1):
-        flush.fill_(float(i))
-        if i:
-            fs[i - 1].record(stream)
-        _lib.check(lib.moss_rvq_encode_ffma(
-            x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(), rvq.packed.data_ptr(),
-            rvq.code_norm.data_ptr(), rvq.stats.data_ptr(), STAGES, CODES, codes_f.data_ptr(),
-            recon_f.data_ptr(), None, sh), "moss_rvq_encode_ffma")
-        if i:
-            fe[i - 1].record(stream)
-    torch.cuda.synchronize()
-    ffma_s = sum(a.elapsed_time(b) for a, b in zip(fs, fe)) * 1e-3 / ffma_steps
-    ok = ok and bool(torch.equal(codes_f, codes))
-    sampler.stop()
-    clocks = sampler.summary(t0, t1)
-
     from fast_moss_b200.shards import max_over_ranks
 
-    kernel_s, e2e_s, bad = max_over_ranks([kernel_s, e2e_s, 0.0 if ok else 1.0], device=dev)
+    _lib.load()
+    peaks, peak_src = measured_peaks()
+    device_s, e2e_s, agree, clocks, details, weights, cfg = headline(torch, dist, dev, rank,
+                                                                      world, args)
+    _lib.check(_lib.load().moss_check_device_error(None), "device error word")
+    device_s, e2e_s, bad = max_over_ranks([device_s, e2e_s, 0.0 if agree else 1.0], device=dev)
 
-    kernels = None
-    if rank == 0 and not args.no_kernels:
-        kernels = kernel_lines(torch, fm, dev, peaks["hbm_gbs"])
-        kernels["rvq_reference_sequence"] = rvq_sequence_line(torch, x, rvq.books, codes,
-                                                              kernel_s / args.steps)
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        rate, threads, rows, passes, dt = cpu_rvq_rate(x_np, books_np, seconds=10.0)
-        cpu = {"value": rate * FRAME_SEC, "unit": "audio-sec/sec", "cores": threads,
-               "kind": "port",
-               "sample": f"{passes} x {rows} of {FRAMES} frames x {STAGES} stages ({dt:.1f} s, "
-                         f"oracle C port, OpenMP)"}
-    stack = None
-    if rank == 0 and not args.no_stack:
-        stack = stack_lines(torch, dev, cpu=world == 1 and not args.no_cpu)
+    extras = {}
+    if rank == 0:
+        ms_per_chunk = device_s / (args.steps * CHUNKS) * 1e3
+        extras["roofline"] = step_roofline(torch, dev, cfg, peaks, ms_per_chunk)
+        if world == 1 and not args.no_cpu:
+            cpu_weights = [{k: v.cpu() for k, v in w.items()} for w in weights]
+            rate, n, threads, dt = _cpu_stack_rate(cfg, cpu_weights, STREAMS, seconds=10.0)
+            extras["cpu_baseline"] = {
+                "value": rate, "unit": "audio-sec/sec", "cores": threads, "kind": "port",
+                "sample": f"{n} chunks of {STREAMS} streams batched ({dt:.1f} s), eager torch "
+                          f"stack (oracle/stack.py) on the host"}
+            del cpu_weights
+        del weights
+        torch.cuda.empty_cache()
+        if world == 1 and not args.no_quantizer:
+            extras["quantizer"] = quantizer_lines(torch, dev, peaks, peak_src, args.steps,
+                                                  args.warmup, cpu=not args.no_cpu)
+        if world == 1 and not args.no_kernels:
+            extras["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src,
+                                 **kernel_lines(torch, None, dev, peaks["hbm_gbs"])}
+        if world == 1 and not args.no_stack:
+            extras["stack"] = stack_variants(torch, dev)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
 
-    per_launch = kernel_s / args.steps
-    value = world * FRAMES * args.steps / kernel_s * FRAME_SEC
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    max_mhz = float(peaks.get("sm_max_mhz", 1965.0))
-    fp32_peak = sms * 128 * 2 * max_mhz * 1e6 / 1e12
-    achieved = FRAMES * FLOP_PER_FRAME / per_launch / 1e12
-    tf32_peak = float(peaks["bf16_tflops"]) / 2
-    traffic = profile_traffic("rvq_tc_kernel")
+    audio = world * STREAMS * CHUNKS * CHUNK_SEC * args.steps
     line = {
-        "metric": "audio-sec/sec (RTF), 32-stage residual VQ encode+decode",
-        "value": value,
+        "metric": METRIC,
+        "value": audio / device_s,
         "unit": "audio-sec/sec",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": per_launch * 1e3,
+        "ms_per_step": device_s / args.steps * 1e3,
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic: seeded N(0,1) frames, N(0,1)/8 codebooks",
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) features, seeded random weights (std 0.02); the "
+                "upstream checkpoint is not available",
         "config": {
-            "workload": f"rvq{STAGES}_encode_decode: {FRAMES} frames x {DIM} per GPU, "
-                        f"{STAGES} codebooks x {CODES} x {DIM}, FP32, int32 codes",
-            "frames_per_gpu": FRAMES, "audio_sec_per_frame": FRAME_SEC,
-            "l2": "flushed between timed steps (256 MiB write, untimed)",
-            "parallelism": f"dp{world} (independent frame shards, no collective)",
+            "workload": f"streaming codec stack (24 layers x 1280, 20 heads, ffn 5120, context "
+                        f"250 tokens), {STREAMS} independent batch-1 streams per GPU, "
+                        f"{CHUNKS} chunks of [1, 4, 1280] = 10 s of audio per stream per step",
+            "streams_per_gpu": STREAMS, "chunks_per_step": CHUNKS,
+            "audio_sec_per_step_per_gpu": STREAMS * CHUNKS * CHUNK_SEC,
+            "stack": "hot-path kernels of this library (residual + LayerNorm, in-kernel RoPE "
+                     "into the history ring, history attention, gated activation) + cuBLAS "
+                     "GEMMs, one CUDA graph replay per chunk",
+            "l2": "inputs larger than L2: every chunk streams 0.94 GB of bf16 weights and "
+                  "2.0 GB of history rings",
+            "parallelism": f"dp{world} (independent stream shards, no collective)",
         },
         "e2e": {
-            "value": world * FRAMES * e2e_steps / e2e_s * FRAME_SEC,
+            "value": audio / e2e_s,
             "unit": "audio-sec/sec",
-            "h2d_bytes_per_step": FRAMES * DIM * 4,
-            "d2h_bytes_per_step": STAGES * FRAMES * 4 + FRAMES * DIM * 4,
-            "api": "ResidualVectorQuantizer.encode_host_batches (C ABI moss_rvq_encode), pinned "
-                   "host buffers, copies overlapped with the neighbouring steps",
+            "h2d_bytes_per_step": details["h2d_bytes_per_chunk"] * CHUNKS,
+            "d2h_bytes_per_step": details["d2h_bytes_per_chunk"] * CHUNKS,
+            "api": "BatchedStreams: each chunk copied from pinned host memory into the graph "
+                   "input, replayed, output copied back to pinned host memory",
         },
-        "roofline": {
-            "bound": "tensor",
-            "kernel": "rvq_tc_kernel (TF32 tcgen05 screening + exact FP32 rerank)",
-            "achieved": achieved,
-            "peak": tf32_peak,
-            "unit": "TFLOP/s",
-            "frac": achieved / tf32_peak,
-            "traffic": traffic,
-            "peak_source": f"TF32 dense = 1/2 of the {peak_src} bf16 dense GEMM rate "
-                           f"({peaks['bf16_tflops']} TFLOP/s)",
-            "flop_per_launch": FRAMES * FLOP_PER_FRAME,
-            "fp32_ffma_peak": fp32_peak,
-        },
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * CHUNKS * details["native_launches_per_chunk"],
         "clocks": clocks,
         "outputs_verified": not bad,
+        **extras,
     }
-    if cpu is not None:
-        line["cpu_baseline"] = cpu
-    ffma_tflops = FRAMES * FLOP_PER_FRAME / ffma_s / 1e12
-    ffma = {"kernel": "rvq_encode_kernel (all-FFMA, identical codes)", "ms": ffma_s * 1e3,
-            "achieved_tflops": ffma_tflops, "fp32_peak_tflops": fp32_peak,
-            "frac": ffma_tflops / fp32_peak}
-    if kernels is not None:
-        line["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src,
-                           "rvq_ffma": ffma, **kernels}
-    else:
-        line["kernels"] = {"rvq_ffma": ffma}
-    if stack is not None:
-        line["stack"] = stack
     print(json.dumps(line), flush=True)
 
 

@@ -46,7 +46,7 @@ import torch
 import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
-from .graphs import GraphedCallable
+from .graphs import CapturedStep
 from .v2_pointwise import (
     gated_activation,
     history_attention,
@@ -110,17 +110,19 @@ WEIGHT_NAMES = ("norm1_w", "norm1_b", "qkv_w", "qkv_b", "out_w", "out_b", "ls1",
                 "norm2_b", "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b", "ls2")
 
 
-def init_weights(cfg, seed=2):
-    """Seeded random FP32 weights on the CPU: every matrix, bias and layer
-    scale ~ 0.02 N(0, 1); LayerNorm weights 1 + 0.02 N(0, 1), biases
-    0.02 N(0, 1).  Drawn in a fixed order, so the values do not depend on
-    the device they are later moved to."""
-    g = torch.Generator().manual_seed(seed)
+def init_weights(cfg, seed=2, device="cpu"):
+    """Seeded random FP32 weights: every matrix, bias and layer scale
+    ~ 0.02 N(0, 1); LayerNorm weights 1 + 0.02 N(0, 1), biases 0.02 N(0, 1).
+    Drawn in a fixed order by a generator on `device` (the CPU by default:
+    those values do not depend on where they are later moved; a CUDA
+    generator draws other values, much faster)."""
+    device = torch.device(device)
+    g = torch.Generator(device=device).manual_seed(seed)
     d, f = cfg.dim, cfg.ffn
     f1 = 2 * f if cfg.gated else f
 
     def n(*shape):
-        return 0.02 * torch.randn(*shape, generator=g)
+        return 0.02 * torch.randn(*shape, generator=g, device=device)
 
     layers = []
     for _ in range(cfg.layers):
@@ -235,6 +237,15 @@ class StreamingTransformer:
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
 
+    def native_launches(self, streams):
+        """Kernels of libfast_moss_b200 that one chunk step launches: the
+        first LayerNorm, then per layer the rotary (moss_rope_kv or
+        moss_qkv_rope), the history attention when it replaces SDPA, the two
+        residual + LayerNorm passes (the last layer's second is
+        moss_scale_add) and the feed-forward activation."""
+        per_layer = 4 + (1 if self.history_attention else 0)
+        return 1 + self.cfg.layers * per_layer
+
     @torch.inference_mode()
     def step(self, x, hist):
         """One chunk [streams, T, dim] FP32 through every layer; advances the
@@ -294,9 +305,12 @@ class BatchedStreams:
 
     `streams` independent streams share every weight read; `chunks_per_graph`
     chunks are captured back to back in one graph, so a replay covers
-    chunks_per_graph x 80 ms of every stream.  Each replay writes its
-    output into a static buffer; `__call__` copies it straight into a
-    buffer allocated once per call (no per-chunk clone, no concatenation).
+    chunks_per_graph x 80 ms of every stream.  The step owns a static input
+    [streams, span, dim] and a static output of the same shape: a caller
+    either writes the next features into `input` (e.g. straight from pinned
+    host memory) and calls `advance()`, or hands them to `push()`, which
+    copies them in.  `__call__` copies every replay's output straight into
+    one buffer allocated per call (no per-chunk clone, no concatenation).
     Use it on the CUDA stream and host thread that built it.
     """
 
@@ -310,27 +324,43 @@ class BatchedStreams:
         self.history = stack.history(self.streams)
         t = stack.cfg.chunk_tokens
         m = self.chunks_per_graph
+        features = torch.zeros(self.streams, self.span, stack.cfg.dim, device=stack.device)
+        out = torch.empty_like(features)
 
-        def run(features):
-            out = torch.empty_like(features)
+        def run(x):
             for c in range(m):
-                out[:, c * t:(c + 1) * t] = stack.step(features[:, c * t:(c + 1) * t],
-                                                       self.history)
+                out[:, c * t:(c + 1) * t] = stack.step(x[:, c * t:(c + 1) * t], self.history)
             return (out,)
 
-        example = torch.zeros(self.streams, self.span, stack.cfg.dim, device=stack.device)
-        self.graph = GraphedCallable(run, example)
+        self._step = CapturedStep(run, [features])
         self.history.reset()  # warm-up and capture advanced the history
+
+    @property
+    def input(self):
+        """The static input [streams, span, dim] FP32 read by the next replay."""
+        return self._step.inputs[0]
+
+    @property
+    def output(self):
+        """The static output [streams, span, dim] FP32 of the last replay."""
+        return self._step.outputs[0]
 
     def reset(self, streams=None):
         """Starts the given streams (all by default) afresh before the next replay."""
         self.history.reset(streams)
 
+    def advance(self):
+        """Advances every stream by one replay on the features already in
+        `input`; returns `output` (valid until the next replay)."""
+        return self._step.replay()[0]
+
     def push(self, features):
-        """Advances every stream by one replay: features [streams, span, dim]
-        FP32 on the device.  Returns the static output (valid until the
-        next push)."""
-        return self.graph.replay(features)[0]
+        """Copies features [streams, span, dim] FP32 (on the device) into
+        `input` and advances; returns the static output."""
+        if features.shape != self.input.shape or features.dtype != torch.float32:
+            raise ValueError(f"expected FP32 features {tuple(self.input.shape)}")
+        self.input.copy_(features)
+        return self.advance()
 
     @torch.inference_mode()
     def __call__(self, features, *, reset=True):
@@ -352,4 +382,5 @@ class BatchedStreams:
         return out[:, :n]
 
     def release(self):
-        self.graph.release()
+        """Drops the captured graph and its static buffers."""
+        self._step.release()

@@ -1,51 +1,86 @@
-"""Fixed-frame offline encode/decode adapters for native stereo v2.
+"""Offline (whole-clip) encode and decode of native 48 kHz stereo clips.
 
-Same contract as fast_moss/v2_codec.py:8-61: complete 3840-sample frames
-only, valid code lengths known from the shape (no host sync), and the
-upstream arithmetic unchanged around the optimized modules.
+Drop-in for fast_moss/v2_codec.py: `encode_fixed(model, audio)` and
+`codec(model, audio)`, plus the complete-frame encoder step
+`_encode_complete` that StreamingCodec captures and replays.  A batch is
+admitted only as whole 80 ms frames (3840 samples) of stereo audio, so
+every code length follows from the tensor shape and nothing waits on the
+device.  The upstream model's own modules do the arithmetic; inside
+`optimized(model)` their patched methods run the B200 kernels.
 """
 
-import sys
+import importlib
+from dataclasses import dataclass
 
 import torch
 
-FRAME = 3840
+FRAME = 3840  # samples per codec frame: 80 ms at 48 kHz
+
+
+@dataclass(frozen=True)
+class ClipSpec:
+    """The clips the fixed-frame adapters accept: `channels`-channel audio
+    at `rate` Hz in whole frames of `frame` samples, on a model built for
+    that rate and channel count with SDPA attention."""
+
+    rate: int = 48000
+    channels: int = 2
+    frame: int = FRAME
+
+    def refusal(self, model, audio):
+        """Why `audio` [B, C, T] cannot be encoded as fixed frames, or None."""
+        if audio.ndim != 3 or audio.shape[0] < 1 or audio.shape[1] != self.channels:
+            return f"expected a B,{self.channels},T batch of clips, got {tuple(audio.shape)}"
+        samples = audio.shape[-1]
+        if samples < self.frame or samples % self.frame:
+            return (f"clips must hold whole {self.frame}-sample frames, got {samples} samples "
+                    f"per channel")
+        if model.sampling_rate != self.rate or model.number_channels != self.channels:
+            return f"the model is not a {self.rate} Hz {self.channels}-channel codec"
+        if model.attention_implementation != "sdpa":
+            return "the fixed-frame path is validated with SDPA attention only"
+        return None
+
+
+STEREO_48K = ClipSpec()
+
+
+def _encoder_output_type(model):
+    """The upstream module's encoder-output record class."""
+    return importlib.import_module(type(model).__module__).MossAudioTokenizerEncoderOutput
+
+
+def _encode_complete(model, audio):
+    """Encoder and quantizer over complete frames of `audio` [B, 2, T]
+    (also valid inside a live stream, which StreamingCodec relies on).
+    Every clip has the full length, so the lengths are a constant tensor."""
+    full = torch.full((audio.shape[0],), audio.shape[-1], device=audio.device, dtype=torch.long)
+    hidden, lengths = model._flatten_channels_for_codec(audio, full)
+    with model._codec_inference_autocast():
+        for block in model.encoder:
+            hidden, lengths = block(hidden, lengths)
+    hidden = hidden.float()  # the quantizer runs in FP32 (its autocast is off)
+    _, codes, code_lengths = model.quantizer(hidden, lengths, None)
+    return _encoder_output_type(model)(audio_codes=codes, audio_codes_lengths=code_lengths,
+                                       encoder_hidden_states=hidden)
 
 
 @torch.no_grad()
 def encode_fixed(model, audio):
-    """Graph-safe full-frame v2 encoding of complete equal-length stereo clips."""
-    if (
-        audio.ndim != 3
-        or audio.shape[1] != 2
-        or audio.shape[0] < 1
-        or audio.shape[-1] < FRAME
-        or audio.shape[-1] % FRAME
-        or model.sampling_rate != 48000
-        or model.number_channels != 2
-        or model.attention_implementation != "sdpa"
-    ):
-        raise ValueError("Expected complete equal-length B,2,T 48 kHz stereo frames with SDPA")
+    """Encodes a batch of equal-length stereo clips of whole frames; safe
+    to capture in a CUDA graph (no host synchronisation)."""
+    reason = STEREO_48K.refusal(model, audio)
+    if reason is not None:
+        raise ValueError(reason)
     if any(getattr(m, "is_streaming", False) for m in model.modules()):
-        raise RuntimeError("Fixed v2 graphs are offline; use StreamingCodec for stateful input")
+        raise RuntimeError("a streaming session is active on this model; fixed-frame encoding is "
+                           "offline only (use StreamingCodec for stateful input)")
     return _encode_complete(model, audio)
 
 
-def _encode_complete(model, audio):
-    """Native arithmetic for complete frames, including an active stream."""
-    lengths = torch.full((audio.shape[0],), audio.shape[-1], device=audio.device,
-                         dtype=torch.long)
-    hidden, lengths = model._flatten_channels_for_codec(audio, lengths)
-    with model._codec_inference_autocast():
-        for module in model.encoder:
-            hidden, lengths = module(hidden, lengths)
-    _, codes, code_lengths = model.quantizer(hidden.float(), lengths, None)
-    output_type = sys.modules[type(model).__module__].MossAudioTokenizerEncoderOutput
-    return output_type(audio_codes=codes, audio_codes_lengths=code_lengths,
-                       encoder_hidden_states=hidden.float())
-
-
 def codec(model, audio):
-    """Return owned-by-caller codes, hidden states and stereo reconstruction."""
-    enc = encode_fixed(model, audio)
-    return enc.audio_codes, enc.encoder_hidden_states, model._decode_frame(enc.audio_codes).audio
+    """(codes, encoder hidden states, reconstruction) of `audio`, all owned
+    by the caller."""
+    encoded = encode_fixed(model, audio)
+    decoded = model._decode_frame(encoded.audio_codes)
+    return encoded.audio_codes, encoded.encoder_hidden_states, decoded.audio

@@ -1,42 +1,58 @@
-"""Reversible B200 optimizations for the pinned 48 kHz stereo v2 checkpoint.
+"""Reversible B200 optimisations of the pinned 48 kHz stereo v2 model.
 
 Drop-in for fast_moss/v2_runtime.py: `optimized(model, cache_linear=True,
-quantizer=True, pointwise=True)` patches the same upstream methods
-(:309-413) under the same guards, falls back to the original method in the
-same situations, restores everything on exit and keeps the same
-single-owner-thread rules.  What runs behind the patch points:
+quantizer=True, pointwise=True)` replaces the same upstream methods, runs
+the B200 path only on the calls the reference's own path covers (every
+other call goes to the original method, as in the reference), restores
+everything when it closes and keeps the reference's single-owner-thread
+rule.
 
-  transformer layer (:231-276): LayerNorm -> attention -> ONE kernel for
-      the residual + layer scale + next LayerNorm -> FFN -> residual kernel;
-      every result bit-identical to the reference's scale_add + torch LN;
-  rotary forward (:186-224): ONE kernel computing the phase, cos/sin and
-      the rotation (no tables in HBM, nothing to warm before capture);
+Design.  Each optimisation is one row of PATCHES (a `PatchSpec`): the
+modules it applies to, the method it replaces, the `optimized()` switch
+that enables it, and a builder.  A builder returns a `_Guarded` method: a
+coverage predicate over the call's arguments and the B200 path for the
+calls it covers.  The runtime walks the model once on entry, installs the
+methods of every matching row as instance attributes, and on exit removes
+them in reverse order.  What runs behind the rows:
+
+  transformer layer (reference :231-276): LayerNorm -> attention -> ONE
+      kernel for the residual + layer scale + next LayerNorm -> FFN ->
+      residual kernel; bit-identical to the reference's scale_add + torch LN;
+  rotary embedding (:186-224): ONE kernel computing the phase, cos/sin and
+      the rotation (no tables in HBM);
   LFQ decode_latents (:143-181): the reference's prepare + FP32 GEMM +
       select sequence, or (fused_lfq=True) one kernel that never writes the
       [B*T, K] dot-product matrix;
-  Linear / weight-norm Conv1d (:77-138): the reference's cached BF16
-      weights and precomputed convolution weights (library GEMM / conv).
+  Linear / weight-norm Conv1d (:77-138): cached bf16 weights and the
+      materialised convolution weight (library GEMM / convolution).
+
+Cached resources (bf16 weights, normalised codebooks, conv weights) belong
+to the runtime; it holds a `graphs.ResourceLease` for its device while open,
+so CUDA graphs captured inside the context stop replaying once it closes.
 """
 
+from collections import Counter
 from contextlib import contextmanager
+from dataclasses import dataclass
 from threading import get_ident
-from types import MethodType
+from typing import Callable, Optional
 
 import torch
 import torch.nn.functional as F
 from torch.nn.modules import module as module_hooks
 
-from . import _lib, storage_epoch
+from . import _lib, graphs
 from .v2_loading import REVISION
-
-_LINEAR_FORWARD = torch.nn.Linear.forward
 
 # Compute capability of the B200 (sm_100) the kernels are built for.
 SUPPORTED_CAPABILITY = (10, 0)
+_FLOATS = (torch.bfloat16, torch.float32)
+_LINEAR_FORWARD = torch.nn.Linear.forward
 
 
 def validate(model):
-    """Checks the pinned checkpoint and an sm_100 device (reference :18-41)."""
+    """The pinned 48 kHz stereo checkpoint on an sm_100 device with SDPA
+    (the reference's checks, :18-41, with B200 in place of its GPU pin)."""
     if (
         type(model).__name__ != "MossAudioTokenizerModel"
         or getattr(model.config, "_commit_hash", None) != REVISION
@@ -57,24 +73,266 @@ def validate(model):
     _lib.load()
 
 
-def _norm_params_ok(norm, x):
-    """A stock LayerNorm over x's last dim whose torch CUDA forward takes the
-    vectorised path the kernels reproduce."""
-    if type(norm) is not torch.nn.LayerNorm or norm._forward_hooks or norm._forward_pre_hooks:
+def _needs_grad(*tensors):
+    return torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tensors)
+
+
+def _global_hooks():
+    return bool(module_hooks._global_forward_hooks or module_hooks._global_forward_pre_hooks)
+
+
+def _hooked(module):
+    return bool(module._forward_hooks or module._forward_pre_hooks)
+
+
+def _class_method(module, name):
+    """True while `module.<name>` is still its class's own method."""
+    return getattr(getattr(module, name), "__func__", None) is getattr(type(module), name)
+
+
+def _stock_norm(norm, x):
+    """A hook-free stock LayerNorm over x's last dimension whose torch CUDA
+    forward is the vectorised path the kernels reproduce bit for bit."""
+    if type(norm) is not torch.nn.LayerNorm or _hooked(norm):
         return False
     if tuple(norm.normalized_shape) != (x.shape[-1],) or x.shape[-1] % 4:
         return False
-    for p in (norm.weight, norm.bias):
-        if p is not None and (
-            p.dtype != torch.float32 or p.device != x.device or not p.is_contiguous()
-            or p.data_ptr() % 16
-        ):
+    return all(p is None or (p.dtype == torch.float32 and p.device == x.device
+                             and p.is_contiguous() and p.data_ptr() % 16 == 0)
+               for p in (norm.weight, norm.bias))
+
+
+class _Guarded:
+    """A replacement method: calls that `covers(*args, **kwargs)` accepts
+    take `fast`, all others the module's original method."""
+
+    def __init__(self, runtime, original, covers, fast):
+        self.runtime = runtime
+        self.original = original
+        self.covers = covers
+        self.fast = fast
+
+    def __call__(self, *args, **kwargs):
+        self.runtime._check()
+        if self.covers(*args, **kwargs):
+            return self.fast(*args, **kwargs)
+        return self.original(*args, **kwargs)
+
+
+# ------------------------------------------------------------ patch builders
+def _build_linear(rt, module, original):
+    weight, bias = module.weight, module.bias
+    versions = (weight._version, None if bias is None else bias._version)
+    w16 = weight.to(torch.bfloat16)
+    b16 = None if bias is None else bias.to(torch.bfloat16)
+    rt.counts["cached_bytes"] += w16.numel() * 2 + (0 if b16 is None else b16.numel() * 2)
+
+    def covers(x):
+        return (module.weight is weight and module.bias is bias
+                and (weight._version, None if bias is None else bias._version) == versions
+                and x.device == rt.device and x.dtype in _FLOATS
+                and torch.is_autocast_enabled("cuda")
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16
+                and not _needs_grad(x, weight, bias))
+
+    def fast(x):
+        rt.counts["linear_calls"] += 1
+        return F.linear(x, w16, b16)
+
+    return _Guarded(rt, original, covers, fast)
+
+
+def _build_conv(rt, module, original):
+    weight = module.weight.detach()  # the parametrisation, evaluated once
+    params = tuple(module.parametrizations.weight.parameters())
+    versions = tuple(p._version for p in params)
+    rt.counts["cached_bytes"] += weight.numel() * weight.element_size()
+
+    def covers(x):
+        if not torch.nn.utils.parametrize.is_parametrized(module, "weight"):
             return False
-    return True
+        now = tuple(module.parametrizations.weight.parameters())
+        return (len(now) == len(params) and all(a is b for a, b in zip(now, params))
+                and tuple(p._version for p in params) == versions
+                and not _global_hooks()
+                and not any(_hooked(m) for m in module.parametrizations.modules())
+                and not _needs_grad(x, *params))
+
+    def fast(x):
+        return module._conv_forward(x, weight, module.bias)
+
+    return _Guarded(rt, original, covers, fast)
+
+
+def _build_lfq(rt, module, original):
+    from .quantizer import decode_latents, select
+    from .quantizer_prepare import prepare
+
+    weight = module.codebook.weight
+    version = weight._version
+    book = F.normalize(weight.float())  # normalised once, as the reference does
+    code_norm = book.pow(2).sum(1, keepdim=True).T
+    rt.counts["cached_bytes"] += book.numel() * 4 + code_norm.numel() * 4
+
+    def covers(x):
+        return (module.codebook.weight is weight and weight._version == version
+                and x.ndim == 3 and x.shape[1] == 8 and x.shape[0] >= 1 and x.shape[2] >= 1
+                and x.device == rt.device and x.dtype == torch.float32
+                and not torch.is_autocast_enabled("cuda") and not _needs_grad(x, weight))
+
+    def fast(x):
+        if x.is_contiguous() and x.numel() < 2 ** 31:
+            if rt.fused_lfq:
+                rt.counts["select_calls"] += 1
+                return decode_latents(x, book, code_norm, weight)
+            _, row_norm, twice, _ = prepare(x)
+            rt.counts["prepare_calls"] += 1
+        else:  # other layouts: the reference's eager normalisation
+            latent = F.normalize(x.transpose(1, 2).reshape(-1, 8).float())
+            row_norm = latent.pow(2).sum(1, keepdim=True)
+            twice = 2 * latent
+        rt.counts["select_calls"] += 1
+        return select(twice @ book.T, row_norm, code_norm, weight, x)
+
+    return _Guarded(rt, original, covers, fast)
+
+
+def _build_rotary(rt, module, original):
+    from .v2_pointwise import rope
+
+    period = module.max_period
+
+    def covers(q, k, offset, time_before_heads=False):
+        return (not time_before_heads and q.ndim == 4 and q.shape == k.shape
+                and q.shape[-1] >= 2 and q.shape[-1] % 2 == 0
+                and q.dtype in _FLOATS and k.dtype == q.dtype
+                and q.device == rt.device and k.device == rt.device
+                and offset.device == rt.device and offset.numel() == q.shape[0]
+                and module.max_period == period and not _needs_grad(q, k, offset))
+
+    def fast(q, k, offset, time_before_heads=False):
+        rt.counts["rope_calls"] += 1
+        return rope(q, k, offset.reshape(-1), period)
+
+    return _Guarded(rt, original, covers, fast)
+
+
+def _build_layer(rt, module, original):
+    from .v2_pointwise import layer_norm, residual_layer_norm, scale_add
+
+    scales = (module.layer_scale_1, module.layer_scale_2)
+    scale_forwards = tuple(type(s).forward for s in scales)
+
+    def covers(x, **kwargs):
+        if (torch.is_grad_enabled() or x.device != rt.device or x.dtype not in _FLOATS
+                or module.layer_scale_1 is not scales[0]
+                or module.layer_scale_2 is not scales[1] or _global_hooks()):
+            return False
+        return all(not _hooked(s) and s.channel_last
+                   and getattr(s.forward, "__func__", None) is fn
+                   and s.scale.dtype == torch.float32 and s.scale.device == rt.device
+                   for s, fn in zip(scales, scale_forwards))
+
+    def norm(norm_module, x):
+        if x.dtype == torch.float32 and x.is_cuda and _stock_norm(norm_module, x):
+            try:
+                out = layer_norm(x, norm_module.weight, norm_module.bias, norm_module.eps)
+                rt.counts["norm_calls"] += 1
+                return out
+            except _lib.UnsupportedError:
+                pass
+        return norm_module(x)
+
+    def kernel_residual(normed, residual, update, scale):
+        return (normed.dtype == torch.float32 and update.dtype in _FLOATS
+                and residual.shape == update.shape and scale.scale.shape == (residual.shape[-1],)
+                and residual.is_contiguous() and update.is_contiguous()
+                and scale.scale.is_contiguous())
+
+    def fast(x, **kwargs):
+        # attention half; its residual update fused with the next LayerNorm
+        normed = norm(module.norm1, x)
+        update = module.self_attn(normed, **kwargs)
+        normed2 = None
+        if kernel_residual(normed, x, update, scales[0]):
+            if _stock_norm(module.norm2, x):
+                try:
+                    x_next, normed2 = residual_layer_norm(
+                        x, update, scales[0].scale, module.norm2.weight, module.norm2.bias,
+                        module.norm2.eps)
+                    rt.counts["fused_norm_calls"] += 1
+                except _lib.UnsupportedError:
+                    normed2 = None
+            if normed2 is None:
+                x_next = scale_add(x, update, scales[0].scale)
+            rt.counts["residual_calls"] += 1
+        else:  # the reference's eager form
+            x_next = x.to(normed) + scales[0](update)
+        x = x_next
+        # feed-forward half
+        if normed2 is None:
+            normed2 = norm(module.norm2, x)
+        update = module.ffn(normed2)
+        if kernel_residual(normed2, x, update, scales[1]):
+            rt.counts["residual_calls"] += 1
+            return scale_add(x, update, scales[1].scale)
+        return x.to(normed2) + scales[1](update)
+
+    return _Guarded(rt, original, covers, fast)
+
+
+# ------------------------------------------------------------ the patch table
+@dataclass(frozen=True)
+class PatchSpec:
+    """One optimisation: `matches(module)` selects the modules, `method` is
+    the attribute replaced, `option` the optimized() switch that enables it
+    (None: always on), `build(runtime, module, original)` the replacement."""
+
+    key: str
+    method: str
+    option: Optional[str]
+    matches: Callable[[torch.nn.Module], bool]
+    build: Callable
+
+
+def _is_rotary(m):
+    return type(m).__name__ == "MossAudioTokenizerRotaryEmbedding"
+
+
+def _is_layer(m):
+    return (type(m).__name__ == "MossAudioTokenizerTransformerLayer"
+            and type(m.norm1) is torch.nn.LayerNorm and type(m.norm2) is torch.nn.LayerNorm
+            and all(type(s).__name__ == "MossAudioTokenizerLayerScale"
+                    for s in (m.layer_scale_1, m.layer_scale_2)))
+
+
+def _is_linear(m):
+    return type(m) is torch.nn.Linear and torch.nn.Linear.forward is _LINEAR_FORWARD
+
+
+def _is_weight_norm_conv(m):
+    return (isinstance(m, torch.nn.Conv1d)
+            and torch.nn.utils.parametrize.is_parametrized(m, "weight")
+            and getattr(m.forward, "__func__", None) is torch.nn.Conv1d.forward)
+
+
+def _is_lfq(m):
+    return type(m).__name__ == "MossAudioTokenizerLFQ"
+
+
+PATCHES = (
+    PatchSpec("rope", "forward", "pointwise", _is_rotary, _build_rotary),
+    PatchSpec("residual", "forward", "pointwise", _is_layer, _build_layer),
+    PatchSpec("linear", "forward", "cache_linear", _is_linear, _build_linear),
+    PatchSpec("conv", "forward", None, _is_weight_norm_conv, _build_conv),
+    PatchSpec("quantizer", "decode_latents", "quantizer", _is_lfq, _build_lfq),
+)
 
 
 class V2Runtime:
-    """Single-host-thread owner; original FP32 parameters remain in place."""
+    """The optimisation context of one model: single host thread, original
+    FP32 parameters left in place.  Counters: `<key>_modules` per patch
+    row, `*_calls` per B200 path taken, `cached_bytes`."""
 
     def __init__(self, model, *, cache_linear=True, quantizer=True, pointwise=True,
                  fused_lfq=False):
@@ -82,315 +340,67 @@ class V2Runtime:
         self.model = model
         self.device = next(model.parameters()).device
         self.thread = get_ident()
-        self.cache_linear = cache_linear
-        self.quantizer = quantizer
-        self.pointwise = pointwise
+        self.options = {"cache_linear": cache_linear, "quantizer": quantizer,
+                        "pointwise": pointwise}
         self.fused_lfq = fused_lfq
+        self.counts = Counter()
         self.active = self.used = False
-        self.saved = []
-        self.cached_bytes = self.linear_calls = self.prepare_calls = self.select_calls = 0
-        self.linear_modules = self.conv_modules = self.quantizer_modules = 0
-        self.rope_modules = self.residual_modules = self.rope_calls = self.residual_calls = 0
-        self.norm_calls = self.fused_norm_calls = 0
+        self.lease = None
+        self._installed = []  # (module, method, previous own attribute or None)
+
+    def __getattr__(self, name):
+        counts = self.__dict__.get("counts")
+        if counts is not None and (name.endswith(("_calls", "_modules"))
+                                   or name == "cached_bytes"):
+            return counts[name]
+        raise AttributeError(name)
 
     def _check(self):
         if not self.active or get_ident() != self.thread:
             raise RuntimeError("Use v2 optimizations on their active owner thread")
 
-    def _replace(self, module, name, value):
-        self.saved.append((module, name, name in module.__dict__, module.__dict__.get(name)))
-        setattr(module, name, value)
-
-    # ----------------------------------------------------------- Linear/Conv
-    def _linear(self, original, weight, bias, cached_weight, cached_bias):
-        versions = (weight._version, bias._version if bias is not None else None)
-
-        def forward(module, x):
-            self._check()
-            if (
-                module.weight is not weight
-                or module.bias is not bias
-                or weight._version != versions[0]
-                or (bias is not None and bias._version != versions[1])
-                or x.device != self.device
-                or x.dtype not in (torch.float32, torch.bfloat16)
-                or not torch.is_autocast_enabled("cuda")
-                or torch.get_autocast_dtype("cuda") != torch.bfloat16
-                or (
-                    torch.is_grad_enabled()
-                    and (x.requires_grad or weight.requires_grad
-                         or (bias is not None and bias.requires_grad))
-                )
-            ):
-                return original(x)
-            self.linear_calls += 1
-            return F.linear(x, cached_weight, cached_bias)
-
-        return forward
-
-    def _conv(self, original, weight, parameters):
-        versions = tuple(p._version for p in parameters)
-
-        def forward(module, x):
-            self._check()
-            current = (
-                tuple(module.parametrizations.weight.parameters())
-                if torch.nn.utils.parametrize.is_parametrized(module, "weight")
-                else ()
-            )
-            if (
-                len(current) != len(parameters)
-                or any(a is not b for a, b in zip(current, parameters))
-                or any(p._version != v for p, v in zip(parameters, versions))
-                or module_hooks._global_forward_hooks
-                or module_hooks._global_forward_pre_hooks
-                or any(m._forward_hooks or m._forward_pre_hooks
-                       for m in module.parametrizations.modules())
-                or (torch.is_grad_enabled()
-                    and (x.requires_grad or any(p.requires_grad for p in parameters)))
-            ):
-                return original(x)
-            return module._conv_forward(x, weight, module.bias)
-
-        return forward
-
-    # ------------------------------------------------------------ quantizer
-    def _decode(self, original, weight, book, norm):
-        version = weight._version
-        from .quantizer import decode_latents, select
-        from .quantizer_prepare import prepare
-
-        def decode(module, x):
-            self._check()
-            if (
-                module.codebook.weight is not weight
-                or weight._version != version
-                or x.ndim != 3
-                or x.shape[1] != 8
-                or x.device != self.device
-                or x.dtype != torch.float32
-                or x.shape[0] < 1
-                or x.shape[2] < 1
-                or torch.is_autocast_enabled("cuda")
-                or (torch.is_grad_enabled() and (x.requires_grad or weight.requires_grad))
-            ):
-                return original(x)
-            if x.is_contiguous() and x.numel() <= 2147483647:
-                if self.fused_lfq:
-                    self.select_calls += 1
-                    return decode_latents(x, book, norm, weight)
-                _, row_norm, twice, _ = prepare(x)
-                self.prepare_calls += 1
-            else:
-                # the reference's eager normalisation for other layouts
-                enc = F.normalize(x.transpose(1, 2).reshape(-1, 8).float())
-                row_norm = enc.pow(2).sum(1, keepdim=True)
-                twice = 2 * enc
-            dots = twice @ book.T
-            self.select_calls += 1
-            return select(dots, row_norm, norm, weight, x)
-
-        return decode
-
-    # ---------------------------------------------------------------- rotary
-    def _rope(self, original, period):
-        from .v2_pointwise import rope
-
-        def forward(module, q, k, offset, time_before_heads=False):
-            self._check()
-            if (
-                time_before_heads
-                or q.ndim != 4
-                or q.shape != k.shape
-                or q.shape[-1] % 2
-                or q.shape[-1] < 2
-                or q.dtype not in (torch.bfloat16, torch.float32)
-                or k.dtype != q.dtype
-                or q.device != self.device
-                or k.device != self.device
-                or offset.device != self.device
-                or offset.numel() != q.shape[0]
-                or module.max_period != period
-                or (torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, offset)))
-            ):
-                return original(q, k, offset, time_before_heads)
-            self.rope_calls += 1
-            return rope(q, k, offset.reshape(-1), period)
-
-        return forward
-
-    # ----------------------------------------------------- transformer layer
-    def _layer(self, original, scales):
-        forwards = tuple(type(s).forward for s in scales)
-        from .v2_pointwise import layer_norm, residual_layer_norm, scale_add
-
-        def norm_of(norm, x):
-            if x.dtype == torch.float32 and x.is_cuda and _norm_params_ok(norm, x):
-                try:
-                    out = layer_norm(x, norm.weight, norm.bias, norm.eps)
-                    self.norm_calls += 1
-                    return out
-                except _lib.UnsupportedError:
-                    pass
-            return norm(x)
-
-        def fusable(normed, residual, update, scale):
-            return (
-                normed.dtype == torch.float32
-                and update.dtype in (torch.bfloat16, torch.float32)
-                and residual.shape == update.shape
-                and scale.scale.shape == (residual.shape[-1],)
-                and all(t.is_contiguous() for t in (residual, update, scale.scale))
-            )
-
-        def forward(module, x, **kwargs):
-            self._check()
-            if (
-                torch.is_grad_enabled()
-                or x.device != self.device
-                or x.dtype not in (torch.bfloat16, torch.float32)
-                or module.layer_scale_1 is not scales[0]
-                or module.layer_scale_2 is not scales[1]
-                or module_hooks._global_forward_hooks
-                or module_hooks._global_forward_pre_hooks
-                or any(
-                    s._forward_hooks
-                    or s._forward_pre_hooks
-                    or not s.channel_last
-                    or getattr(s.forward, "__func__", None) is not fn
-                    or s.scale.dtype != torch.float32
-                    or s.scale.device != self.device
-                    for s, fn in zip(scales, forwards)
-                )
-            ):
-                return original(x, **kwargs)
-            # attention half
-            residual = x
-            normed = norm_of(module.norm1, x)
-            update = module.self_attn(normed, **kwargs)
-            normed2 = None
-            if fusable(normed, residual, update, scales[0]):
-                if _norm_params_ok(module.norm2, residual):
-                    try:
-                        x, normed2 = residual_layer_norm(
-                            residual, update, scales[0].scale, module.norm2.weight,
-                            module.norm2.bias, module.norm2.eps)
-                        self.fused_norm_calls += 1
-                    except _lib.UnsupportedError:
-                        normed2 = None
-                if normed2 is None:
-                    x = scale_add(residual, update, scales[0].scale)
-                self.residual_calls += 1
-            else:
-                x = residual.to(normed) + scales[0](update)
-            # feed-forward half
-            residual = x
-            if normed2 is None:
-                normed2 = norm_of(module.norm2, x)
-            update = module.ffn(normed2)
-            if fusable(normed2, residual, update, scales[1]):
-                x = scale_add(residual, update, scales[1].scale)
-                self.residual_calls += 1
-            else:
-                x = residual.to(normed2) + scales[1](update)
-            return x
-
-        return forward
-
-    # ------------------------------------------------------------- lifecycle
-    def __enter__(self):
-        if (
-            self.used
-            or getattr(self.model, "_fast_v2_runtime", None) is not None
-            or getattr(self.model, "_fast_optimization_active", False)
-        ):
+    def _admit(self):
+        if (self.used or getattr(self.model, "_fast_v2_runtime", None) is not None
+                or getattr(self.model, "_fast_optimization_active", False)):
             raise RuntimeError("V2 optimization context is already active or has been used")
         if get_ident() != self.thread:
             raise RuntimeError("Enter v2 optimization on its construction host thread")
-        if self.model.training or any(
-            p.requires_grad or p.dtype != torch.float32 or p.device != self.device
-            for p in self.model.parameters()
-        ):
+        if self.model.training or any(p.requires_grad or p.dtype != torch.float32
+                                      or p.device != self.device
+                                      for p in self.model.parameters()):
             raise ValueError("V2 optimizations require a frozen FP32 checkpoint on one CUDA device")
         if any(getattr(m, "is_streaming", False) for m in self.model.modules()):
             raise RuntimeError("Enter v2 optimization before starting streaming")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("Enter v2 optimization before CUDA graph capture")
+
+    def __enter__(self):
         with torch.cuda.device(self.device):
-            if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError("Enter v2 optimization before CUDA graph capture")
+            self._admit()
             torch.cuda.synchronize(self.device)
-            storage_epoch.advance(self.device, context=True)
+        self.lease = graphs.open_lease(self.device, self)
         self.active = self.used = True
         self.model._fast_v2_runtime = self
         try:
             with torch.inference_mode(), torch.autocast("cuda", enabled=False):
                 for module in self.model.modules():
-                    self._patch(module)
-            return self
+                    self._install(module)
         except BaseException:
             self.close()
             raise
+        return self
 
-    def _patch(self, module):
-        name = type(module).__name__
-        if (
-            self.pointwise
-            and name == "MossAudioTokenizerRotaryEmbedding"
-            and getattr(module.forward, "__func__", None) is type(module).forward
-        ):
-            self._replace(module, "forward",
-                          MethodType(self._rope(module.forward, module.max_period), module))
-            self.rope_modules += 1
-        if (
-            self.pointwise
-            and name == "MossAudioTokenizerTransformerLayer"
-            and getattr(module.forward, "__func__", None) is type(module).forward
-            and type(module.norm1) is torch.nn.LayerNorm
-            and type(module.norm2) is torch.nn.LayerNorm
-            and all(type(s).__name__ == "MossAudioTokenizerLayerScale"
-                    for s in (module.layer_scale_1, module.layer_scale_2))
-        ):
-            self._replace(module, "forward", MethodType(
-                self._layer(module.forward, (module.layer_scale_1, module.layer_scale_2)),
-                module))
-            self.residual_modules += 1
-        if (
-            self.cache_linear
-            and type(module) is torch.nn.Linear
-            and torch.nn.Linear.forward is _LINEAR_FORWARD
-            and getattr(module.forward, "__func__", None) is _LINEAR_FORWARD
-        ):
-            weight, bias = module.weight, module.bias
-            cached_weight = weight.to(torch.bfloat16)
-            cached_bias = bias.to(torch.bfloat16) if bias is not None else None
-            self.cached_bytes += cached_weight.numel() * 2 + (
-                cached_bias.numel() * 2 if cached_bias is not None else 0)
-            self._replace(module, "forward", MethodType(
-                self._linear(module.forward, weight, bias, cached_weight, cached_bias), module))
-            self.linear_modules += 1
-        if (
-            isinstance(module, torch.nn.Conv1d)
-            and torch.nn.utils.parametrize.is_parametrized(module, "weight")
-            and getattr(module.forward, "__func__", None) is torch.nn.Conv1d.forward
-        ):
-            weight = module.weight.detach()
-            parameters = tuple(module.parametrizations.weight.parameters())
-            self._replace(module, "forward",
-                          MethodType(self._conv(module.forward, weight, parameters), module))
-            self.cached_bytes += weight.numel() * weight.element_size()
-            self.conv_modules += 1
-        if (
-            self.quantizer
-            and name == "MossAudioTokenizerLFQ"
-            and getattr(module.decode_latents, "__func__", None) is type(module).decode_latents
-        ):
-            weight = module.codebook.weight
-            book = F.normalize(weight.float())
-            norm = book.pow(2).sum(1, keepdim=True).T
-            self._replace(module, "decode_latents",
-                          MethodType(self._decode(module.decode_latents, weight, book, norm),
-                                     module))
-            self.cached_bytes += book.numel() * 4 + norm.numel() * 4
-            self.quantizer_modules += 1
+    def _install(self, module):
+        for spec in PATCHES:
+            if spec.option is not None and not self.options[spec.option]:
+                continue
+            if not spec.matches(module) or not _class_method(module, spec.method):
+                continue
+            original = getattr(module, spec.method)
+            replacement = spec.build(self, module, original)
+            self._installed.append((module, spec.method, module.__dict__.get(spec.method)))
+            setattr(module, spec.method, replacement)
+            self.counts[f"{spec.key}_modules"] += 1
 
     def close(self):
         if not self.active:
@@ -398,13 +408,14 @@ class V2Runtime:
         try:
             torch.cuda.synchronize(self.device)
         finally:
-            storage_epoch.advance(self.device, context=True)
-            for module, name, existed, old in reversed(self.saved):
-                if existed:
-                    setattr(module, name, old)
+            if self.lease is not None:
+                graphs.close_lease(self.lease)
+            for module, method, previous in reversed(self._installed):
+                if previous is None:
+                    module.__dict__.pop(method, None)
                 else:
-                    delattr(module, name)
-            self.saved.clear()
+                    setattr(module, method, previous)
+            self._installed.clear()
             self.model.__dict__.pop("_fast_v2_runtime", None)
             self.active = False
 
@@ -414,8 +425,8 @@ class V2Runtime:
 
 @contextmanager
 def optimized(model, *, cache_linear=True, quantizer=True, pointwise=True, fused_lfq=False):
-    """Cache native casts and run the exact B200 quantizer, rotary, residual
-    and LayerNorm kernels (reference fast_moss/v2_runtime.py:441-447)."""
+    """Runs the model's hot path on the B200 kernels inside the context
+    (reference fast_moss/v2_runtime.py:441-447)."""
     with V2Runtime(model, cache_linear=cache_linear, quantizer=quantizer, pointwise=pointwise,
                    fused_lfq=fused_lfq) as runtime:
         yield runtime

@@ -1,6 +1,6 @@
 """The one-JSON-line output of bench.py: the reference arm on the CPU, the
-B200 arm on a GPU (a few steps, without the optional kernel, stack and CPU
-sections)."""
+B200 arm on a GPU (a few steps, without the optional quantizer, kernel,
+stack and CPU sections)."""
 
 import json
 import os
@@ -29,7 +29,7 @@ def _common(line, steps, warmup):
     assert line["higher_is_better"] is True
     assert line["scaling"] == "weak"
     assert line["vs_baseline"] is None
-    assert line["dtype"] == "f32"
+    assert line["dtype"] == "bf16"
     assert "synthetic" in line["data"]
     assert "workload" in line["config"]
     e2e = line["e2e"]
@@ -49,8 +49,9 @@ def test_reference_arm_line():
 
 @pytest.mark.gpu
 def test_b200_arm_line(cuda_device):
-    line = _run_bench("--steps", "3", "--warmup", "3", "--no-cpu", "--no-stack", "--no-kernels")
-    _common(line, 3, 3)
+    line = _run_bench("--steps", "2", "--warmup", "3", "--no-cpu", "--no-stack", "--no-kernels",
+                      "--no-quantizer")
+    _common(line, 2, 3)
     assert "impl" not in line
     roof = line["roofline"]
     assert roof["bound"] in ("hbm", "tensor")
@@ -58,7 +59,9 @@ def test_b200_arm_line(cuda_device):
     assert roof["achieved"] > 0 and roof["peak"] > 0
     assert roof["frac"] == pytest.approx(roof["achieved"] / roof["peak"])
     assert "traffic" in roof
-    assert line["gpu_launches"] == 3
+    # 125 chunks per step, 121 library kernels per chunk (1 + 24 layers x 5)
+    assert line["gpu_launches"] == 2 * 125 * 121
+    assert line["roofline"]["step"]["frac"] > 0
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= set(line["clocks"])
     assert line["outputs_verified"] is True
     assert line["e2e"]["h2d_bytes_per_step"] > 0 and line["e2e"]["d2h_bytes_per_step"] > 0

@@ -110,3 +110,31 @@ def test_qkv_rope_validation(moss, cuda_device):
                       torch.zeros(1, 3, device=cuda_device, dtype=torch.long),
                       torch.zeros(1, 1, 5, 64, device=cuda_device, dtype=torch.bfloat16),
                       torch.zeros(1, 1, 5, 64, device=cuda_device, dtype=torch.bfloat16))
+
+
+@pytest.mark.parametrize("b,t,h,k", [(1, 4, 20, 1280), (64, 4, 20, 1280), (33, 4, 4, 512)])
+def test_qkv_rope_projection_within_one_ulp_of_its_sum_bound(moss, cuda_device, b, t, h, k):
+    """The values (the projection's third part, stored unrotated) isolate
+    the GEMM: each is one FP32 sum of k products plus the bias, rounded once
+    to bf16 in both paths.  Two summation orders differ by at most
+    2 gamma_{k+1} (sum|x w| + |bias|) (gamma_n = n u / (1 - n u),
+    u = 2^-24), so the bf16 results differ by at most one bf16 ulp plus
+    that bound.  (The rotated q
+    and k can differ by 2 ulps: a one-ulp step in an input of the rotation
+    moves an output of smaller magnitude by more than one of its own ulps.)"""
+    case = _case(cuda_device, b, t, h, k, False, 11 * b + h)
+    got, want = _both(moss, cuda_device, case, h)
+    x, w, bias, offset, slots, total = case
+    gv, wv = got[2].float(), want[2].float()
+    # sum |x w| of every value feature, laid out like the value ring
+    mag = (x.float().abs() @ w[2 * h * 64:].float().abs().T
+           + bias[2 * h * 64:].float().abs()).view(b, t, h, 64)
+    sum_abs = torch.zeros_like(gv)
+    for bi in range(b):
+        sum_abs[bi, :, slots[bi]] = mag[bi].transpose(0, 1)
+    u = 2.0 ** -24
+    gamma = (k + 1) * u / (1 - (k + 1) * u)  # k products and the bias
+    top = torch.maximum(gv.abs(), wv.abs()).clamp_min(2.0 ** -126)
+    ulp = torch.exp2(torch.floor(torch.log2(top)) - 7)
+    assert torch.all((gv - wv).abs() <= ulp + 2 * gamma * sum_abs)
+    assert (gv == wv).float().mean() > 0.98

@@ -142,3 +142,25 @@ def test_optimized_falls_back_where_the_reference_does(moss, model, cuda_device)
         with moss.optimized(model) as rt:
             with moss.optimized(model):
                 pass
+
+
+def test_graph_captured_in_context_stops_replaying_after_it(moss, model, cuda_device):
+    """A graph captured inside optimized(model) holds the context's cached
+    resources; once the context closes the graph refuses to replay, while
+    a graph captured outside any context keeps working."""
+    q = torch.randn(2, 4, 16, 64, device=cuda_device).to(torch.bfloat16)
+    offset = torch.tensor([0, 3], device=cuda_device)
+
+    def rotary(x):
+        return model.rope(x, x, offset)
+
+    with moss.optimized(model, cache_linear=False) as rt:
+        inside = moss.GraphedCallable(rotary, q)
+        first = inside(q)
+        assert rt.rope_calls >= 1
+    with pytest.raises(RuntimeError, match="released or rebuilt"):
+        inside(q)
+    outside = moss.GraphedCallable(rotary, q)  # the upstream path, no context
+    again = outside(q)
+    assert torch.equal(again[0].view(torch.int16), first[0].view(torch.int16))
+    outside.release()
