@@ -470,6 +470,64 @@ def kernel_lines(torch, fm, dev, hbm_peak):
     return out
 
 
+def lfq_loop_line(torch, dev):
+    """The real codec's 32-stage LFQ quantizer over the full-codec batch (64
+    clips x 125 frames of 80 ms, hidden 1280, 1024-entry codebooks) as one
+    kernel (LFQResidualQuantizer, moss_lfq_rvq_encode), against the
+    reference's per-stage sequence on the same GPU: FP32 input projection
+    (cuBLAS, TF32 off), moss_lfq_prepare, the FP32 dot-product GEMM,
+    moss_lfq_select, the output projection and the residual update; all 32
+    stages in one CUDA graph."""
+    import torch.nn.functional as F
+    from fast_moss_b200.lfq_rvq import LFQResidualQuantizer
+    from fast_moss_b200.quantizer import select
+    from fast_moss_b200.quantizer_prepare import prepare
+
+    b, d, t, stages, k = 64, 1280, 125, 32, 1024
+    g = torch.Generator(device=dev).manual_seed(8)
+    w_in = torch.randn(stages, 8, d, device=dev, generator=g) / d ** 0.5
+    b_in = 0.1 * torch.randn(stages, 8, device=dev, generator=g)
+    books = torch.randn(stages, k, 8, device=dev, generator=g)
+    w_out = 0.1 * torch.randn(stages, d, 8, device=dev, generator=g)
+    b_out = 0.01 * torch.randn(stages, d, device=dev, generator=g)
+    q = LFQResidualQuantizer(w_in, b_in, books, w_out, b_out)
+    sets = [torch.randn(b, d, t, device=dev, generator=g) for _ in range(2)]
+    codes = torch.empty(stages, b, t, device=dev, dtype=torch.long)
+
+    def fused(x, _h):
+        q.encode(x, codes=codes)
+
+    book_t = [q.book_normed[s].T.contiguous() for s in range(stages)]
+    cnorm = [q.code_norm[s].view(1, k) for s in range(stages)]
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    seq_codes = torch.empty_like(codes)
+
+    def sequence(x, _h):
+        r = x.transpose(1, 2).reshape(b * t, d)
+        for s in range(stages):
+            z = F.linear(r, w_in[s], b_in[s]).view(b, t, 8).transpose(1, 2).contiguous()
+            _, row_norm, twice, _ = prepare(z)
+            values, idx = select(twice @ book_t[s], row_norm, cnorm[s], books[s], z)
+            seq_codes[s].copy_(idx)
+            r = r - F.linear(values.transpose(1, 2).reshape(b * t, 8), w_out[s], b_out[s])
+
+    try:
+        tf = time_launches(torch, fused, sets, launches=4, replays=3)
+        ts = time_launches(torch, sequence, sets, launches=2, replays=3)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    flop = 2 * b * t * stages * (8 * d + k * 8 + d * 8)
+    return {"shape": {"clips": b, "frames_per_clip": t, "hidden": d, "stages": stages,
+                      "codes": k},
+            "us_fused": tf * 1e6, "us_reference_sequence": ts * 1e6,
+            "speedup": ts / tf, "fused_tflops": flop / tf / 1e12,
+            "frames_per_sec": b * t / tf,
+            "sequence": "per stage: F.linear in (FP32, TF32 off), moss_lfq_prepare, FP32 GEMM, "
+                        "moss_lfq_select, F.linear out, r -= o (the reference's stage on "
+                        "this library's prepare/select), 32 stages in one CUDA graph"}
+
+
 def rvq_sequence_line(torch, x, books, codes_fused, fused_s):
     """The reference's per-stage RVQ algorithm on the same GPU: per stage 2r,
     the row norm, the FP32 dot-product GEMM with TF32 off (cuBLAS; the
@@ -599,6 +657,49 @@ def _qkv_kernel_line(torch, dev, cfg, weights):
     return res
 
 
+def _linear_kernel_line(torch, dev, cfg, weights):
+    """The stack's four Linears per layer at 1 and 64 streams (4 and 256
+    token rows): moss_linear (tcgen05, K split over a cluster; the first
+    feed-forward Linear with its bias + GELU in the epilogue) against
+    F.linear (cuBLAS; + moss_gated_act for the feed-forward), over the 24
+    layers' weights in turn (more than L2), graph-timed.  `gbs` counts the
+    weight bytes of one launch."""
+    import torch.nn.functional as F
+    from fast_moss_b200.linear import linear
+    from fast_moss_b200.v2_pointwise import gated_activation
+
+    layers = [{k: w[k].to(dev, torch.bfloat16) for k in ("qkv_w", "qkv_b", "out_w", "out_b",
+                                                         "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b")}
+              for w in weights]
+    shapes = (("qkv", "qkv_w", "qkv_b", cfg.dim, None), ("out", "out_w", "out_b", cfg.dim, None),
+              ("ffn1_act", "ffn1_w", "ffn1_b", cfg.dim, cfg.activation),
+              ("ffn2", "ffn2_w", "ffn2_b", cfg.ffn, None))
+    res = {}
+    for streams in (1, 64):
+        rows = streams * cfg.chunk_tokens
+        g = torch.Generator(device=dev).manual_seed(7)
+        line = {}
+        for name, wk, bk, k, act in shapes:
+            x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+
+            def owned(layer, _h):
+                linear(x, layer[wk], layer[bk], activation=act)
+
+            def library(layer, _h):
+                if act is None:
+                    F.linear(x, layer[wk], layer[bk])
+                else:
+                    gated_activation(F.linear(x, layer[wk]), layer[bk], act, False)
+
+            to = time_launches(torch, owned, layers, launches=48, replays=5)
+            tl = time_launches(torch, library, layers, launches=48, replays=5)
+            wbytes = layers[0][wk].numel() * 2
+            line[name] = {"us_owned": to * 1e6, "us_cublas": tl * 1e6,
+                          "owned_weight_gbs": wbytes / to / 1e9, "weight_bytes": wbytes}
+        res[f"streams_{streams}"] = line
+    return res
+
+
 def _attention_kernel_line(torch, dev, cfg):
     """The stack's attention over its history ring, per layer: the owned
     kernel (moss_history_attention) against the SDPA call it replaces
@@ -674,6 +775,7 @@ def stack_variants(torch, dev):
             dst[f"streams_{streams}"] = _stack_rate(torch, dev, cfg, stack, streams, CHUNKS)
         del stack
     out["qkv_kernel"] = _qkv_kernel_line(torch, dev, cfg, weights)
+    out["linear_kernel"] = _linear_kernel_line(torch, dev, cfg, weights)
     out["attention_kernel"] = _attention_kernel_line(torch, dev, cfg)
     torch.cuda.synchronize()
     return out
@@ -929,7 +1031,8 @@ def run_b200(args):
                                                   args.warmup, cpu=not args.no_cpu)
         if world == 1 and not args.no_kernels:
             extras["kernels"] = {"peak_hbm_gbs": peaks["hbm_gbs"], "peak_source": peak_src,
-                                 **kernel_lines(torch, None, dev, peaks["hbm_gbs"])}
+                                 **kernel_lines(torch, None, dev, peaks["hbm_gbs"]),
+                                 "lfq_loop": lfq_loop_line(torch, dev)}
         if world == 1 and not args.no_stack:
             extras["stack"] = stack_variants(torch, dev)
     if world > 1:

@@ -26,6 +26,9 @@ ACT_SILU = 0
 ACT_GELU_ERF = 1
 ACT_GELU_TANH = 2
 
+LINEAR_BIAS = 0
+LINEAR_BIAS_ACT = 1
+
 
 class UnsupportedError(ValueError):
     """Valid input that the B200 kernels do not cover (caller may fall back to
@@ -60,10 +63,14 @@ _SIGNATURES = {
     "moss_history_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _f, _vp, _vp]),
     "moss_gated_act": (_i, [_vp, _vp, _vp, _i, _i64, _i64, _i, _i, _vp]),
+    "moss_linear": (_i, [_vp, _i64, _i64, _vp, _i64, _vp, _i, _i, _vp, _vp]),
+    "moss_linear_cluster": (_i, [_i64, _i64, _i64]),
     "moss_lfq_prepare": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),
     "moss_lfq_select": (_i, [_vp, _vp, _vp, _vp, _vp, _pi64, _i64, _i64, _i64, _i64, _i, _vp, _vp,
                              _vp]),
     "moss_lfq_decode": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "moss_lfq_rvq_encode": (_i, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _vp, _vp, _vp, _vp]),
     "moss_rvq_packed_floats": (_i64, [_i64, _i64, _i64]),
     "moss_rvq_prepare_codebooks": (_i, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_rvq_encode": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),

@@ -19,6 +19,12 @@ native kernels of libfast_moss_b200:
   residual + layer scale 2 + next LN 1       moss_residual_layer_norm_out
                                              (moss_scale_add after the last layer)
 
+With `owned_linear=True` the four Linears of a layer run as moss_linear
+(tcgen05 bf16 GEMM with TMA-fed operands, K split across a thread-block
+cluster and reduced in a fixed order) and the feed-forward's bias +
+activation move into the first feed-forward Linear's epilogue; the sums run
+in that kernel's order, not cuBLAS's.
+
 With `fused_qkv=True` the qkv Linear, the rotary embedding and the history
 writes are one tcgen05 kernel (moss_qkv_rope: bf16 tensor-core GEMM whose
 epilogue rounds, rotates and stores into the ring; its dot products are
@@ -47,6 +53,7 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .graphs import CapturedStep
+from .linear import linear as owned_linear
 from .v2_pointwise import (
     gated_activation,
     history_attention,
@@ -58,6 +65,8 @@ from .v2_pointwise import (
     scale_add,
 )
 
+
+_LINEAR_ACTS = ("silu", "gelu", "gelu_tanh")
 
 # Token rows (streams x chunk tokens) up to which the fused qkv projection
 # runs: one 32-row tile of moss_qkv_rope.  Measured per layer on B200 at
@@ -207,7 +216,8 @@ class StreamingTransformer:
     """The stack: FP32 parameters on one CUDA device, bf16 GEMM weights cached
     once (the reference's cached Linear, fast_moss/v2_runtime.py:77-106)."""
 
-    def __init__(self, cfg, weights, device, *, fused_qkv=False, history_attention=False):
+    def __init__(self, cfg, weights, device, *, fused_qkv=False, history_attention=False,
+                 owned_linear=False):
         device = torch.device(device)
         if device.type != "cuda":
             raise ValueError("StreamingTransformer runs on a CUDA device")
@@ -226,6 +236,14 @@ class StreamingTransformer:
         self.fused_qkv = bool(fused_qkv)
         if self.fused_qkv and cfg.head_dim != 64:
             raise ValueError("the fused qkv projection needs heads of 64")
+        # the four Linears as moss_linear (tcgen05, K split over a cluster)
+        # with the feed-forward's bias + activation in the first one's
+        # epilogue, instead of cuBLAS + moss_gated_act
+        self.owned_linear = bool(owned_linear)
+        if self.owned_linear and (cfg.gated or cfg.dim % 128 or cfg.ffn % 128
+                                  or cfg.activation not in _LINEAR_ACTS):
+            raise ValueError("the owned Linear needs widths that are multiples of 128 and an "
+                             "ungated silu / gelu / gelu_tanh feed-forward")
         # the attention as moss_history_attention (FP32 softmax and P.V over
         # the ring, mask from the slot positions) instead of SDPA
         self.history_attention = bool(history_attention)
@@ -237,6 +255,9 @@ class StreamingTransformer:
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
 
+    def _linear(self, x, w, b):
+        return owned_linear(x, w, b) if self.owned_linear else F.linear(x, w, b)
+
     def native_launches(self, streams):
         """Kernels of libfast_moss_b200 that one chunk step launches: the
         first LayerNorm, then per layer the rotary (moss_rope_kv or
@@ -244,6 +265,8 @@ class StreamingTransformer:
         residual + LayerNorm passes (the last layer's second is
         moss_scale_add) and the feed-forward activation."""
         per_layer = 4 + (1 if self.history_attention else 0)
+        if self.owned_linear:
+            per_layer += 3  # four Linears, the activation in the first feed-forward one
         return 1 + self.cfg.layers * per_layer
 
     @torch.inference_mode()
@@ -265,11 +288,11 @@ class StreamingTransformer:
         # LayerNorm outputs go straight to the next GEMM as its bf16 input
         normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps, out_dtype=bf16)
         for i, p in enumerate(self.layers):
-            if self.fused_qkv and s * t <= FUSED_QKV_MAX_ROWS:
+            if self.fused_qkv and s * t <= FUSED_QKV_MAX_ROWS and not self.owned_linear:
                 q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
                              slots, hist.keys[i], hist.values[i])
             else:
-                qkv = F.linear(normed, p["qkv_w16"], p["qkv_b16"])
+                qkv = self._linear(normed, p["qkv_w16"], p["qkv_b16"])
                 qkv = qkv.view(s, t, 3, h, dh)
                 q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
                             qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
@@ -282,12 +305,15 @@ class StreamingTransformer:
                     a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
                                                        attn_mask=mask)
                 a = a.transpose(1, 2).reshape(s, t, d)
-            u = F.linear(a, p["out_w16"], p["out_b16"])
+            u = self._linear(a, p["out_w16"], p["out_b16"])
             x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps,
                                             out_dtype=bf16)
-            f = F.linear(normed, p["ffn1_w16"])
-            f = gated_activation(f, p["ffn1_b16"], cfg.activation, cfg.gated)
-            u = F.linear(f, p["ffn2_w16"], p["ffn2_b16"])
+            if self.owned_linear:
+                f = owned_linear(normed, p["ffn1_w16"], p["ffn1_b16"], activation=cfg.activation)
+            else:
+                f = F.linear(normed, p["ffn1_w16"])
+                f = gated_activation(f, p["ffn1_b16"], cfg.activation, cfg.gated)
+            u = self._linear(f, p["ffn2_w16"], p["ffn2_b16"])
             if i + 1 < len(self.layers):
                 nxt = self.layers[i + 1]
                 x, normed = residual_layer_norm(x, u, p["ls2"], nxt["norm1_w"], nxt["norm1_b"],

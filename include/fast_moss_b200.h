@@ -55,6 +55,9 @@ extern "C" {
 #define MOSS_ACT_GELU_ERF 1
 #define MOSS_ACT_GELU_TANH 2
 
+#define MOSS_LINEAR_BIAS 0      /* y = x w^T + bias                       */
+#define MOSS_LINEAR_BIAS_ACT 1  /* y = act(bf16(x w^T) + bias), ungated   */
+
 /* Library ABI version (major*100 + minor). */
 MOSS_API int moss_version(void);
 
@@ -230,6 +233,27 @@ MOSS_API int moss_history_attention(const void* q, const void* k_cache, const vo
               void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Linear layer on cached bf16 weights, tcgen05 tensor cores, bias or bias +
+ * activation in the epilogue.
+ * Replaces the cached bf16 Linear of the patched model
+ * (fast_moss/v2_runtime.py:77-106, F.linear at :104) and, with
+ * MOSS_LINEAR_BIAS_ACT, the Linear followed by the feed-forward's
+ * bias + activation (moss_gated_act, ungated):
+ *   MOSS_LINEAR_BIAS      y = bf16(x w^T + bias)          (bias may be NULL)
+ *   MOSS_LINEAR_BIAS_ACT  y = bf16(act(bf16(bf16(x w^T) + bias)))
+ * x [m, k], w [n, k], bias [n], y [m, n]: bf16, row-major, 16-byte aligned;
+ * k a multiple of 64, n a multiple of 128 (MOSS_ERR_UNSUPPORTED otherwise).
+ * FP32 accumulation; K is split across the CTAs of a thread-block cluster
+ * (moss_linear_cluster(m, n, k) CTAs) whose partial sums are added in a
+ * fixed order, so results are deterministic but summed in another order
+ * than cuBLAS's: an output can differ from F.linear's by the rounding of a
+ * different FP32 sum.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_linear(const void* x, int64_t m, int64_t k, const void* w, int64_t n,
+                const void* bias, int epilogue, int act, void* y, void* stream);
+MOSS_API int moss_linear_cluster(int64_t m, int64_t n, int64_t k);
+
+/* ---------------------------------------------------------------------------
  * Bias + gated activation, bf16 or float32 in and out.
  * No kernel in the reference (its FFN activation is upstream model code);
  * this is the eager-PyTorch chain it replaces, one rounding per torch op:
@@ -285,6 +309,35 @@ MOSS_API int moss_lfq_decode(const float* x, const float* book_normed,
                     const float* code_norm, const float* weight, int64_t b,
                     int64_t t, int64_t k, float* out, int64_t* indices,
                     void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Multi-stage LFQ quantizer of the real codec, every stage in one kernel.
+ * Replaces, per stage, the upstream quantizer's input projection, the
+ * patched LFQ decode (fast_moss/v2_runtime.py:143-181: prepare,
+ * fast_moss/quantizer_prepare.py:111-157; the FP32 dot-product GEMM; select,
+ * fast_moss/quantizer.py:52-108), the output projection and the residual
+ * update -- the stage loop the reference leaves to the upstream quantizer
+ * (fast_moss/v2_codec.py:45).  Per frame (b, t), r = x[b, :, t], and for
+ * every stage s:
+ *   z_j = dot(w_in[s, j, :], r) + b_in[s, j]  (32 lane partial sums over
+ *         d = l, l + 32, ..., sequential FMA from +0, then added pairwise
+ *         across lanes 16, 8, 4, 2, 1 apart)
+ *   index = the LFQ decode of z viewed as a [b, 8, t] latent (the
+ *         reference's prepare orders, transposed when b == 1 and t > 1;
+ *         dots = product + 7 FMAs; first NaN, else first minimum)
+ *   o_d = (FMA chain over j of w_out[s, d, j] * weight[s, index, j] from
+ *         +0) + b_out[s, d] ;  r_d -= o_d ;  codes[s, b * t + t_i] = index
+ * x, residual_out [b, d, t] FP32 (residual_out may be NULL); w_in [s, 8, d],
+ * b_in [s, 8], book_normed [s, k, 8] (F.normalize of the codebook weight),
+ * code_norm [s, k] (sum of squares of book_normed rows), weight [s, k, 8]
+ * (raw codebooks), w_out [s, d, 8], b_out [s, d]; book_normed and w_out
+ * 16-byte aligned; codes int64 [s, b * t].  d <= 2048, k <= 65536.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_lfq_rvq_encode(const float* x, int64_t b, int64_t d, int64_t t, int64_t stages,
+                        int64_t k, const float* w_in, const float* b_in,
+                        const float* book_normed, const float* code_norm,
+                        const float* weight, const float* w_out, const float* b_out,
+                        int64_t* codes, float* residual_out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Codebook preparation for the multi-stage residual vector quantizer,

@@ -277,15 +277,12 @@ static float sum8(const float* v, int transposed) {
   return l + r;
 }
 
-static void prepare_one(const float* x, int64_t row, int64_t b, int64_t t, float* e, float* tw,
-                        float* norm, float* denom) {
-  int transposed = (b == 1 && t > 1);
-  int64_t bi = row / t, ti = row % t;
-  float v[8], sq[8], es[8];
-  for (int d = 0; d < 8; ++d) {
-    v[d] = x[bi * 8 * t + d * t + ti];
-    sq[d] = v[d] * v[d];
-  }
+/* The preparation of one 8-value latent v; `transposed` selects the order
+ * the reference uses for a [1, 8, t > 1] batch. */
+static void prepare_values(const float* v, int transposed, float* e, float* tw, float* norm,
+                           float* denom) {
+  float sq[8], es[8];
+  for (int d = 0; d < 8; ++d) sq[d] = v[d] * v[d];
   float total;
   if (transposed) {
     float a = fmaf(v[4], v[4], sq[0]), bb = fmaf(v[5], v[5], sq[1]);
@@ -305,6 +302,14 @@ static void prepare_one(const float* x, int64_t row, int64_t b, int64_t t, float
   }
   *norm = sum8(es, transposed);
   *denom = den;
+}
+
+static void prepare_one(const float* x, int64_t row, int64_t b, int64_t t, float* e, float* tw,
+                        float* norm, float* denom) {
+  int64_t bi = row / t, ti = row % t;
+  float v[8];
+  for (int d = 0; d < 8; ++d) v[d] = x[bi * 8 * t + d * t + ti];
+  prepare_values(v, b == 1 && t > 1, e, tw, norm, denom);
 }
 
 EXPORT void oracle_lfq_prepare(const float* x, int64_t b, int64_t t, float* e, float* norm,
@@ -389,6 +394,77 @@ EXPORT void oracle_lfq_decode(const float* x, const float* book_normed, const fl
     for (int q = 0; q < 8; ++q) out[row * 8 + q] = weight[idx * 8 + q];
   }
   free(dist);
+}
+
+/* ------------------------------------------------ multi-stage LFQ quantizer
+ * The stage loop of the real codec's quantizer (the upstream module called at
+ * fast_moss/v2_codec.py:45), every stage: the 8-wide input projection, the
+ * LFQ decode above (prepare with the reference's orders, dots, select:
+ * fast_moss/v2_runtime.py:143-181), the output projection and r -= o.  The
+ * projections' summation order is defined here (the upstream module that
+ * fixes it is not available):
+ *   z_j = dot_lanes(w_in[s, j], r) + b_in[s, j]; dot_lanes = 32 partial
+ *         sums p_l (sequential FMA from +0 over d = l, l + 32, ...) added as
+ *         p_l = p_l + p_(l ^ off) for off = 16, 8, 4, 2, 1, result p_0;
+ *   o_d = fma chain over j of w_out[s, d, j] c_j from +0, plus b_out[s, d]. */
+static float dot_lanes(const float* w, const float* r, int64_t d) {
+  float p[32];
+  for (int l = 0; l < 32; ++l) {
+    float acc = 0.0f;
+    for (int64_t i = l; i < d; i += 32) acc = fmaf(w[i], r[i], acc);
+    p[l] = acc;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    float q[32];
+    for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+    for (int l = 0; l < 32; ++l) p[l] = q[l];
+  }
+  return p[0];
+}
+
+EXPORT void oracle_lfq_rvq_encode(const float* x, int64_t b, int64_t d, int64_t t,
+                                  int64_t stages, int64_t k, const float* w_in, const float* b_in,
+                                  const float* book_normed, const float* cnorm,
+                                  const float* weight, const float* w_out, const float* b_out,
+                                  int64_t* codes, float* residual) {
+  const int64_t rows = b * t;
+  const int transposed_b = (b == 1 && t > 1) ? 1 : 0;
+  float* r = (float*)malloc(sizeof(float) * (size_t)d);
+  float* dist = (float*)malloc(sizeof(float) * (size_t)k);
+  for (int64_t row = 0; row < rows; ++row) {
+    const int64_t bi = row / t, ti = row % t;
+    for (int64_t c = 0; c < d; ++c) r[c] = x[(bi * d + c) * t + ti];
+    for (int64_t s = 0; s < stages; ++s) {
+      float z[8], e[8], tw[8], norm, den;
+      for (int j = 0; j < 8; ++j)
+        z[j] = dot_lanes(w_in + (s * 8 + j) * d, r, d) + b_in[s * 8 + j];
+      /* z is one latent of the stage's [b, 8, t] tensor */
+      prepare_values(z, transposed_b, e, tw, &norm, &den);
+      const float* bn = book_normed + s * k * 8;
+      const float* cn = cnorm + s * k;
+      for (int64_t j = 0; j < k; ++j) {
+        const float* c = bn + j * 8;
+        float dot = tw[0] * c[0];
+        for (int q = 1; q < 8; ++q) dot = fmaf(tw[q], c[q], dot);
+        float diff = norm - dot;
+        dist[j] = diff + cn[j];
+      }
+      const int64_t idx = select_first(dist, k);
+      codes[s * rows + row] = idx;
+      const float* cw = weight + (s * k + idx) * 8;
+      for (int64_t c = 0; c < d; ++c) {
+        const float* wo = w_out + (s * d + c) * 8;
+        float o = 0.0f;
+        for (int j = 0; j < 8; ++j) o = fmaf(wo[j], cw[j], o);
+        o = o + b_out[s * d + c];
+        r[c] = r[c] - o;
+      }
+    }
+    if (residual)
+      for (int64_t c = 0; c < d; ++c) residual[(bi * d + c) * t + ti] = r[c];
+  }
+  free(dist);
+  free(r);
 }
 
 /* ------------------------------------------------------ residual VQ

@@ -196,6 +196,24 @@ def lfq_decode(x, book_normed, code_norm, weight):
     return out, idx
 
 
+def lfq_rvq_encode(x, w_in, b_in, book_normed, code_norm, weight, w_out, b_out):
+    """The multi-stage LFQ quantizer of the real codec in the loop order
+    moss_oracle.c defines (projections) around the reference's LFQ decode of
+    every stage; x [b, d, t].  Returns (codes int64 [stages, b*t], final
+    residual [b, d, t])."""
+    x = _f32(x)
+    w_in, b_in, bn, cn = _f32(w_in), _f32(b_in), _f32(book_normed), _f32(code_norm)
+    weight, w_out, b_out = _f32(weight), _f32(w_out), _f32(b_out)
+    b, d, t = x.shape
+    stages, k, _ = bn.shape
+    codes = np.empty((stages, b * t), np.int64)
+    res = np.empty_like(x)
+    lib().oracle_lfq_rvq_encode(_p(x), _i64(b), _i64(d), _i64(t), _i64(stages), _i64(k),
+                                _p(w_in), _p(b_in), _p(bn), _p(cn), _p(weight), _p(w_out),
+                                _p(b_out), _p(codes), _p(res))
+    return codes, res
+
+
 def rvq_code_norms(books):
     """sum_d c^2 per code, sequential FMA (books [stages, k, d])."""
     books = _f32(books)

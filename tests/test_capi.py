@@ -78,6 +78,13 @@ def test_bad_arguments_map_to_value_errors(lib):
     assert lib.moss_rvq_packed_floats(32, 1000, 64) == 32 * 1024 * 64 + 32 * 4 * 256 * 72
     assert lib.moss_rvq_encode_ffma(None, 8, 32, None, None, None, None, 1, 4, None, None, None,
                                     None) == _lib.ERR_UNSUPPORTED
+    # the Linear covers k % 64 == 0 and n % 128 == 0; the K split of the
+    # stack's shapes (148 SMs): 8 CTAs per 1280-wide output, 4 for qkv
+    assert lib.moss_linear(None, 4, 96, None, 128, None, 0, 0, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.moss_linear(None, 4, 128, None, 100, None, 0, 0, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.moss_linear(None, 4, 128, None, 128, None, 5, 0, None, None) == _lib.ERR_VALUE
+    assert lib.moss_linear(None, 0, 128, None, 128, None, 0, 0, None, None) == _lib.OK
+    assert lib.moss_linear(None, 4, 128, None, 128, None, 0, 0, None, None) == _lib.ERR_VALUE
     # the bounded-wait self-test takes limits of 1 us to 100 ms only
     assert lib.moss_test_bounded_wait(10, 0, None) == _lib.ERR_VALUE
     assert lib.moss_test_bounded_wait(10**9, 0, None) == _lib.ERR_VALUE

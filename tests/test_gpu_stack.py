@@ -128,3 +128,31 @@ def test_fused_qkv_stack(moss, cuda_device):
     assert rel < 2e-2, rel
     sp.release()
     sf.release()
+
+
+def test_owned_linear_stack(moss, cuda_device):
+    """The stack on the tcgen05 Linear (all four projections; the first
+    feed-forward one with bias + GELU in its epilogue), with and without the
+    history attention: graph replays equal the stack's own eager steps bit
+    for bit, and it tracks the cuBLAS stack to bf16 noise (the projections'
+    sums are ordered differently)."""
+    from fast_moss_b200.transformer import (BatchedStreams, StackConfig, StreamingTransformer,
+                                            init_weights)
+
+    cfg = StackConfig()
+    weights = init_weights(cfg, seed=2)
+    plain = StreamingTransformer(cfg, weights, cuda_device)
+    feats = _features(3, 4 * 6, cfg.dim, 5).to(cuda_device)
+    sp = BatchedStreams(plain, streams=3)
+    a = sp(feats)
+    sp.release()
+    for opts in ({"owned_linear": True}, {"owned_linear": True, "history_attention": True}):
+        owned = StreamingTransformer(cfg, weights, cuda_device, **opts)
+        so = BatchedStreams(owned, streams=3)
+        b = so(feats)
+        hist = owned.history(3)
+        eager = torch.cat([owned.step(feats[:, c * 4:(c + 1) * 4], hist) for c in range(6)], 1)
+        assert torch.equal(b, eager), opts
+        rel = float((a - b).norm() / a.norm())
+        assert rel < 2e-2, (opts, rel)
+        so.release()
