@@ -665,12 +665,15 @@ def _linear_kernel_line(torch, dev, cfg, weights):
     layers' weights in turn (more than L2), graph-timed.  `gbs` counts the
     weight bytes of one launch."""
     import torch.nn.functional as F
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
     from fast_moss_b200.v2_pointwise import gated_activation
 
     layers = [{k: w[k].to(dev, torch.bfloat16) for k in ("qkv_w", "qkv_b", "out_w", "out_b",
                                                          "ffn1_w", "ffn1_b", "ffn2_w", "ffn2_b")}
               for w in weights]
+    for layer in layers:
+        for k in ("qkv_w", "out_w", "ffn1_w", "ffn2_w"):
+            layer[k + "_packed"] = pack_weight(layer[k])
     shapes = (("qkv", "qkv_w", "qkv_b", cfg.dim, None), ("out", "out_w", "out_b", cfg.dim, None),
               ("ffn1_act", "ffn1_w", "ffn1_b", cfg.dim, cfg.activation),
               ("ffn2", "ffn2_w", "ffn2_b", cfg.ffn, None))
@@ -683,7 +686,7 @@ def _linear_kernel_line(torch, dev, cfg, weights):
             x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
 
             def owned(layer, _h):
-                linear(x, layer[wk], layer[bk], activation=act)
+                linear(x, layer[wk + "_packed"], layer[bk], activation=act)
 
             def library(layer, _h):
                 if act is None:

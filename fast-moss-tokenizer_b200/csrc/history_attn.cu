@@ -23,9 +23,11 @@
 // The weights and the partial sums reuse K's shared memory once the scores
 // are formed, so that three CTAs fit on an SM (registers capped to match):
 // one CTA's loads then overlap the others' arithmetic.
+#include <cuda.h>
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "pipeline.cuh"
 
 namespace moss {
 namespace hattn {
@@ -230,6 +232,287 @@ __global__ void __launch_bounds__(kThreads, 3) history_attn_kernel(const Args a)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Persistent variant for many (stream, head) items: a CTA loops over items
+// blockIdx.x, blockIdx.x + gridDim.x, ... (two CTAs per SM).  The arithmetic
+// is that of history_attn_kernel, value for value; what changes is how the
+// bytes arrive.  One thread loads an item's K block with one TMA 2-D load
+// (the ring viewed as [S * H * N, 64] bf16 rows; the 128-byte swizzle
+// puts 16-byte chunk c of row j at chunk c ^ (j % 8), the layout the
+// per-key dot products read without bank conflicts) and its V block with
+// one bulk copy, each completing on its own mbarrier; the next item's K is
+// requested as soon as the current scores are formed and its V as soon as
+// the current P.V is done, so HBM streams the next item while this one
+// computes.  The next item's queries, slot positions and position are
+// loaded into registers while the current one computes.  n <= 256 (one
+// TMA box).  Every wait is bounded (~2 s, MOSS_ERR_TIMEOUT).
+constexpr int kStreamMaxKeys = 256;
+
+struct StreamArgs {
+  CUtensorMap k_map;  // k_cache as [S * H * N, 64] bf16, box {64, n}, 128-byte swizzle
+  Args a;
+  int64_t items;
+};
+
+__host__ __device__ constexpr size_t stream_smem(int t, int n) {
+  // K (whole 1024-byte swizzle atoms) | V | weights [t][np] | partial sums
+  // [warps][t][64] | q [t][64] | reduction slots | 2 mbarriers
+  return static_cast<size_t>((n + 7) / 8) * 1024 + static_cast<size_t>(n) * kDim * 2 +
+         static_cast<size_t>(t) * padded_keys(n) * 4 + static_cast<size_t>(kWarps) * t * kDim * 4 +
+         static_cast<size_t>(t) * kDim * 4 + static_cast<size_t>(kWarps) * kMaxQueries * 4 + 16 +
+         1024;
+}
+
+__device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* map, int row,
+                                              unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(row), "r"(pipe::smem_u32(bar))
+      : "memory");
+}
+
+template <int T>
+__global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
+    const __grid_constant__ StreamArgs sa) {
+  extern __shared__ unsigned char smem_raw[];
+  const Args& a = sa.a;
+  const int n = a.n;
+  const int np = padded_keys(n);
+  unsigned char* ks = smem_raw + ((1024u - (static_cast<uint32_t>(
+                                                 __cvta_generic_to_shared(smem_raw)) & 1023u)) &
+                                  1023u);
+  unsigned char* vs = ks + static_cast<size_t>((n + 7) / 8) * 1024;
+  float* ps = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [T][np]
+  float* part = ps + T * np;                                                     // [warps][T][64]
+  float* qs = part + kWarps * T * kDim;                                          // [T][64]
+  float* red = qs + T * kDim;                                                    // [warps][8]
+  unsigned long long* kfull = reinterpret_cast<unsigned long long*>(red + kWarps * kMaxQueries);
+  unsigned long long* vfull = kfull + 1;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t bytes = static_cast<uint32_t>(n) * kDim * 2;
+
+  if (tid == 0) {
+    pipe::mbar_init(kfull, 1);
+    pipe::mbar_init(vfull, 1);
+    pipe::fence_mbar_init();
+  }
+  __syncthreads();
+  int64_t item = blockIdx.x;
+  if (item >= sa.items) return;  // uniform over the CTA
+  auto issue_k = [&](int64_t it) {
+    pipe::mbar_arrive_expect_tx(kfull, bytes);
+    tma_load_rows(pipe::smem_u32(ks), &sa.k_map, static_cast<int>(it * n), kfull);
+  };
+  auto issue_v = [&](int64_t it) {
+    pipe::mbar_arrive_expect_tx(vfull, bytes);
+    pipe::bulk_g2s(vs, a.v + it * n * kDim, bytes, vfull);
+  };
+  if (tid == 0) {
+    issue_k(item);
+    issue_v(item);
+  }
+  // this item's queries, slot positions and position, in registers
+  auto load_meta = [&](int64_t it, float (&qv)[(T * kDim + kThreads - 1) / kThreads],
+                       int64_t (&held)[kKeysPerThread], int64_t& p0) {
+    const int64_t s = it / a.h;
+    const uint16_t* qg = a.q + it * T * kDim;
+#pragma unroll
+    for (int c = 0; c < (T * kDim + kThreads - 1) / kThreads; ++c) {
+      const int i = tid + c * kThreads;
+      qv[c] = i < T * kDim ? bf16_bits_to_f32(qg[i]) : 0.0f;
+    }
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) {
+      const int j = tid + m * kThreads;
+      held[m] = j < n ? a.slot_pos[s * n + j] : -1;
+    }
+    p0 = a.pos[s];
+  };
+  constexpr int QC = (T * kDim + kThreads - 1) / kThreads;
+  float qv[QC];
+  int64_t held[kKeysPerThread];
+  int64_t p0;
+  load_meta(item, qv, held, p0);
+  int issued_k = 1, issued_v = 1, done_k = 0, done_v = 0;
+  for (int i = 0;; ++i) {
+    const int64_t s = item / a.h;
+    const int hh = static_cast<int>(item - s * a.h);
+    const int64_t next = item + gridDim.x;
+    const bool more = next < sa.items;
+#pragma unroll
+    for (int c = 0; c < QC; ++c) {
+      const int q = tid + c * kThreads;
+      if (q < T * kDim) qs[q] = qv[c];
+    }
+    const int kok = pipe::mbar_wait(kfull, i & 1) ? 1 : 0;
+    done_k = i + kok;  // loads this thread saw land
+    if (__syncthreads_or(!kok)) break;  // K and the queries are visible to all
+    // ---- scores: thread tid takes keys tid and tid + 256
+    float sc[kKeysPerThread][T];
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) {
+      const int j = tid + m * kThreads;
+#pragma unroll
+      for (int t = 0; t < T; ++t) sc[m][t] = -CUDART_INF_F;
+      if (j < n) {
+        float acc[T];
+#pragma unroll
+        for (int t = 0; t < T; ++t) acc[t] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(ks + j * 128 + ((c ^ (j & 7)) << 4));
+          float kv[8];
+          unpack_bf16x8(raw, kv);
+#pragma unroll
+          for (int t = 0; t < T; ++t) {
+            const float4 qa = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8);
+            const float4 qb = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8 + 4);
+            acc[t] = __fmaf_rn(qa.x, kv[0], acc[t]);
+            acc[t] = __fmaf_rn(qa.y, kv[1], acc[t]);
+            acc[t] = __fmaf_rn(qa.z, kv[2], acc[t]);
+            acc[t] = __fmaf_rn(qa.w, kv[3], acc[t]);
+            acc[t] = __fmaf_rn(qb.x, kv[4], acc[t]);
+            acc[t] = __fmaf_rn(qb.y, kv[5], acc[t]);
+            acc[t] = __fmaf_rn(qb.z, kv[6], acc[t]);
+            acc[t] = __fmaf_rn(qb.w, kv[7], acc[t]);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+          const int64_t qp = p0 + t;
+          const bool on = held[m] >= 0 && held[m] <= qp && held[m] > qp - a.context;
+          sc[m][t] = on ? __fmul_rn(acc[t], a.scale) : -CUDART_INF_F;
+        }
+      }
+    }
+    float mx[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float v = sc[0][t];
+#pragma unroll
+      for (int m = 1; m < kKeysPerThread; ++m) v = fmaxf(v, sc[m][t]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) red[warp * kMaxQueries + t] = v;
+    }
+    __syncthreads();  // every read of K is done: the next item's K may come in
+    if (tid == 0 && more) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue_k(next);
+      ++issued_k;
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float v = red[t];
+      for (int w = 1; w < kWarps; ++w) v = fmaxf(v, red[w * kMaxQueries + t]);
+      mx[t] = v;
+    }
+    __syncthreads();  // the maxima are read before `red` takes the sums
+    float l[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int m = 0; m < kKeysPerThread; ++m) {
+        const int j = tid + m * kThreads;
+        const float e = (j < n && mx[t] != -CUDART_INF_F) ? expf(__fsub_rn(sc[m][t], mx[t])) : 0.0f;
+        if (j < n) ps[t * np + j] = e;
+        sum = __fadd_rn(sum, e);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+      if (lane == 0) red[warp * kMaxQueries + t] = sum;
+    }
+    // the next item's metadata while V lands
+    float qn[QC];
+    int64_t heldn[kKeysPerThread];
+    int64_t p0n = 0;
+    if (more) load_meta(next, qn, heldn, p0n);
+    const int vok = pipe::mbar_wait(vfull, i & 1) ? 1 : 0;
+    done_v = i + vok;
+    if (__syncthreads_or(!vok)) break;  // V, the weights and the sums are visible
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+      float v = red[t];
+      for (int w = 1; w < kWarps; ++w) v = __fadd_rn(v, red[w * kMaxQueries + t]);
+      l[t] = v;
+    }
+    // ---- P.V: warp w takes keys w, w + 8, ...; lane l dims 2l, 2l + 1
+    float o0[T], o1[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) o0[t] = o1[t] = 0.0f;
+    for (int j = warp; j < n; j += kWarps) {
+      const uint32_t raw = *reinterpret_cast<const uint32_t*>(vs + j * 128 + lane * 4);
+      const float v0 = __uint_as_float(raw << 16), v1 = __uint_as_float(raw & 0xffff0000u);
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const float p = ps[t * np + j];
+        o0[t] = __fmaf_rn(p, v0, o0[t]);
+        o1[t] = __fmaf_rn(p, v1, o1[t]);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < T; ++t)
+      *reinterpret_cast<float2*>(part + (warp * T + t) * kDim + 2 * lane) = make_float2(o0[t], o1[t]);
+    __syncthreads();  // every read of V is done: the next item's V may come in
+    if (tid == 0 && more) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue_v(next);
+      ++issued_v;
+    }
+    for (int e = tid; e < T * kDim; e += kThreads) {
+      const int t = e / kDim, d = e - t * kDim;
+      float acc = part[t * kDim + d];
+      for (int w = 1; w < kWarps; ++w) acc = __fadd_rn(acc, part[(w * T + t) * kDim + d]);
+      float lt = l[0];
+#pragma unroll
+      for (int u = 1; u < T; ++u) lt = t == u ? l[u] : lt;
+      a.out[((s * T + t) * a.h + hh) * kDim + d] = f32_to_bf16_bits(__fdiv_rn(acc, lt));
+    }
+    if (!more) break;
+    item = next;
+#pragma unroll
+    for (int c = 0; c < QC; ++c) qv[c] = qn[c];
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) held[m] = heldn[m];
+    p0 = p0n;
+    __syncthreads();  // `part`, `ps` and `qs` are read before they are rewritten
+  }
+  // after a timeout: the copies still in flight land before the CTA retires
+  if (tid == 0) {
+    for (int i = done_k; i < issued_k; ++i) pipe::mbar_wait(kfull, i & 1);
+    for (int i = done_v; i < issued_v; ++i) pipe::mbar_wait(vfull, i & 1);
+  }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                 const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                 const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                 CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// The key ring as [rows, 64] bf16 with a box of n rows and the 128-byte swizzle.
+bool encode_ring(CUtensorMap* map, const void* base, int64_t rows, int n) {
+  static EncodeTiled fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiled>(f);
+  }();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kDim) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kDim), static_cast<cuuint32_t>(n)};
+  const cuuint32_t elem[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 }  // namespace hattn
 }  // namespace moss
 
@@ -255,9 +538,40 @@ extern "C" int moss_history_attention(const void* q, const void* k_cache, const 
   Args a{static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
          static_cast<const uint16_t*>(v_cache), slot_pos, pos, static_cast<uint16_t*>(out),
          context, scale, static_cast<int>(h), static_cast<int>(t), static_cast<int>(n)};
+  cudaStream_t st = as_stream(stream);
+  // many items of at most 256 slots: the persistent kernel (two CTAs per SM
+  // streaming the next item while computing this one)
+  const int64_t items = s * h;
+  const int64_t sms = sm_count();
+  if (n <= kStreamMaxKeys && items >= 2 * sms && items * n < 0x7fffffffLL) {
+    StreamArgs sa;
+    if (!encode_ring(&sa.k_map, k_cache, items * n, static_cast<int>(n)))
+      return fail(MOSS_ERR_CUDA, "%s: tensor map encoding failed", name);
+    sa.a = Args{static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
+                static_cast<const uint16_t*>(v_cache), slot_pos, pos,
+                static_cast<uint16_t*>(out), context, scale, static_cast<int>(h),
+                static_cast<int>(t), static_cast<int>(n)};
+    sa.items = items;
+    const size_t sh = stream_smem(static_cast<int>(t), static_cast<int>(n));
+    const size_t sh_max = stream_smem(kMaxQueries, kStreamMaxKeys);
+    const unsigned sgrid = static_cast<unsigned>(2 * sms < items ? 2 * sms : items);
+#define MOSS_HATTN_STREAM(T)                                                            \
+  case T: {                                                                             \
+    static bool attr_done[kMaxDevices] = {};                                            \
+    allow_dynamic_smem(history_attn_stream_kernel<T>, sh_max, attr_done);               \
+    history_attn_stream_kernel<T><<<sgrid, kThreads, sh, st>>>(sa);                     \
+    break;                                                                              \
+  }
+    switch (t) {
+      MOSS_HATTN_STREAM(1) MOSS_HATTN_STREAM(2) MOSS_HATTN_STREAM(3) MOSS_HATTN_STREAM(4)
+      MOSS_HATTN_STREAM(5) MOSS_HATTN_STREAM(6) MOSS_HATTN_STREAM(7) MOSS_HATTN_STREAM(8)
+      default: break;
+    }
+#undef MOSS_HATTN_STREAM
+    return launch_status(name);
+  }
   const size_t shmem = smem_bytes(static_cast<int>(t), static_cast<int>(n));
   const unsigned grid = static_cast<unsigned>(s * h);
-  cudaStream_t st = as_stream(stream);
 #define MOSS_HATTN(T)                                                                   \
   case T: {                                                                             \
     static bool attr_done[kMaxDevices] = {};                                            \

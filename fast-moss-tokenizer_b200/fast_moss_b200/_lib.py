@@ -63,6 +63,7 @@ _SIGNATURES = {
     "moss_history_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _f, _vp, _vp]),
     "moss_gated_act": (_i, [_vp, _vp, _vp, _i, _i64, _i64, _i, _i, _vp]),
+    "moss_linear_pack_weight": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "moss_linear": (_i, [_vp, _i64, _i64, _vp, _i64, _vp, _i, _i, _vp, _vp]),
     "moss_linear_cluster": (_i, [_i64, _i64, _i64]),
     "moss_lfq_prepare": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp]),

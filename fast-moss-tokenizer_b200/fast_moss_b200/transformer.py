@@ -54,6 +54,7 @@ from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from .graphs import CapturedStep
 from .linear import linear as owned_linear
+from .linear import pack_weight
 from .v2_pointwise import (
     gated_activation,
     history_attention,
@@ -232,6 +233,9 @@ class StreamingTransformer:
                 p[k + "16"] = p[k].to(torch.bfloat16)
             if fused_qkv:
                 p["qkv_image"] = pack_qkv_weight(p["qkv_w16"])
+            if owned_linear:
+                for k in ("qkv_w", "out_w", "ffn1_w", "ffn2_w"):
+                    p[k + "_packed"] = pack_weight(p[k + "16"])
             self.layers.append(p)
         self.fused_qkv = bool(fused_qkv)
         if self.fused_qkv and cfg.head_dim != 64:
@@ -255,8 +259,10 @@ class StreamingTransformer:
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
 
-    def _linear(self, x, w, b):
-        return owned_linear(x, w, b) if self.owned_linear else F.linear(x, w, b)
+    def _linear(self, x, p, name):
+        if self.owned_linear:
+            return owned_linear(x, p[name + "_w_packed"], p[name + "_b16"])
+        return F.linear(x, p[name + "_w16"], p[name + "_b16"])
 
     def native_launches(self, streams):
         """Kernels of libfast_moss_b200 that one chunk step launches: the
@@ -292,7 +298,7 @@ class StreamingTransformer:
                 q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
                              slots, hist.keys[i], hist.values[i])
             else:
-                qkv = self._linear(normed, p["qkv_w16"], p["qkv_b16"])
+                qkv = self._linear(normed, p, "qkv")
                 qkv = qkv.view(s, t, 3, h, dh)
                 q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
                             qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
@@ -305,15 +311,16 @@ class StreamingTransformer:
                     a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
                                                        attn_mask=mask)
                 a = a.transpose(1, 2).reshape(s, t, d)
-            u = self._linear(a, p["out_w16"], p["out_b16"])
+            u = self._linear(a, p, "out")
             x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps,
                                             out_dtype=bf16)
             if self.owned_linear:
-                f = owned_linear(normed, p["ffn1_w16"], p["ffn1_b16"], activation=cfg.activation)
+                f = owned_linear(normed, p["ffn1_w_packed"], p["ffn1_b16"],
+                                 activation=cfg.activation)
             else:
                 f = F.linear(normed, p["ffn1_w16"])
                 f = gated_activation(f, p["ffn1_b16"], cfg.activation, cfg.gated)
-            u = self._linear(f, p["ffn2_w16"], p["ffn2_b16"])
+            u = self._linear(f, p, "ffn2")
             if i + 1 < len(self.layers):
                 nxt = self.layers[i + 1]
                 x, normed = residual_layer_norm(x, u, p["ls2"], nxt["norm1_w"], nxt["norm1_b"],

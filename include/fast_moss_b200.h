@@ -241,15 +241,20 @@ MOSS_API int moss_history_attention(const void* q, const void* k_cache, const vo
  * bias + activation (moss_gated_act, ungated):
  *   MOSS_LINEAR_BIAS      y = bf16(x w^T + bias)          (bias may be NULL)
  *   MOSS_LINEAR_BIAS_ACT  y = bf16(act(bf16(bf16(x w^T) + bias)))
- * x [m, k], w [n, k], bias [n], y [m, n]: bf16, row-major, 16-byte aligned;
- * k a multiple of 64, n a multiple of 128 (MOSS_ERR_UNSUPPORTED otherwise).
- * FP32 accumulation; K is split across the CTAs of a thread-block cluster
+ * x [m, k], bias [n], y [m, n]: bf16, row-major, 16-byte aligned; w_image:
+ * the weight w [n, k] packed once by moss_linear_pack_weight (n * k bf16:
+ * per 128-row tile and 64-column chunk a 16 KB block in the tensor cores'
+ * 128-byte-swizzled K-major layout, a tile's chunks back to back); k a
+ * multiple of 64, n of 128 (MOSS_ERR_UNSUPPORTED otherwise).  FP32
+ * accumulation; K is split across the CTAs of a thread-block cluster
  * (moss_linear_cluster(m, n, k) CTAs) whose partial sums are added in a
  * fixed order, so results are deterministic but summed in another order
  * than cuBLAS's: an output can differ from F.linear's by the rounding of a
  * different FP32 sum.
  * ------------------------------------------------------------------------- */
-MOSS_API int moss_linear(const void* x, int64_t m, int64_t k, const void* w, int64_t n,
+MOSS_API int moss_linear_pack_weight(const void* w, int64_t n, int64_t k, void* w_image,
+                            void* stream);
+MOSS_API int moss_linear(const void* x, int64_t m, int64_t k, const void* w_image, int64_t n,
                 const void* bias, int epilogue, int act, void* y, void* stream);
 MOSS_API int moss_linear_cluster(int64_t m, int64_t n, int64_t k);
 

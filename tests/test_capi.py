@@ -85,6 +85,8 @@ def test_bad_arguments_map_to_value_errors(lib):
     assert lib.moss_linear(None, 4, 128, None, 128, None, 5, 0, None, None) == _lib.ERR_VALUE
     assert lib.moss_linear(None, 0, 128, None, 128, None, 0, 0, None, None) == _lib.OK
     assert lib.moss_linear(None, 4, 128, None, 128, None, 0, 0, None, None) == _lib.ERR_VALUE
+    assert lib.moss_linear_pack_weight(None, 100, 128, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.moss_linear_pack_weight(None, 128, 128, None, None) == _lib.ERR_VALUE
     # the bounded-wait self-test takes limits of 1 us to 100 ms only
     assert lib.moss_test_bounded_wait(10, 0, None) == _lib.ERR_VALUE
     assert lib.moss_test_bounded_wait(10**9, 0, None) == _lib.ERR_VALUE

@@ -57,11 +57,11 @@ def _device_errors():
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
 def test_linear_bit_exact_on_exact_sums(moss, cuda_device, m, n, k):
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
 
     x, w, b = _integer_case(m, n, k, m + n + k, cuda_device)
     for bias in (b, None):
-        got = linear(x, w, bias)
+        got = linear(x, pack_weight(w), bias)
         want = _cublas(x, w, bias)
         _device_errors()
         assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (m, n, k, bias is None)
@@ -73,7 +73,7 @@ def test_linear_activation_epilogue_bit_exact(moss, cuda_device, m, n, k, act):
     """Integer operands scaled by 1/16 (still exact sums): the fused
     epilogue must give the bits of F.linear (no bias) followed by the
     eager bias + activation chain."""
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
 
     x, w, b = _integer_case(m, n, k, 3 * m + k, cuda_device)
     x = x * 0.0625
@@ -81,18 +81,19 @@ def test_linear_activation_epilogue_bit_exact(moss, cuda_device, m, n, k, act):
     f = _cublas(x, w, None)
     for bias in (b, None):
         want = moss.gated_activation(f, bias, act, False)
-        got = linear(x, w, bias, activation=act)
+        got = linear(x, pack_weight(w), bias, activation=act)
         _device_errors()
         assert torch.equal(got.view(torch.int16), want.view(torch.int16)), (act, bias is None)
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES[:8])
 def test_linear_random_within_one_ulp_of_the_sum_bound(moss, cuda_device, m, n, k):
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
 
     x, w, b = _random_case(m, n, k, 7 * m + n, cuda_device)
-    got = linear(x, w, b)
-    again = linear(x, w, b)
+    pw = pack_weight(w)
+    got = linear(x, pw, b)
+    again = linear(x, pw, b)
     want = _cublas(x, w, b)
     _device_errors()
     assert torch.equal(got.view(torch.int16), again.view(torch.int16))  # deterministic
@@ -107,26 +108,28 @@ def test_linear_random_within_one_ulp_of_the_sum_bound(moss, cuda_device, m, n, 
 
 
 def test_linear_leading_dims_and_out_buffer(moss, cuda_device):
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
 
     x, w, b = _integer_case(12, 256, 128, 5, cuda_device)
     out = torch.full((3, 4, 256), 7.0, device=cuda_device, dtype=torch.bfloat16)
-    got = linear(x.view(3, 4, 128), w, b, out=out)
+    got = linear(x.view(3, 4, 128), pack_weight(w), b, out=out)
     assert got is out
     assert torch.equal(out.view(12, 256), _cublas(x, w, b))
 
 
 def test_linear_rejects_shapes_it_does_not_cover(moss, cuda_device):
     from fast_moss_b200 import _lib
-    from fast_moss_b200.linear import linear
+    from fast_moss_b200.linear import linear, pack_weight
 
-    x = torch.zeros(4, 96, device=cuda_device, dtype=torch.bfloat16)
     with pytest.raises(_lib.UnsupportedError):
-        linear(x, torch.zeros(128, 96, device=cuda_device, dtype=torch.bfloat16))
+        pack_weight(torch.zeros(128, 96, device=cuda_device, dtype=torch.bfloat16))
+    with pytest.raises(_lib.UnsupportedError):
+        pack_weight(torch.zeros(100, 128, device=cuda_device, dtype=torch.bfloat16))
     x = torch.zeros(4, 128, device=cuda_device, dtype=torch.bfloat16)
-    with pytest.raises(_lib.UnsupportedError):
-        linear(x, torch.zeros(100, 128, device=cuda_device, dtype=torch.bfloat16))
+    pw = pack_weight(torch.zeros(128, 128, device=cuda_device, dtype=torch.bfloat16))
     with pytest.raises(ValueError):
-        linear(x.float(), torch.zeros(128, 128, device=cuda_device))
-    empty = linear(x[:0], torch.zeros(128, 128, device=cuda_device, dtype=torch.bfloat16))
+        linear(x.float(), pw)
+    with pytest.raises(ValueError):
+        linear(x, torch.zeros(128, 128, device=cuda_device, dtype=torch.bfloat16))  # not packed
+    empty = linear(x[:0], pw)
     assert empty.shape == (0, 128)
