@@ -96,6 +96,10 @@ def parse_args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     p.add_argument("--no-stack", action="store_true",
                    help="skip the stack variants (the headline always runs)")
+    p.add_argument("--section", choices=["kernels", "quantizer", "lfq_loop", "linear",
+                                         "attention"],
+                   help="run only this measurement on one GPU and print its JSON (for "
+                        "profiling single kernels; no headline line)")
     return p.parse_args()
 
 
@@ -1088,8 +1092,34 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+def run_section(args):
+    """One measurement alone, on cuda:0 (small device footprint)."""
+    import torch
+
+    from fast_moss_b200.transformer import StackConfig, init_weights
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = measured_peaks()
+    cfg = StackConfig()
+    if args.section == "kernels":
+        out = kernel_lines(torch, None, dev, peaks["hbm_gbs"])
+    elif args.section == "quantizer":
+        out = quantizer_lines(torch, dev, peaks, peak_src, args.steps, args.warmup, cpu=False)
+    elif args.section == "lfq_loop":
+        out = lfq_loop_line(torch, dev)
+    elif args.section == "linear":
+        out = _linear_kernel_line(torch, dev, cfg, init_weights(cfg, seed=2, device=dev))
+    else:
+        out = _attention_kernel_line(torch, dev, cfg)
+    print(json.dumps({"section": args.section, **out}), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.section:
+        run_section(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -79,4 +79,10 @@ __device__ __forceinline__ float activation_exact(float v) {
   }
 }
 
+// The per-device tables of the three activations over all 65536 bf16
+// inputs (gated_act.cu), and whether they are built on the current device
+// (the first call outside a stream capture builds them and waits).
+extern __device__ uint16_t g_act_lut[3 * 65536];
+bool act_lut_ready(cudaStream_t s);
+
 }  // namespace moss

@@ -199,7 +199,7 @@ __global__ void act_lut_kernel() {
 // While `s` is being captured nothing may be waited for, and a build
 // recorded into the graph would run only at its replay: the caller then
 // takes the register kernel, which gives the same bits.
-static bool act_lut_ready(cudaStream_t s) {
+bool act_lut_ready(cudaStream_t s) {
   static std::atomic<bool> ready[kMaxDevices];
   static std::mutex build;
   int dev = 0;

@@ -68,6 +68,7 @@ struct Params {
   int cluster;   // CTAs splitting K
   int epilogue;  // MOSS_LINEAR_*
   int act;       // MOSS_ACT_* (epilogue BIAS_ACT)
+  int use_lut;   // the activation tables are built: look act(h) up
 };
 
 __host__ __device__ inline uint32_t stage_bytes(int npad) {
@@ -155,10 +156,13 @@ __device__ __forceinline__ void st_async(uint32_t addr, float v, uint32_t bar) {
 
 // act(h) with h = f + bias rounded to bf16, f the Linear's bf16 output;
 // without a bias there is no add (so -0 stays -0, as in the eager chain).
+// With the tables built, act(h) rounded to bf16 is looked up (the tables
+// hold activation_exact of every bf16 input: the same bits).
 template <int ACT>
-__device__ __forceinline__ float bias_act(float acc, float b, bool has_bias) {
+__device__ __forceinline__ float bias_act(float acc, float b, bool has_bias, bool lut) {
   const float f = round_to<MOSS_BF16>(acc);
   const float h = has_bias ? round_to<MOSS_BF16>(__fadd_rn(f, b)) : f;
+  if (lut) return bf16_bits_to_f32(g_act_lut[ACT * 65536 + f32_to_bf16_bits(h)]);
   return activation_exact<ACT>(h);
 }
 
@@ -319,15 +323,16 @@ __global__ void __launch_bounds__(kThreads, 1) linear_kernel(const __grid_consta
         }
       } else if (p.act == MOSS_ACT_SILU) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = bias_act<MOSS_ACT_SILU>(v[e], b[e], p.bias != nullptr);
+        for (int e = 0; e < 8; ++e)
+          v[e] = bias_act<MOSS_ACT_SILU>(v[e], b[e], p.bias != nullptr, p.use_lut != 0);
       } else if (p.act == MOSS_ACT_GELU_ERF) {
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          v[e] = bias_act<MOSS_ACT_GELU_ERF>(v[e], b[e], p.bias != nullptr);
+          v[e] = bias_act<MOSS_ACT_GELU_ERF>(v[e], b[e], p.bias != nullptr, p.use_lut != 0);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          v[e] = bias_act<MOSS_ACT_GELU_TANH>(v[e], b[e], p.bias != nullptr);
+          v[e] = bias_act<MOSS_ACT_GELU_TANH>(v[e], b[e], p.bias != nullptr, p.use_lut != 0);
       }
       *reinterpret_cast<uint4*>(p.y + (m0 + j) * p.n + n0) = pack_bf16x8(v);
     }
@@ -464,6 +469,7 @@ extern "C" int moss_linear(const void* x, int64_t m, int64_t k, const void* w_im
   p.cluster = moss_linear_cluster(m, n, k);
   p.epilogue = epilogue;
   p.act = act;
+  p.use_lut = epilogue == MOSS_LINEAR_BIAS_ACT && act_lut_ready(as_stream(stream)) ? 1 : 0;
   const uint32_t sbytes = lin::stage_bytes(p.npad);
   int stages = static_cast<int>((lin::kSmemBudget - lin::recv_bytes(p.npad)) / sbytes);
   const int per_cta = (p.nchunks + p.cluster - 1) / p.cluster;

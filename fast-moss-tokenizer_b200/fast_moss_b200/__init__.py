@@ -7,12 +7,15 @@ and entry points (`optimized`, `StreamingCodec`, `codec`, `encode_fixed`,
 libfast_moss_b200.so, plus
 the fused forms (residual + LayerNorm, in-kernel RoPE phase, gated
 activation, fused LFQ decode, the whole multi-stage residual VQ in one
-kernel), and the streaming transformer stack with its batched CUDA-graph
-scheduler (`StreamingTransformer`, `BatchedStreams`).
+kernel, the real codec's 32-stage LFQ loop in one kernel, a tcgen05 Linear
+with its activation epilogue), and the streaming transformer stack with
+its batched CUDA-graph scheduler (`StreamingTransformer`, `BatchedStreams`).
 """
 
 from . import _lib
-from .graphs import GraphedCallable
+from .graphs import CapturedStep, GraphedCallable
+from .lfq_rvq import LFQResidualQuantizer
+from .linear import PackedWeight, linear, pack_weight
 from .quantizer import decode_latents, select
 from .quantizer_prepare import prepare
 from .rvq import ResidualVectorQuantizer
@@ -50,6 +53,11 @@ __all__ = [
     "prepare",
     "ResidualVectorQuantizer",
     "GraphedCallable",
+    "CapturedStep",
+    "LFQResidualQuantizer",
+    "linear",
+    "pack_weight",
+    "PackedWeight",
     "StreamingCodec",
     "StackConfig",
     "StreamingTransformer",

@@ -16,7 +16,8 @@
  *     -> RuntimeError, the same exception classes the reference raises.
  *   - Calls on distinct streams are independent.  The only state shared
  *     between calls is read-only after its first use on a device: the SM
- *     count and the bf16 activation tables of moss_gated_act.  The tables
+ *     count and the bf16 activation tables of moss_gated_act (also read by
+ *     moss_linear's activation epilogue).  The tables
  *     are built by one kernel at the first moss_gated_act call on a device
  *     that is large enough to use them (2^22 outputs) and is not inside a
  *     stream capture; that call waits for the caller's stream once.  Calls
@@ -250,7 +251,10 @@ MOSS_API int moss_history_attention(const void* q, const void* k_cache, const vo
  * (moss_linear_cluster(m, n, k) CTAs) whose partial sums are added in a
  * fixed order, so results are deterministic but summed in another order
  * than cuBLAS's: an output can differ from F.linear's by the rounding of a
- * different FP32 sum.
+ * different FP32 sum.  The activation epilogue looks act(h) up in the
+ * activation tables of moss_gated_act when they are built (same bits); like
+ * there, the first such call on a device outside a stream capture builds
+ * them and waits for the caller's stream once.
  * ------------------------------------------------------------------------- */
 MOSS_API int moss_linear_pack_weight(const void* w, int64_t n, int64_t k, void* w_image,
                             void* stream);
