@@ -979,10 +979,10 @@ def step_roofline(torch, dev, cfg, peaks, ms_per_chunk):
     chunk_bytes = weight_bytes + ring_bytes
     return {
         "bound": "hbm",
-        "kernel": "history_attn_kernel (moss_history_attention: 64 streams x 20 heads, 4 queries "
-                  "over 253 ring slots of 64, bf16)",
+        "kernel": "history_attn_stream_kernel (moss_history_attention: 64 streams x 20 heads, "
+                  "4 queries over 253 ring slots of 64, bf16)",
         "achieved": att["owned_gbs"], "peak": hbm, "unit": "GB/s", "frac": att["owned_gbs"] / hbm,
-        "traffic": profile_traffic("history_attn_kernel"),
+        "traffic": profile_traffic("history_attn_stream_kernel"),
         "bytes_per_launch": att["bytes"], "us_per_launch": att["us_owned"],
         "us_per_launch_sdpa": att["us_sdpa"],
         "step": {"what": "one chunk of all 64 streams: bf16 weights of 24 layers + every layer's "

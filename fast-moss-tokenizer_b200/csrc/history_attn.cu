@@ -255,10 +255,11 @@ struct StreamArgs {
 };
 
 __host__ __device__ constexpr size_t stream_smem(int t, int n) {
-  // K (whole 1024-byte swizzle atoms) | V | weights [t][np] | partial sums
-  // [warps][t][64] | q [t][64] | reduction slots | 2 mbarriers
+  // K (whole 1024-byte swizzle atoms) | V | weights [n][4 or 8] (key-major,
+  // so P.V reads one key's weights of every query with one vector load) |
+  // partial sums [warps][t][64] | q [t][64] | reduction slots | 2 mbarriers
   return static_cast<size_t>((n + 7) / 8) * 1024 + static_cast<size_t>(n) * kDim * 2 +
-         static_cast<size_t>(t) * padded_keys(n) * 4 + static_cast<size_t>(kWarps) * t * kDim * 4 +
+         static_cast<size_t>(n) * (t <= 4 ? 4 : 8) * 4 + static_cast<size_t>(kWarps) * t * kDim * 4 +
          static_cast<size_t>(t) * kDim * 4 + static_cast<size_t>(kWarps) * kMaxQueries * 4 + 16 +
          1024;
 }
@@ -278,13 +279,13 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
   extern __shared__ unsigned char smem_raw[];
   const Args& a = sa.a;
   const int n = a.n;
-  const int np = padded_keys(n);
+  constexpr int TP = T <= 4 ? 4 : 8;  // weights per key row (queries, padded)
   unsigned char* ks = smem_raw + ((1024u - (static_cast<uint32_t>(
                                                  __cvta_generic_to_shared(smem_raw)) & 1023u)) &
                                   1023u);
   unsigned char* vs = ks + static_cast<size_t>((n + 7) / 8) * 1024;
-  float* ps = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [T][np]
-  float* part = ps + T * np;                                                     // [warps][T][64]
+  float* ps = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [n][TP]
+  float* part = ps + n * TP;                                                     // [warps][T][64]
   float* qs = part + kWarps * T * kDim;                                          // [T][64]
   float* red = qs + T * kDim;                                                    // [warps][8]
   unsigned long long* kfull = reinterpret_cast<unsigned long long*>(red + kWarps * kMaxQueries);
@@ -312,6 +313,12 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     issue_k(item);
     issue_v(item);
   }
+  // Keys: thread tid < 128 scores keys tid and tid + 128 (every query
+  // value it loads serves two keys); the other threads score none.
+  constexpr int kPair = kStreamMaxKeys / 2;
+  static_assert(kKeysPerThread == 2 && 2 * kPair == kStreamMaxKeys,
+                "128 threads x 2 keys must cover the ring");
+  auto key_of = [&](int m) { return tid < kPair ? tid + m * kPair : kStreamMaxKeys; };
   // this item's queries, slot positions and position, in registers
   auto load_meta = [&](int64_t it, float (&qv)[(T * kDim + kThreads - 1) / kThreads],
                        int64_t (&held)[kKeysPerThread], int64_t& p0) {
@@ -324,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     }
 #pragma unroll
     for (int m = 0; m < kKeysPerThread; ++m) {
-      const int j = tid + m * kThreads;
+      const int j = key_of(m);
       held[m] = j < n ? a.slot_pos[s * n + j] : -1;
     }
     p0 = a.pos[s];
@@ -348,42 +355,47 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     const int kok = pipe::mbar_wait(kfull, i & 1) ? 1 : 0;
     done_k = i + kok;  // loads this thread saw land
     if (__syncthreads_or(!kok)) break;  // K and the queries are visible to all
-    // ---- scores: thread tid takes keys tid and tid + 256
+    // ---- scores: thread tid < 128 takes keys tid and tid + 128; each key's
+    // dot products are summed in the same order as history_attn_kernel's
     float sc[kKeysPerThread][T];
 #pragma unroll
-    for (int m = 0; m < kKeysPerThread; ++m) {
-      const int j = tid + m * kThreads;
+    for (int m = 0; m < kKeysPerThread; ++m)
 #pragma unroll
       for (int t = 0; t < T; ++t) sc[m][t] = -CUDART_INF_F;
-      if (j < n) {
-        float acc[T];
+    if (tid < kPair) {
+      const int j0 = tid, j1 = tid + kPair;
+      const bool v0 = j0 < n, v1 = j1 < n;  // rows past n are never read
+      float acc0[T], acc1[T];
 #pragma unroll
-        for (int t = 0; t < T; ++t) acc[t] = 0.0f;
+      for (int t = 0; t < T; ++t) acc0[t] = acc1[t] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(ks + j * 128 + ((c ^ (j & 7)) << 4));
-          float kv[8];
-          unpack_bf16x8(raw, kv);
-#pragma unroll
-          for (int t = 0; t < T; ++t) {
-            const float4 qa = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8);
-            const float4 qb = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8 + 4);
-            acc[t] = __fmaf_rn(qa.x, kv[0], acc[t]);
-            acc[t] = __fmaf_rn(qa.y, kv[1], acc[t]);
-            acc[t] = __fmaf_rn(qa.z, kv[2], acc[t]);
-            acc[t] = __fmaf_rn(qa.w, kv[3], acc[t]);
-            acc[t] = __fmaf_rn(qb.x, kv[4], acc[t]);
-            acc[t] = __fmaf_rn(qb.y, kv[5], acc[t]);
-            acc[t] = __fmaf_rn(qb.z, kv[6], acc[t]);
-            acc[t] = __fmaf_rn(qb.w, kv[7], acc[t]);
-          }
-        }
+      for (int c = 0; c < 8; ++c) {
+        float k0[8], k1[8];
+        const uint4 r0 = v0 ? *reinterpret_cast<const uint4*>(ks + j0 * 128 + ((c ^ (j0 & 7)) << 4))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 r1 = v1 ? *reinterpret_cast<const uint4*>(ks + j1 * 128 + ((c ^ (j1 & 7)) << 4))
+                            : make_uint4(0u, 0u, 0u, 0u);
+        unpack_bf16x8(r0, k0);
+        unpack_bf16x8(r1, k1);
 #pragma unroll
         for (int t = 0; t < T; ++t) {
-          const int64_t qp = p0 + t;
-          const bool on = held[m] >= 0 && held[m] <= qp && held[m] > qp - a.context;
-          sc[m][t] = on ? __fmul_rn(acc[t], a.scale) : -CUDART_INF_F;
+          const float4 qa = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8 + 4);
+          const float qq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            acc0[t] = __fmaf_rn(qq[e], k0[e], acc0[t]);
+            acc1[t] = __fmaf_rn(qq[e], k1[e], acc1[t]);
+          }
         }
+      }
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        const int64_t qp = p0 + t;
+        const bool on0 = v0 && held[0] >= 0 && held[0] <= qp && held[0] > qp - a.context;
+        const bool on1 = v1 && held[1] >= 0 && held[1] <= qp && held[1] > qp - a.context;
+        sc[0][t] = on0 ? __fmul_rn(acc0[t], a.scale) : -CUDART_INF_F;
+        sc[1][t] = on1 ? __fmul_rn(acc1[t], a.scale) : -CUDART_INF_F;
       }
     }
     float mx[T];
@@ -410,19 +422,33 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     }
     __syncthreads();  // the maxima are read before `red` takes the sums
     float l[T];
+    float sum[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) sum[t] = 0.0f;
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) {
+      const int j = key_of(m);
+      float e[TP];
+#pragma unroll
+      for (int t = 0; t < TP; ++t) e[t] = 0.0f;
+#pragma unroll
+      for (int t = 0; t < T; ++t) {
+        e[t] = (j < n && mx[t] != -CUDART_INF_F) ? expf(__fsub_rn(sc[m][t], mx[t])) : 0.0f;
+        sum[t] = __fadd_rn(sum[t], e[t]);
+      }
+      if (j < n) {
+#pragma unroll
+        for (int c = 0; c < TP / 4; ++c)
+          *reinterpret_cast<float4*>(ps + j * TP + 4 * c) =
+              make_float4(e[4 * c], e[4 * c + 1], e[4 * c + 2], e[4 * c + 3]);
+      }
+    }
 #pragma unroll
     for (int t = 0; t < T; ++t) {
-      float sum = 0.0f;
+      float s_t = sum[t];
 #pragma unroll
-      for (int m = 0; m < kKeysPerThread; ++m) {
-        const int j = tid + m * kThreads;
-        const float e = (j < n && mx[t] != -CUDART_INF_F) ? expf(__fsub_rn(sc[m][t], mx[t])) : 0.0f;
-        if (j < n) ps[t * np + j] = e;
-        sum = __fadd_rn(sum, e);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-      if (lane == 0) red[warp * kMaxQueries + t] = sum;
+      for (int o = 16; o > 0; o >>= 1) s_t = __fadd_rn(s_t, __shfl_xor_sync(0xffffffffu, s_t, o));
+      if (lane == 0) red[warp * kMaxQueries + t] = s_t;
     }
     // the next item's metadata while V lands
     float qn[QC];
@@ -445,11 +471,16 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     for (int j = warp; j < n; j += kWarps) {
       const uint32_t raw = *reinterpret_cast<const uint32_t*>(vs + j * 128 + lane * 4);
       const float v0 = __uint_as_float(raw << 16), v1 = __uint_as_float(raw & 0xffff0000u);
+      float p[TP];
+#pragma unroll
+      for (int c = 0; c < TP / 4; ++c) {
+        const float4 p4 = *reinterpret_cast<const float4*>(ps + j * TP + 4 * c);
+        p[4 * c] = p4.x; p[4 * c + 1] = p4.y; p[4 * c + 2] = p4.z; p[4 * c + 3] = p4.w;
+      }
 #pragma unroll
       for (int t = 0; t < T; ++t) {
-        const float p = ps[t * np + j];
-        o0[t] = __fmaf_rn(p, v0, o0[t]);
-        o1[t] = __fmaf_rn(p, v1, o1[t]);
+        o0[t] = __fmaf_rn(p[t], v0, o0[t]);
+        o1[t] = __fmaf_rn(p[t], v1, o1[t]);
       }
     }
 #pragma unroll

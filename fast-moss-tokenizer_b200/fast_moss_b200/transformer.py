@@ -184,14 +184,18 @@ class StreamHistory:
                 self.slot_pos.index_fill_(0, idx, -1)
                 self.pos.index_fill_(0, idx, 0)
 
-    def advance(self, tokens):
+    def advance(self, tokens, *, mask=True):
         """Writes the slot positions of the next `tokens` tokens and returns
-        (positions [S, T], slots [S, T], attention mask [S, 1, T, slots])."""
+        (positions [S, T], slots [S, T], attention mask [S, 1, T, slots] or
+        None when `mask` is false: the history attention kernel derives the
+        mask from the slot positions itself)."""
         if not 1 <= tokens <= self.max_tokens:
             raise ValueError(f"a chunk holds 1 to {self.max_tokens} tokens")
         positions = self.pos[:, None] + torch.arange(tokens, device=self.pos.device)
         slots = torch.remainder(positions, self.slot_pos.shape[1])
         self.slot_pos.scatter_(1, slots, positions)
+        if not mask:
+            return positions, slots, None
         held = self.slot_pos[:, None, :]
         query = positions[:, :, None]
         mask = (held >= 0) & (held <= query) & (held > query - self.context)
@@ -285,7 +289,7 @@ class StreamingTransformer:
             raise ValueError("expected a [streams, tokens, dim] FP32 chunk on the stack's device")
         h, dh = cfg.heads, cfg.head_dim
         offset = hist.pos  # position of the chunk's first token (advanced at the end)
-        _, slots, mask = hist.advance(t)
+        _, slots, mask = hist.advance(t, mask=not self.history_attention)
         if not self.history_attention:
             mask = additive_mask(mask, torch.bfloat16)
         first = self.layers[0]
