@@ -813,28 +813,33 @@ def quantizer_lines(torch, dev, peaks, peak_src, steps, warmup, cpu):
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
 
-    def launch(entry, c, r):
+    def launch(entry, c, r, *kernel):
         _lib.check(getattr(lib, entry)(
             x.data_ptr(), FRAMES, DIM, rvq.books.data_ptr(), rvq.packed.data_ptr(),
             rvq.code_norm.data_ptr(), rvq.stats.data_ptr(), STAGES, CODES, c.data_ptr(),
-            r.data_ptr(), None, sh), entry)
+            r.data_ptr(), None, *kernel, sh), entry)
 
-    def timed(entry, n, c, r):
+    def timed(entry, n, c, r, *kernel):
         for _ in range(max(warmup, 3)):
-            launch(entry, c, r)
+            launch(entry, c, r, *kernel)
         s = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         e = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
         for i in range(n):
             flush.fill_(float(i))  # evict the previous launch's data from L2 (untimed)
             s[i].record(stream)
-            launch(entry, c, r)
+            launch(entry, c, r, *kernel)
             e[i].record(stream)
         torch.cuda.synchronize()
         return sum(a.elapsed_time(b) for a, b in zip(s, e)) * 1e-3 / n
 
     n = max(steps, 10)
+    # moss_rvq_encode: the single-CTA kernel (MOSS_RVQ_AUTO)
     tc_s = timed("moss_rvq_encode", n, codes, recon)
     ok = bool(torch.equal(rvq.decode(codes), recon))
+    codes_2 = torch.empty_like(codes)
+    recon_2 = torch.empty_like(recon)
+    pair_s = timed("moss_rvq_encode_kernel", n, codes_2, recon_2, 2)  # MOSS_RVQ_PAIR
+    ok = ok and bool(torch.equal(codes_2, codes)) and bool(torch.equal(recon_2, recon))
     codes_f = torch.empty_like(codes)
     recon_f = torch.empty_like(recon)
     ffma_s = timed("moss_rvq_encode_ffma", max(3, min(n, 20)), codes_f, recon_f)
@@ -889,6 +894,10 @@ def quantizer_lines(torch, dev, peaks, peak_src, steps, warmup, cpu):
                                     f"({peaks['bf16_tflops']} TFLOP/s)",
                      "flop_per_launch": flop, "fp32_ffma_peak": fp32_peak,
                      "frac_of_fp32_ffma_peak": flop / tc_s / 1e12 / fp32_peak},
+        "pair": {"kernel": "rvq_pair_kernel (CTA pairs, each screening half of every "
+                           "codebook, one key per row exchanged per stage; identical codes)",
+                 "us_per_launch": pair_s * 1e6, "achieved_tflops": flop / pair_s / 1e12,
+                 "frac_of_tf32_peak": flop / pair_s / 1e12 / tf32_peak},
         "ffma": {"kernel": "rvq_encode_kernel (all-FFMA, identical codes)",
                  "us_per_launch": ffma_s * 1e6, "achieved_tflops": flop / ffma_s / 1e12,
                  "frac_of_fp32_ffma_peak": flop / ffma_s / 1e12 / fp32_peak},

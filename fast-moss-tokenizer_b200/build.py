@@ -18,7 +18,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB = os.path.join(HERE, "fast_moss_b200", "libfast_moss_b200.so")
 SOURCES = ["capi.cu", "layer_norm.cu", "rope.cu", "gated_act.cu", "lfq.cu", "rvq.cu",
-           "rvq_tc.cu", "rvq_noalloc.cu", "qkv_rope.cu", "history_attn.cu", "linear.cu",
+           "rvq_tc.cu", "rvq_pair.cu", "rvq_noalloc.cu", "qkv_rope.cu", "history_attn.cu", "linear.cu",
            "lfq_rvq.cu"]
 
 NVCC_FLAGS = [

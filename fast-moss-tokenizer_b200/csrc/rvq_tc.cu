@@ -24,10 +24,13 @@
 // (rare, short) record of {chunk, mask, chunk max} in shared memory; the
 // records are filtered against the final window at the end of the stage.
 //
-// A CTA owns `rows_per_cta` rows for all stages, 320 threads:
-//   warps 0-7  epilogue (256 threads).  With at most 64 rows per CTA (the
-//              default while the rows fit one CTA per SM: 8192 rows -> 147
-//              CTAs of 56) every row is written into two TMEM lanes (lane i
+// This kernel gives one CTA its rows for the whole codebook; rvq_pair.cu
+// splits each codebook over a CTA pair and is used wherever it applies (at
+// least two 256-code tiles, the rows within one wave of pairs).  Here a CTA
+// owns `rows_per_cta` rows for all stages, 320 threads:
+//   warps 0-7  epilogue (256 threads).  With at most 64 rows per CTA (while
+//              the rows fit one CTA per SM: e.g. 8192 rows -> 147 CTAs of
+//              56) every row is written into two TMEM lanes (lane i
 //              and 64 + i), so four threads screen its 256 columns per tile
 //              (two lane copies x two column halves); with 128 rows per CTA
 //              each row has one lane and two threads.  The part-0 thread of
@@ -40,28 +43,10 @@
 //              (M=128, N=256, K=8) into one of two 256-column accumulators.
 // Every wait is bounded (~2 s) and records MOSS_ERR_TIMEOUT; all roles then
 // meet at the final barrier where the TMEM is released.
-#include "common.cuh"
-
-#include <math_constants.h>
+#include "rvq_tc.cuh"
 
 namespace moss {
 namespace rvqtc {
-
-constexpr int kDim = 64;
-constexpr int kRows = 128;
-constexpr int kTileCodes = 256;
-constexpr int kSlots = 2;
-constexpr int kRec = 8;       // screening records per row, column half and stage
-constexpr int kQueue = 256;   // candidates resolved exactly per epilogue warp and stage
-constexpr int kEpiThreads = 256;  // two threads per row (column halves)
-constexpr int kThreads = kEpiThreads + 64;
-constexpr int kProducerWarp = kEpiThreads / 32;
-constexpr int kMmaWarp = kProducerWarp + 1;
-constexpr uint32_t kMainBytes = kTileCodes * kDim * 4;   // 65536: swizzled dims
-constexpr uint32_t kExtraBytes = kTileCodes * 8 * 4;     // 8192: norm column block
-constexpr uint32_t kTileBytes = kMainBytes + kExtraBytes;  // 73728 per tile image
-constexpr uint32_t kTmemCols = 512;
-constexpr int kMaxCodes = 4096;
 
 struct __align__(1024) Smem {
   float btile[kSlots][kTileBytes / 4];  // tile images (each 1024-aligned)
@@ -92,279 +77,6 @@ struct __align__(1024) Smem {
 };
 // The dynamic allocation adds 1024 bytes of alignment slack.
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the sm_100 per-block limit");
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
-               : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-               "r"(bytes)
-               : "memory");
-}
-// The waiting thread is suspended (up to ~20 us per attempt) instead of
-// spinning, so waiting roles leave the issue slots to the epilogue warps.
-__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (~2 s); false after recording a timeout.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t parity) {
-  return bounded_wait([&] { return mbar_try_wait(bar, parity); });
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
-                                         unsigned long long* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// Barrier of the epilogue warps (both column halves).
-__device__ __forceinline__ void epi_bar() {
-  __syncwarp();
-  asm volatile("bar.sync 1, 256;" ::: "memory");
-}
-__device__ __forceinline__ int epi_bar_or(int pred) {
-  int out;
-  __syncwarp();
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.b32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 2, 256, p;\n\t"
-      "selp.b32 %0, 1, 0, q;\n\t}"
-      : "=r"(out)
-      : "r"(pred)
-      : "memory");
-  return out;
-}
-
-// Shared-memory matrix descriptors (descriptor version 1).
-//   K-major, 128-byte swizzle, 8-row groups 1024 bytes apart (SBO).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) |
-         (1ull << 46) | (2ull << 61);
-}
-//   K-major, no swizzle: 8-row x 16-byte core matrices; the two K halves
-//   128 bytes apart (LBO), 8-row groups 256 bytes apart (SBO).
-__device__ __forceinline__ uint64_t plain_desc(uint32_t saddr) {
-  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (8ull << 16) | (16ull << 32) |
-         (1ull << 46);
-}
-// Instruction descriptor: kind::tf32, D f32, A/B tf32 K-major, M=128, N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((256u >> 3) << 17) |
-                            ((128u >> 4) << 24);
-
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(unsigned long long* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
-
-// 32 consecutive accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
-  __syncwarp();  // .sync.aligned: the whole warp, converged
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr)
-      : "memory");
-}
-// Waits for the outstanding TMEM loads; the registers are threaded through so
-// that no use of them can be scheduled before the wait.
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
-  __syncwarp();
-  asm volatile(
-      "tcgen05.wait::ld.sync.aligned;"
-      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
-        "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
-        "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
-        "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
-        "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-      :
-      : "memory");
-}
-
-// Byte offset of (row, k) in a K-major SW128 image: 8-row groups 1024 bytes
-// apart, 16-byte chunk index XOR row % 8, the two 32-element K halves `half`
-// bytes apart.  The tile images built by rvq.cu use the same formula.
-__device__ __forceinline__ uint32_t sw128_offset(int row, int k, uint32_t half) {
-  const int kk = k & 31;
-  return static_cast<uint32_t>(k >> 5) * half + static_cast<uint32_t>(row >> 3) * 1024u +
-         static_cast<uint32_t>(row & 7) * 128u +
-         static_cast<uint32_t>(((kk >> 2) ^ (row & 7)) << 4) + static_cast<uint32_t>(kk & 3) * 4u;
-}
-// Byte offset of (row, k < 8) in the no-swizzle K block.
-__device__ __forceinline__ uint32_t plain_offset(int row, int k) {
-  return static_cast<uint32_t>(row >> 3) * 256u + static_cast<uint32_t>(k >> 2) * 128u +
-         static_cast<uint32_t>(row & 7) * 16u + static_cast<uint32_t>(k & 3) * 4u;
-}
-
-struct Args {
-  const float* x;
-  const float* books;      // raw [stages][k][64]
-  const float* image;      // [stages][ntiles][kTileBytes]
-  const float* code_norm;  // [stages][kpad]
-  const float* stats;      // [stages][4]: max code norm, non-finite flag
-  int32_t* codes;
-  float* recon;
-  float* residual_out;
-  int64_t rows;
-  int stages;
-  int k;
-  int kpad;
-  int rows_per_cta;  // 128, or 64 with every row in two TMEM lanes
-};
-
-// Exact NaN-aware selection of one row by one warp (pinned arithmetic).
-__device__ int exact_scan(const float* tw, float norm, const float* __restrict__ book,
-                          const float* __restrict__ cnorm, int k, int lane) {
-  float best = CUDART_INF_F;
-  int best_i = lane;
-  int nan_i = INT_MAX;
-  for (int j = lane; j < k; j += 32) {
-    const float* c = book + static_cast<int64_t>(j) * kDim;
-    float dot = 0.0f;
-    for (int d = 0; d < kDim; ++d) dot = __fmaf_rn(tw[d], c[d], dot);
-    const float dist = __fadd_rn(__fsub_rn(norm, dot), cnorm[j]);
-    if (dist != dist) {
-      if (j < nan_i) nan_i = j;
-    } else if (dist < best) {
-      best = dist;
-      best_i = j;
-    }
-  }
-#pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, m);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_i, m);
-    const int on = __shfl_xor_sync(0xffffffffu, nan_i, m);
-    if (ob < best || (ob == best && oi < best_i)) {
-      best = ob;
-      best_i = oi;
-    }
-    nan_i = min(nan_i, on);
-  }
-  return nan_i != INT_MAX ? nan_i : best_i;
-}
-
-__device__ __forceinline__ void prefetch_l1(const void* p) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
-}
-
-// Shared-memory vector store at a 32-bit shared address.
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, float x0, float x1, float x2,
-                                             float x3) {
-  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(x0), "f"(x1), "f"(x2),
-               "f"(x3)
-               : "memory");
-}
-
-// Keeps the records (of one column half) whose chunk maximum is still
-// inside the window.
-__device__ __noinline__ int compact_records(Smem& sm, int slot, float athr) {
-  int w = 0;
-  for (int e = 0; e < kRec; ++e) {
-    if (sm.rec_max[e][slot] >= athr) {
-      sm.rec_max[w][slot] = sm.rec_max[e][slot];
-      sm.rec_mask[w][slot] = sm.rec_mask[e][slot];
-      sm.rec_chunk[w][slot] = sm.rec_chunk[e][slot];
-      ++w;
-    }
-  }
-  return w;
-}
-
-// Screening record: stores {chunk max, mask, chunk} and returns the new
-// record count (kRec + 1 once the records overflowed; compaction of records
-// that left the window is the rare case).
-__device__ __forceinline__ int add_record(Smem& sm, int slot, int chunk, uint32_t mask, float cmx,
-                                          float athr, int nrec) {
-  if (nrec >= kRec) {
-    if (nrec > kRec) return nrec;
-    nrec = compact_records(sm, slot, athr);
-    if (nrec == kRec) return kRec + 1;
-  }
-  sm.rec_max[nrec][slot] = cmx;
-  sm.rec_mask[nrec][slot] = mask;
-  sm.rec_chunk[nrec][slot] = static_cast<unsigned char>(chunk);
-  return nrec + 1;
-}
-
-// Float ordering as an unsigned key (finite values; -0 is mapped to +0 by
-// the caller so that equal distances compare equal).
-__device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// Maximum of 32 accumulator values: a depth-4 tree of three-input maxima
-// (16 instructions).
-__device__ __forceinline__ float max32(const uint32_t (&acc)[32]) {
-  float m[11];
-#pragma unroll
-  for (int j = 0; j < 10; ++j)
-    m[j] = max3f(__uint_as_float(acc[3 * j]), __uint_as_float(acc[3 * j + 1]),
-                 __uint_as_float(acc[3 * j + 2]));
-  m[10] = fmaxf(__uint_as_float(acc[30]), __uint_as_float(acc[31]));
-  const float a = max3f(m[0], m[1], m[2]), b = max3f(m[3], m[4], m[5]);
-  const float c = max3f(m[6], m[7], m[8]), d = fmaxf(m[9], m[10]);
-  return fmaxf(max3f(a, b, c), d);
-}
-
-// Bit j set iff acc[j] >= athr; four independent 8-bit partial masks.
-__device__ __forceinline__ uint32_t mask32(const uint32_t (&acc)[32], float athr) {
-  uint32_t part[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-#pragma unroll
-    for (int p = 0; p < 4; ++p)
-      part[p] |= (__uint_as_float(acc[8 * p + j]) >= athr) ? (1u << (8 * p + j)) : 0u;
-  }
-  return (part[0] | part[1]) | (part[2] | part[3]);
-}
 
 __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   extern __shared__ unsigned char smem_raw[];
@@ -843,12 +555,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
 
 using namespace moss;
 
-extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const float* books,
-                               const float* packed, const float* code_norm, const float* stats,
-                               int64_t stages, int64_t k, int32_t* codes, float* recon,
-                               float* residual_out, void* stream) {
+namespace moss {
+int rvq_pair_capacity(size_t smem);
+size_t rvq_pair_smem();
+int launch_rvq_pair(const rvqtc::Args& args, int64_t pairs, void* stream);
+}  // namespace moss
+
+extern "C" int moss_rvq_encode_kernel(const float* x, int64_t rows, int64_t d, const float* books,
+                                      const float* packed, const float* code_norm,
+                                      const float* stats, int64_t stages, int64_t k,
+                                      int32_t* codes, float* recon, float* residual_out,
+                                      int kernel, void* stream) {
   const char* name = "moss_rvq_encode";
   if (rows < 0 || stages < 1 || k < 1) return fail(MOSS_ERR_VALUE, "%s: bad shape", name);
+  if (kernel != MOSS_RVQ_AUTO && kernel != MOSS_RVQ_SINGLE && kernel != MOSS_RVQ_PAIR)
+    return fail(MOSS_ERR_VALUE, "%s: unknown kernel %d", name, kernel);
   if (d != rvqtc::kDim) return fail(MOSS_ERR_UNSUPPORTED, "%s: only 64-dim codewords are supported", name);
   if (k > rvqtc::kMaxCodes || stages > 65535)
     return fail(MOSS_ERR_UNSUPPORTED, "%s: at most 4096 codes per stage (use moss_rvq_encode_ffma)", name);
@@ -859,31 +580,61 @@ extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const fl
       !aligned16(recon) || (residual_out && !aligned16(residual_out)))
     return fail(MOSS_ERR_VALUE, "%s: buffers must be 16-byte aligned", name);
   const int64_t kpad = (k + rvqtc::kTileCodes - 1) / rvqtc::kTileCodes * rvqtc::kTileCodes;
-  // While the rows fit one CTA per SM at 64 rows per CTA, they are spread
-  // evenly over all SMs (ceil(rows / SMs) rows per CTA, each row in two
-  // TMEM lanes so four threads share its columns: 8192 rows -> 147 CTAs of
-  // 56); above that a CTA takes 128 rows, one lane each.
   const int64_t sms = sm_count();
+  // The tensor-core tile images follow the FFMA layout in the packed buffer.
+  const float* image = packed + stages * kpad * rvqtc::kDim;
+  rvqtc::Args args{x, books, image, code_norm, stats, codes, recon, residual_out, rows,
+                   static_cast<int>(stages), static_cast<int>(k), static_cast<int>(kpad), 0};
+
+  // CTA pairs (rvq_pair.cu) on request, where the codebook has at least two
+  // 256-code tiles and the rows fit one wave of pairs at <= 128 rows each:
+  // the rows are spread evenly over the pairs that fit on the device at once
+  // (8192 rows on 148 SMs -> 74 pairs of 111).  MOSS_RVQ_AUTO takes the
+  // single-CTA kernel, the faster of the two as measured at 8192 x 32 x 1024.
+  if (kernel == MOSS_RVQ_PAIR) {
+    const int64_t ntiles = kpad / rvqtc::kTileCodes;
+    int64_t pairs_max = ntiles >= 2 ? rvq_pair_capacity(rvq_pair_smem()) : 0;
+    if (pairs_max > sms / 2) pairs_max = sms / 2;
+    if (pairs_max >= 1 && rows <= pairs_max * rvqtc::kRows) {
+      const int64_t per_pair = (rows + pairs_max - 1) / pairs_max;
+      args.rows_per_cta = static_cast<int>(per_pair);
+      return launch_rvq_pair(args, (rows + per_pair - 1) / per_pair, stream);
+    }
+    return fail(MOSS_ERR_UNSUPPORTED,
+                  "%s: the pair kernel needs at least 257 codes and at most 128 rows per pair "
+                  "(%lld pairs fit on this device)",
+                  name, static_cast<long long>(pairs_max));
+  }
+
+  // One CTA per row block, the whole codebook each: while the rows fit one
+  // CTA per SM at 64 rows per CTA, they are spread evenly over all SMs
+  // (ceil(rows / SMs) rows per CTA, each row in two TMEM lanes so four
+  // threads share its columns); above that a CTA takes 128 rows, one lane
+  // each.
   const int rows_per_cta =
       rows <= sms * 64 ? static_cast<int>((rows + sms - 1) / sms) : rvqtc::kRows;
   const int64_t grid = (rows + rows_per_cta - 1) / rows_per_cta;
   if (grid > 0x7fffffffLL) return fail(MOSS_ERR_UNSUPPORTED, "%s: too many rows", name);
+  args.rows_per_cta = rows_per_cta;
   const size_t smem = sizeof(rvqtc::Smem) + 1024;
-  static bool configured[64] = {false};
+  static bool configured[kMaxDevices] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  if (dev < 0 || dev >= kMaxDevices || !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(rvqtc::rvq_tc_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return fail(MOSS_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < kMaxDevices) configured[dev] = true;
   }
-  // The tensor-core tile images follow the FFMA layout in the packed buffer.
-  const float* image = packed + stages * kpad * rvqtc::kDim;
-  rvqtc::Args args{x, books, image, code_norm, stats, codes, recon, residual_out, rows,
-                   static_cast<int>(stages), static_cast<int>(k), static_cast<int>(kpad),
-                   rows_per_cta};
   rvqtc::rvq_tc_kernel<<<static_cast<unsigned>(grid), rvqtc::kThreads, smem, as_stream(stream)>>>(args);
   return launch_status(name);
+}
+
+extern "C" int moss_rvq_encode(const float* x, int64_t rows, int64_t d, const float* books,
+                               const float* packed, const float* code_norm, const float* stats,
+                               int64_t stages, int64_t k, int32_t* codes, float* recon,
+                               float* residual_out, void* stream) {
+  return moss_rvq_encode_kernel(x, rows, d, books, packed, code_norm, stats, stages, k, codes,
+                                recon, residual_out, MOSS_RVQ_AUTO, stream);
 }

@@ -75,6 +75,8 @@ _SIGNATURES = {
     "moss_rvq_packed_floats": (_i64, [_i64, _i64, _i64]),
     "moss_rvq_prepare_codebooks": (_i, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_rvq_encode": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "moss_rvq_encode_kernel": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp,
+                                    _i, _vp]),
     "moss_rvq_encode_static": (_i, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
     "moss_rvq_encode_ffma": (_i, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp,
                                   _vp]),

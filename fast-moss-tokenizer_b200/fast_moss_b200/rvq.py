@@ -4,10 +4,15 @@ The stage loop of the upstream quantizer that the reference calls at
 fast_moss/v2_codec.py:45, every stage selecting with the rule of
 fast_moss/quantizer.py:33-39 (distance = (norm - dot) + code_norm, first
 NaN, else first minimum).  The whole loop runs in ONE kernel with the
-residual kept on chip across stages.  Two kernels implement it with
+residual kept on chip across stages.  Two algorithms implement it with
 identical results: "tensor_core" screens the codes with TF32 tcgen05 dot
 products under a proven error margin and resolves the survivors exactly
-(the default), "ffma" evaluates every distance with FP32 FMAs.  Numerics
+(the default), "ffma" evaluates every distance with FP32 FMAs.  The
+tensor-core algorithm has two kernels: one CTA per row block over the whole
+codebook ("tensor_core_single", what "tensor_core" runs), and a CTA pair per
+row block, each CTA screening half of every codebook and the two exchanging
+one key per row and stage ("tensor_core_pair", for codebooks of more than
+256 codes and rows within one wave of pairs).  Numerics
 (the documented order the CPU oracle also follows): norm and code norms
 are sequential FMAs over the
 dimensions in ascending order starting from +0, dot_j = the same over
@@ -17,6 +22,10 @@ dimensions in ascending order starting from +0, dot_j = the same over
 import torch
 
 from . import _lib
+
+
+# algorithm -> tensor-core kernel selector of moss_rvq_encode_kernel (None: FFMA)
+_KERNELS = {"tensor_core": 0, "tensor_core_single": 1, "tensor_core_pair": 2, "ffma": None}
 
 
 class ResidualVectorQuantizer:
@@ -57,13 +66,18 @@ class ResidualVectorQuantizer:
 
         Output buffers may be passed in (e.g. static buffers of a CUDA graph);
         `residual` (optional) receives the final residual.  `algorithm` picks
-        the kernel ("tensor_core" or "ffma"; both give the same bits); books
-        with more than 4096 codes always use "ffma".
+        the kernel ("tensor_core", "tensor_core_pair", "tensor_core_single" or
+        "ffma"; all give the same bits); books with more than 4096 codes use
+        "ffma" under "tensor_core".  "tensor_core_pair" raises UnsupportedError
+        where the pair kernel does not apply.
         """
-        if algorithm not in ("tensor_core", "ffma"):
+        if algorithm not in _KERNELS:
             raise ValueError(f"Unknown algorithm {algorithm!r}")
-        entry = "moss_rvq_encode" if algorithm == "tensor_core" and self.codes <= 4096 \
-            else "moss_rvq_encode_ffma"
+        kernel = _KERNELS[algorithm]
+        if kernel is None or (algorithm == "tensor_core" and self.codes > 4096):
+            entry, extra = "moss_rvq_encode_ffma", ()
+        else:
+            entry, extra = "moss_rvq_encode_kernel", (kernel,)
         self._check_rows(x)
         x = x.contiguous()
         n = x.shape[0]
@@ -81,7 +95,7 @@ class ResidualVectorQuantizer:
                 entry, x.data_ptr(), n, self.dim, self.books.data_ptr(),
                 self.packed.data_ptr(), self.code_norm.data_ptr(), self.stats.data_ptr(),
                 self.stages, self.codes, codes.data_ptr(), recon.data_ptr(),
-                residual.data_ptr() if residual is not None else None,
+                residual.data_ptr() if residual is not None else None, *extra,
                 torch.cuda.current_stream(dev).cuda_stream)
         return codes, recon
 

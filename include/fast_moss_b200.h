@@ -59,6 +59,10 @@ extern "C" {
 #define MOSS_LINEAR_BIAS 0      /* y = x w^T + bias                       */
 #define MOSS_LINEAR_BIAS_ACT 1  /* y = act(bf16(x w^T) + bias), ungated   */
 
+#define MOSS_RVQ_AUTO 0    /* tensor-core quantizer: the faster kernel (SINGLE)         */
+#define MOSS_RVQ_SINGLE 1  /* one CTA per row block, the whole codebook each         */
+#define MOSS_RVQ_PAIR 2    /* a CTA pair per row block, each half of the codebook     */
+
 /* Library ABI version (major*100 + minor). */
 MOSS_API int moss_version(void);
 
@@ -388,6 +392,18 @@ MOSS_API int moss_rvq_encode(const float* x, int64_t rows, int64_t d,
                     const float* code_norm, const float* stats,
                     int64_t stages, int64_t k, int32_t* codes, float* recon,
                     float* residual_out, void* stream);
+/* moss_rvq_encode with the tensor-core kernel chosen (same results): MOSS_RVQ_AUTO
+ * (what moss_rvq_encode does: the single-CTA kernel, measured faster at
+ * 8192 rows x 32 stages x 1024 codes), MOSS_RVQ_SINGLE (one CTA holds its rows for the
+ * whole codebook), MOSS_RVQ_PAIR (two CTAs of a cluster hold the same <= 128
+ * rows and each screens half of every codebook; needs k > 256 and rows within
+ * one wave of pairs, else MOSS_ERR_UNSUPPORTED).  Same reference row as
+ * moss_rvq_encode (fast_moss/v2_codec.py:45 with fast_moss/quantizer.py:33-39). */
+MOSS_API int moss_rvq_encode_kernel(const float* x, int64_t rows, int64_t d,
+                    const float* books, const float* packed,
+                    const float* code_norm, const float* stats,
+                    int64_t stages, int64_t k, int32_t* codes, float* recon,
+                    float* residual_out, int kernel, void* stream);
 MOSS_API int moss_rvq_encode_ffma(const float* x, int64_t rows, int64_t d,
                     const float* books, const float* packed,
                     const float* code_norm, const float* stats,

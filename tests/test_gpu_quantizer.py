@@ -95,12 +95,25 @@ def rvq_case(rows, k, stages, seed, device):
     return x, books
 
 
-ALGOS = ["tensor_core", "ffma"]
+ALGOS = ["tensor_core_pair", "tensor_core_single", "ffma"]
+
+
+def pair_applies(rows, k):
+    """The pair kernel takes codebooks of two or more 256-code tiles and at
+    most 128 rows per pair; every B200 fits at least 64 pairs (8192 rows)."""
+    return -(-k // 256) >= 2 and rows <= 8192
 
 
 def run_rvq(moss, x, books, device, algorithm="tensor_core"):
+    from fast_moss_b200 import _lib
     q = moss.ResidualVectorQuantizer(dev(books, device))
     res = torch.empty(x.shape, device=device)
+    if algorithm == "tensor_core_pair" and not pair_applies(x.shape[0], books.shape[1]):
+        try:
+            q.encode(dev(x, device), residual=res, algorithm=algorithm)
+        except _lib.UnsupportedError:
+            pytest.skip("the pair kernel does not cover this shape")
+        # it covered it (more pairs fit than assumed): check the results below
     codes, recon = q.encode(dev(x, device), residual=res, algorithm=algorithm)
     torch.cuda.synchronize()
     from fast_moss_b200 import _lib
@@ -134,7 +147,12 @@ def test_rvq_config2_bit_exact(moss, cuda_device, algorithm):
                                            (300, 37, 5), (56, 2049, 2), (129, 4096, 2),
                                            (9000, 512, 3),   # 61 rows per CTA, last CTA short
                                            (9472, 300, 2),   # 148 x 64: exactly 64 per CTA
-                                           (10001, 300, 2)])  # > 148 x 64 rows: 128 per CTA
+                                           (10001, 300, 2),  # > 148 x 64 rows: 128 per CTA
+                                           # pair splits: 1 + 1 tiles with one real code on
+                                           # rank 1, 2 + 1, 3 + 2 tiles; rows not a multiple
+                                           # of the pair count; one row per pair
+                                           (1000, 257, 3), (8191, 768, 2), (777, 1280, 3),
+                                           (74, 1024, 2), (8192, 4096, 1)])
 def test_rvq_ragged_shapes(moss, cuda_device, rows, k, stages, algorithm):
     x, books = rvq_case(rows, k, stages, rows + k, cuda_device)
     q, codes, recon, res = run_rvq(moss, x, books, cuda_device, algorithm)
