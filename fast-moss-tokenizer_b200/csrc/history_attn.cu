@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
 
 namespace moss {
 namespace hattn {
@@ -244,7 +245,19 @@ __global__ void __launch_bounds__(kThreads, 3) history_attn_kernel(const Args a)
 // requested as soon as the current scores are formed and its V as soon as
 // the current P.V is done, so HBM streams the next item while this one
 // computes.  The next item's queries, slot positions and position are
-// loaded into registers while the current one computes.  n <= 256 (one
+// loaded into registers while the current one computes.
+//
+// Scores on the tensor cores: K as it lands (128-byte-swizzled rows of 64
+// bf16: the K-major operand layout) is the A operand, the item's queries
+// (bf16, padded to 16 rows of zeros, same layout, 2 KB) the B operand, and
+// one thread issues per 128-key tile four tcgen05.mma kind::f16 (M = 128
+// keys, N = 16 queries, K = 16 dims each) into 16 TMEM columns; thread tid
+// < 128 then reads the scores of keys tid and tid + 128 (its TMEM lane in
+// the two tiles) with one tcgen05.ld each.  The products of bf16 values are
+// exact in FP32 and the tensor cores sum them in FP32, so the scores differ
+// from a sequential FMA chain only by FP32 rounding (well inside the
+// kernel's bound against float64 attention); this replaces 512 FMAs and 80
+// shared-memory loads per scoring thread and item.  n <= 256 (one
 // TMA box).  Every wait is bounded (~2 s, MOSS_ERR_TIMEOUT).
 constexpr int kStreamMaxKeys = 256;
 
@@ -254,14 +267,51 @@ struct StreamArgs {
   int64_t items;
 };
 
+constexpr int kScoreRows = 16;  // MMA N: the queries, padded with zero rows
+
 __host__ __device__ constexpr size_t stream_smem(int t, int n) {
-  // K (whole 1024-byte swizzle atoms) | V | weights [n][4 or 8] (key-major,
+  // K (whole 1024-byte swizzle atoms) | the queries as the MMA's B operand
+  // (16 rows x 128 bytes, swizzled) | V | weights [n][4 or 8] (key-major,
   // so P.V reads one key's weights of every query with one vector load) |
-  // partial sums [warps][t][64] | q [t][64] | reduction slots | 2 mbarriers
-  return static_cast<size_t>((n + 7) / 8) * 1024 + static_cast<size_t>(n) * kDim * 2 +
+  // partial sums [warps][t][64] | reduction slots | 3 mbarriers and the TMEM
+  // address
+  return static_cast<size_t>((n + 7) / 8) * 1024 + kScoreRows * 128 +
+         static_cast<size_t>(n) * kDim * 2 +
          static_cast<size_t>(n) * (t <= 4 ? 4 : 8) * 4 + static_cast<size_t>(kWarps) * t * kDim * 4 +
-         static_cast<size_t>(t) * kDim * 4 + static_cast<size_t>(kWarps) * kMaxQueries * 4 + 16 +
-         1024;
+         static_cast<size_t>(kWarps) * kMaxQueries * 4 + 32 + 1024;
+}
+
+// K-major operand with the 128-byte swizzle (the TMA layout): 128-byte rows,
+// 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// kind::f16, D f32, A and B bf16 K-major, M = 128, N = 16.
+constexpr uint32_t kScoreIdesc =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((kScoreRows >> 3) << 17) | ((128u >> 4) << 24);
+__device__ __forceinline__ void mma_score(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kScoreIdesc), "r"(acc)
+      : "memory");
+}
+// 8 accumulator columns of this thread's TMEM lane (whole warp), then wait.
+__device__ __forceinline__ void tmem_load8(uint32_t taddr, uint32_t (&r)[8]) {
+  __syncwarp();
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7])
+               :
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* map, int row,
@@ -283,24 +333,34 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
   unsigned char* ks = smem_raw + ((1024u - (static_cast<uint32_t>(
                                                  __cvta_generic_to_shared(smem_raw)) & 1023u)) &
                                   1023u);
-  unsigned char* vs = ks + static_cast<size_t>((n + 7) / 8) * 1024;
+  unsigned char* qimg = ks + static_cast<size_t>((n + 7) / 8) * 1024;  // [16][128 B], swizzled
+  unsigned char* vs = qimg + kScoreRows * 128;
   float* ps = reinterpret_cast<float*>(vs + static_cast<size_t>(n) * kDim * 2);  // [n][TP]
   float* part = ps + n * TP;                                                     // [warps][T][64]
-  float* qs = part + kWarps * T * kDim;                                          // [T][64]
-  float* red = qs + T * kDim;                                                    // [warps][8]
+  float* red = part + kWarps * T * kDim;                                         // [warps][8]
   unsigned long long* kfull = reinterpret_cast<unsigned long long*>(red + kWarps * kMaxQueries);
   unsigned long long* vfull = kfull + 1;
+  unsigned long long* sfull = kfull + 2;  // the scores are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(kfull + 3);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t bytes = static_cast<uint32_t>(n) * kDim * 2;
+  int64_t item = blockIdx.x;
+  if (item >= sa.items) return;  // uniform over the CTA
 
   if (tid == 0) {
     pipe::mbar_init(kfull, 1);
     pipe::mbar_init(vfull, 1);
+    pipe::mbar_init(sfull, 1);
     pipe::fence_mbar_init();
   }
+  // the padding rows of the query operand stay zero
+  for (int i = tid; i < kScoreRows * 128 / 16; i += kThreads)
+    reinterpret_cast<uint4*>(qimg)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (warp == 0) tc::alloc(tmem_slot, 32);  // two 128-key tiles x 16 columns
+  tc::fence_before();
   __syncthreads();
-  int64_t item = blockIdx.x;
-  if (item >= sa.items) return;  // uniform over the CTA
+  tc::fence_after();
+  const uint32_t tmem = *tmem_slot;
   auto issue_k = [&](int64_t it) {
     pipe::mbar_arrive_expect_tx(kfull, bytes);
     tma_load_rows(pipe::smem_u32(ks), &sa.k_map, static_cast<int>(it * n), kfull);
@@ -341,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
   int64_t held[kKeysPerThread];
   int64_t p0;
   load_meta(item, qv, held, p0);
-  int issued_k = 1, issued_v = 1, done_k = 0, done_v = 0;
+  int issued_k = 1, issued_v = 1, done_k = 0, done_v = 0, issued_s = 0, done_s = 0;
   for (int i = 0;; ++i) {
     const int64_t s = item / a.h;
     const int hh = static_cast<int>(item - s * a.h);
@@ -350,11 +410,34 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
 #pragma unroll
     for (int c = 0; c < QC; ++c) {
       const int q = tid + c * kThreads;
-      if (q < T * kDim) qs[q] = qv[c];
+      if (q < T * kDim) {
+        // the MMA's B operand: row t, dim d (bf16, exact: qv holds bf16 values)
+        const int tq = q / kDim, d = q - tq * kDim;
+        *reinterpret_cast<uint16_t*>(qimg + (tq & 7) * 128 + ((((d >> 3) ^ (tq & 7)) << 4)) +
+                                     (d & 7) * 2) = f32_to_bf16_bits(qv[c]);
+      }
     }
+    tc::fence_async_shared();  // the query operand is visible to the tensor cores
     const int kok = pipe::mbar_wait(kfull, i & 1) ? 1 : 0;
     done_k = i + kok;  // loads this thread saw land
     if (__syncthreads_or(!kok)) break;  // K and the queries are visible to all
+    if (tid == 0) {
+      // scores: per 128-key tile 4 MMAs of K = 16 dims into 16 columns
+      tc::fence_after();
+      const uint32_t kb = pipe::smem_u32(ks), qb = pipe::smem_u32(qimg);
+      for (int tile = 0; tile * 128 < n; ++tile) {
+#pragma unroll
+        for (int kk = 0; kk < kDim / 16; ++kk)
+          mma_score(tmem + static_cast<uint32_t>(tile * kScoreRows),
+                    sw128_desc(kb + static_cast<uint32_t>(tile) * 16384u + kk * 32u),
+                    sw128_desc(qb + kk * 32u), kk > 0 ? 1u : 0u);
+      }
+      tc::commit(sfull);
+      ++issued_s;
+    }
+    const int sok = pipe::mbar_wait(sfull, i & 1) ? 1 : 0;
+    done_s = i + sok;
+    tc::fence_after();
     // ---- scores: thread tid < 128 takes keys tid and tid + 128; each key's
     // dot products are summed in the same order as history_attn_kernel's
     float sc[kKeysPerThread][T];
@@ -365,29 +448,16 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     if (tid < kPair) {
       const int j0 = tid, j1 = tid + kPair;
       const bool v0 = j0 < n, v1 = j1 < n;  // rows past n are never read
+      // this thread's TMEM lane holds key j0 in tile 0 and key j1 in tile 1
+      const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+      uint32_t r0[8], r1[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      tmem_load8(lane_addr, r0);
+      if (n > kPair) tmem_load8(lane_addr + kScoreRows, r1);
       float acc0[T], acc1[T];
 #pragma unroll
-      for (int t = 0; t < T; ++t) acc0[t] = acc1[t] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float k0[8], k1[8];
-        const uint4 r0 = v0 ? *reinterpret_cast<const uint4*>(ks + j0 * 128 + ((c ^ (j0 & 7)) << 4))
-                            : make_uint4(0u, 0u, 0u, 0u);
-        const uint4 r1 = v1 ? *reinterpret_cast<const uint4*>(ks + j1 * 128 + ((c ^ (j1 & 7)) << 4))
-                            : make_uint4(0u, 0u, 0u, 0u);
-        unpack_bf16x8(r0, k0);
-        unpack_bf16x8(r1, k1);
-#pragma unroll
-        for (int t = 0; t < T; ++t) {
-          const float4 qa = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8);
-          const float4 qb = *reinterpret_cast<const float4*>(qs + t * kDim + c * 8 + 4);
-          const float qq[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            acc0[t] = __fmaf_rn(qq[e], k0[e], acc0[t]);
-            acc1[t] = __fmaf_rn(qq[e], k1[e], acc1[t]);
-          }
-        }
+      for (int t = 0; t < T; ++t) {
+        acc0[t] = __uint_as_float(r0[t]);
+        acc1[t] = __uint_as_float(r1[t]);
       }
 #pragma unroll
       for (int t = 0; t < T; ++t) {
@@ -408,7 +478,8 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
       for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
       if (lane == 0) red[warp * kMaxQueries + t] = v;
     }
-    __syncthreads();  // every read of K is done: the next item's K may come in
+    tc::fence_before();
+    if (__syncthreads_or(!sok)) break;  // every read of K and of the scores is done
     if (tid == 0 && more) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue_k(next);
@@ -508,13 +579,19 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
 #pragma unroll
     for (int m = 0; m < kKeysPerThread; ++m) held[m] = heldn[m];
     p0 = p0n;
-    __syncthreads();  // `part`, `ps` and `qs` are read before they are rewritten
+    __syncthreads();  // `part` and `ps` are read before they are rewritten
   }
   // after a timeout: the copies still in flight land before the CTA retires
   if (tid == 0) {
     for (int i = done_k; i < issued_k; ++i) pipe::mbar_wait(kfull, i & 1);
     for (int i = done_v; i < issued_v; ++i) pipe::mbar_wait(vfull, i & 1);
+    // and the score MMAs still in flight finish before the TMEM is freed
+    for (int i = done_s; i < issued_s; ++i) pipe::mbar_wait(sfull, i & 1);
   }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  if (warp == 0) tc::dealloc(tmem, 32);
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,

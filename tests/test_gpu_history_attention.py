@@ -63,6 +63,10 @@ def _reference(q, k, v, slot_pos, pos, context, scale):
     (2, 3, 8, 512, 500),
     (5, 2, 3, 257, 100),     # keys beyond the first 256 threads
     (64, 20, 4, 253, 250),   # 64 batched streams
+    # the persistent kernel (at least two items per resident CTA), its tensor-
+    # core scores over one or two 128-key tiles, 1 to 8 queries
+    (16, 20, 1, 253, 250), (40, 8, 2, 100, 60), (20, 16, 3, 200, 150),
+    (16, 20, 8, 256, 250),
 ])
 def test_history_attention_matches_float64(moss, cuda_device, streams, heads, tokens, slots,
                                            context):
