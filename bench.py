@@ -716,7 +716,7 @@ def _attention_kernel_line(torch, dev, cfg):
     the output."""
     from torch.nn.attention import SDPBackend, sdpa_kernel
     from fast_moss_b200.transformer import StreamHistory, additive_mask
-    from fast_moss_b200.v2_pointwise import history_attention
+    from fast_moss_b200.v2_pointwise import history_attention, history_attention_qkv
 
     h, t, dh = cfg.heads, cfg.chunk_tokens, cfg.head_dim
     res = {}
@@ -746,8 +746,26 @@ def _attention_kernel_line(torch, dev, cfg):
         ts = time_launches(torch, sdpa, layers, launches=48, replays=5)
         n = cfg.history_slots
         nbytes = streams * (h * n * dh * 2 * 2 + 2 * h * t * dh * 2 + n * 8 + 8)
-        res[f"streams_{streams}"] = {"us_owned": to * 1e6, "us_sdpa": ts * 1e6,
-                                     "owned_gbs": nbytes / to / 1e9, "bytes": nbytes}
+        line = {"us_owned": to * 1e6, "us_sdpa": ts * 1e6, "owned_gbs": nbytes / to / 1e9,
+                "bytes": nbytes}
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        if streams * h >= 2 * sms:
+            # the form the stack runs at this size: the rotary and the ring
+            # update inside the attention kernel (moss_history_attention_qkv)
+            qkv = torch.randn(streams, t, 3 * h * dh, device=dev, generator=g).to(torch.bfloat16)
+            slots = torch.remainder(offset[:, None] + torch.arange(t, device=dev), n)
+
+            def fused(layer, _handle):
+                history_attention_qkv(qkv, h, offset, cfg.max_period, slots, layer[0], layer[1],
+                                      hist.slot_pos, cfg.context)
+
+            tf = time_launches(torch, fused, layers, launches=48, replays=5)
+            # rings read, qkv read, the chunk's keys and values written, out
+            fbytes = streams * (h * n * dh * 2 * 2 + 3 * h * t * dh * 2 + 2 * h * t * dh * 2 +
+                                h * t * dh * 2 + n * 8 + 8 + t * 8)
+            line["fused_rotary"] = {"us": tf * 1e6, "gbs": fbytes / tf / 1e9, "bytes": fbytes,
+                                    "us_rope_kv_then_attention_kernel_only": to * 1e6}
+        res[f"streams_{streams}"] = line
         del hist, layers
     return res
 
@@ -936,11 +954,8 @@ def headline(torch, dist, dev, rank, world, args):
             sched.input.copy_(feats[c])
             out_dev[c].copy_(sched.advance())
 
-    def step_host():  # pinned host buffers, copies inside the step
-        sched.reset()
-        for c in range(CHUNKS):
-            sched.input.copy_(host_in[c], non_blocking=True)
-            host_out[c].copy_(sched.advance(), non_blocking=True)
+    def step_host():  # pinned host buffers, copies inside the step (overlapped with replays)
+        sched.run_host(host_in, host_out)
 
     def timed(step, k):
         for _ in range(max(args.warmup, 3)):
@@ -985,6 +1000,7 @@ def step_roofline(torch, dev, cfg, peaks, ms_per_chunk):
     history attention, measured at the step's shapes), and the whole
     chunk's algorithmic HBM bytes against the chunk time."""
     att = _attention_kernel_line(torch, dev, cfg)["streams_64"]
+    fused = att["fused_rotary"]
     hbm = float(peaks["hbm_gbs"])
     d, f, h = cfg.dim, cfg.ffn, cfg.heads
     weight_bytes = cfg.layers * (3 * d * d + d * d + 2 * d * f) * 2
@@ -992,12 +1008,13 @@ def step_roofline(torch, dev, cfg, peaks, ms_per_chunk):
     chunk_bytes = weight_bytes + ring_bytes
     return {
         "bound": "hbm",
-        "kernel": "history_attn_stream_kernel (moss_history_attention: 64 streams x 20 heads, "
-                  "4 queries over 253 ring slots of 64, bf16)",
-        "achieved": att["owned_gbs"], "peak": hbm, "unit": "GB/s", "frac": att["owned_gbs"] / hbm,
-        "traffic": profile_traffic("history_attn_stream_kernel"),
-        "bytes_per_launch": att["bytes"], "us_per_launch": att["us_owned"],
-        "us_per_launch_sdpa": att["us_sdpa"],
+        "kernel": "history_attn_stream_kernel<4, true> (moss_history_attention_qkv: rotary, ring "
+                  "update and attention, 64 streams x 20 heads, 4 queries over 253 ring slots "
+                  "of 64, bf16)",
+        "achieved": fused["gbs"], "peak": hbm, "unit": "GB/s", "frac": fused["gbs"] / hbm,
+        "traffic": profile_traffic("history_attn_qkv_stream_kernel"),
+        "bytes_per_launch": fused["bytes"], "us_per_launch": fused["us"],
+        "us_per_launch_attention_alone": att["us_owned"], "us_per_launch_sdpa": att["us_sdpa"],
         "step": {"what": "one chunk of all 64 streams: bf16 weights of 24 layers + every layer's "
                          "key/value ring read once",
                  "bytes_per_chunk": chunk_bytes, "weight_bytes": weight_bytes,
@@ -1094,8 +1111,9 @@ def run_b200(args):
             "unit": "audio-sec/sec",
             "h2d_bytes_per_step": details["h2d_bytes_per_chunk"] * CHUNKS,
             "d2h_bytes_per_step": details["d2h_bytes_per_chunk"] * CHUNKS,
-            "api": "BatchedStreams: each chunk copied from pinned host memory into the graph "
-                   "input, replayed, output copied back to pinned host memory",
+            "api": "BatchedStreams.run_host: each chunk copied from pinned host memory to the "
+                   "device and its output back on copy streams, overlapped with the "
+                   "neighbouring chunks' graph replays",
         },
         "gpu_launches": args.steps * CHUNKS * details["native_launches_per_chunk"],
         "clocks": clocks,

@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "pipeline.cuh"
+#include "rotary.cuh"
 #include "tcgen05.cuh"
 
 namespace moss {
@@ -265,6 +266,14 @@ struct StreamArgs {
   CUtensorMap k_map;  // k_cache as [S * H * N, 64] bf16, box {64, n}, 128-byte swizzle
   Args a;
   int64_t items;
+  // With the rotary fused in (moss_history_attention_qkv): the qkv
+  // projection's output [S * T, 3 * H * 64] bf16 (row s * T + t: q, k, v of
+  // every head), the ring slot of every token [S, T], the rotary frequency
+  // coefficient; k_cache and v_cache (a.k, a.v) receive the chunk's keys and
+  // values.
+  const uint16_t* qkv;
+  const int64_t* slots;
+  float coef;
 };
 
 constexpr int kScoreRows = 16;  // MMA N: the queries, padded with zero rows
@@ -323,7 +332,7 @@ __device__ __forceinline__ void tma_load_rows(uint32_t dst, const CUtensorMap* m
       : "memory");
 }
 
-template <int T>
+template <int T, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     const __grid_constant__ StreamArgs sa) {
   extern __shared__ unsigned char smem_raw[];
@@ -396,30 +405,100 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     }
     p0 = a.pos[s];
   };
+  // the slot positions and the position only (the queries come from qkv)
+  auto load_meta_keys = [&](int64_t it, int64_t (&held)[kKeysPerThread], int64_t& p0) {
+    const int64_t s = it / a.h;
+#pragma unroll
+    for (int m = 0; m < kKeysPerThread; ++m) {
+      const int j = key_of(m);
+      held[m] = j < n ? a.slot_pos[s * n + j] : -1;
+    }
+    p0 = a.pos[s];
+  };
+  // Fused rotary: thread tid < 32 T owns dims 2p, 2p + 1 (p = tid % 32) of
+  // token tid / 32: it reads that pair of q, k and v from the projection's
+  // output and the token's ring slot.
+  constexpr int kPairThreads = 32 * T;
+  auto load_pairs = [&](int64_t it, uint32_t (&raw)[3], int64_t& slot) {
+    if (FUSED && tid < kPairThreads) {
+      const int64_t s = it / a.h;
+      const int hh = static_cast<int>(it - s * a.h);
+      const int tq = tid >> 5, p = tid & 31;
+      const uint32_t* row =
+          reinterpret_cast<const uint32_t*>(sa.qkv + (s * T + tq) * (3 * a.h * kDim));
+      raw[0] = row[hh * (kDim / 2) + p];
+      raw[1] = row[(a.h + hh) * (kDim / 2) + p];
+      raw[2] = row[(2 * a.h + hh) * (kDim / 2) + p];
+      slot = sa.slots[s * T + tq];
+    }
+  };
   constexpr int QC = (T * kDim + kThreads - 1) / kThreads;
   float qv[QC];
   int64_t held[kKeysPerThread];
   int64_t p0;
-  load_meta(item, qv, held, p0);
+  uint32_t raw[3] = {0u, 0u, 0u};
+  int64_t slot = 0;
+  if (!FUSED) load_meta(item, qv, held, p0);
+  if (FUSED) {
+    load_meta_keys(item, held, p0);
+    load_pairs(item, raw, slot);
+  }
   int issued_k = 1, issued_v = 1, done_k = 0, done_v = 0, issued_s = 0, done_s = 0;
   for (int i = 0;; ++i) {
     const int64_t s = item / a.h;
     const int hh = static_cast<int>(item - s * a.h);
     const int64_t next = item + gridDim.x;
     const bool more = next < sa.items;
+    uint32_t kbits = 0u;  // fused: this thread's rotated key pair (bf16 x 2)
+    if constexpr (FUSED) {
+      if (tid < kPairThreads) {
+        // moss_rope_kv's arithmetic: phase = exp(p * coef) * (pos + t),
+        // each product and sum rounded, one bf16 rounding per output
+        const int tq = tid >> 5, p = tid & 31;
+        const float ts = __fadd_rn(static_cast<float>(p0), static_cast<float>(tq));
+        const float phase = __fmul_rn(expf(__fmul_rn(static_cast<float>(p), sa.coef)), ts);
+        const float c = cosf(phase), sn = sinf(phase);
+        float o0, o1;
+        rotate_pair(__uint_as_float(raw[0] << 16), __uint_as_float(raw[0] & 0xffff0000u), c, sn,
+                    o0, o1);
+        *reinterpret_cast<uint32_t*>(qimg + (tq & 7) * 128 + ((((2 * p) >> 3) ^ (tq & 7)) << 4) +
+                                     ((2 * p) & 7) * 2) = pack_bf16x2(o0, o1);
+        rotate_pair(__uint_as_float(raw[1] << 16), __uint_as_float(raw[1] & 0xffff0000u), c, sn,
+                    o0, o1);
+        kbits = pack_bf16x2(o0, o1);
+      }
+    } else {
 #pragma unroll
-    for (int c = 0; c < QC; ++c) {
-      const int q = tid + c * kThreads;
-      if (q < T * kDim) {
-        // the MMA's B operand: row t, dim d (bf16, exact: qv holds bf16 values)
-        const int tq = q / kDim, d = q - tq * kDim;
-        *reinterpret_cast<uint16_t*>(qimg + (tq & 7) * 128 + ((((d >> 3) ^ (tq & 7)) << 4)) +
-                                     (d & 7) * 2) = f32_to_bf16_bits(qv[c]);
+      for (int c = 0; c < QC; ++c) {
+        const int q = tid + c * kThreads;
+        if (q < T * kDim) {
+          // the MMA's B operand: row t, dim d (bf16, exact: qv holds bf16 values)
+          const int tq = q / kDim, d = q - tq * kDim;
+          *reinterpret_cast<uint16_t*>(qimg + (tq & 7) * 128 + ((((d >> 3) ^ (tq & 7)) << 4)) +
+                                       (d & 7) * 2) = f32_to_bf16_bits(qv[c]);
+        }
       }
     }
     tc::fence_async_shared();  // the query operand is visible to the tensor cores
     const int kok = pipe::mbar_wait(kfull, i & 1) ? 1 : 0;
     done_k = i + kok;  // loads this thread saw land
+    if constexpr (FUSED) {
+      // the chunk's rotated keys: into the ring for the chunks after this
+      // one, and over the (stale) rows of their slots in the landed K tile
+      if (kok && tid < kPairThreads) {
+        const int p = tid & 31;
+        if (slot >= 0 && slot < n) {
+          *reinterpret_cast<uint32_t*>(ks + (slot >> 3) * 1024 + (slot & 7) * 128 +
+                                       ((((2 * p) >> 3) ^ (static_cast<int>(slot) & 7)) << 4) +
+                                       ((2 * p) & 7) * 2) = kbits;
+          reinterpret_cast<uint32_t*>(const_cast<uint16_t*>(a.k))[(item * n + slot) * (kDim / 2) + p] =
+              kbits;
+        } else {
+          record_device_error(MOSS_ERR_VALUE);
+        }
+      }
+      tc::fence_async_shared();  // the patched rows are visible to the tensor cores
+    }
     if (__syncthreads_or(!kok)) break;  // K and the queries are visible to all
     if (tid == 0) {
       // scores: per 128-key tile 4 MMAs of K = 16 dims into 16 columns
@@ -525,9 +604,27 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     float qn[QC];
     int64_t heldn[kKeysPerThread];
     int64_t p0n = 0;
-    if (more) load_meta(next, qn, heldn, p0n);
+    uint32_t rawn[3] = {0u, 0u, 0u};
+    int64_t slotn = 0;
+    if (more) {
+      if constexpr (FUSED) {
+        load_meta_keys(next, heldn, p0n);
+        load_pairs(next, rawn, slotn);
+      } else {
+        load_meta(next, qn, heldn, p0n);
+      }
+    }
     const int vok = pipe::mbar_wait(vfull, i & 1) ? 1 : 0;
     done_v = i + vok;
+    if constexpr (FUSED) {
+      // the chunk's values: into the ring and over their slots' rows of V
+      if (vok && tid < kPairThreads && slot >= 0 && slot < n) {
+        const int p = tid & 31;
+        *reinterpret_cast<uint32_t*>(vs + slot * 128 + p * 4) = raw[2];
+        reinterpret_cast<uint32_t*>(const_cast<uint16_t*>(a.v))[(item * n + slot) * (kDim / 2) + p] =
+            raw[2];
+      }
+    }
     if (__syncthreads_or(!vok)) break;  // V, the weights and the sums are visible
 #pragma unroll
     for (int t = 0; t < T; ++t) {
@@ -574,8 +671,14 @@ __global__ void __launch_bounds__(kThreads, 2) history_attn_stream_kernel(
     }
     if (!more) break;
     item = next;
+    if constexpr (FUSED) {
 #pragma unroll
-    for (int c = 0; c < QC; ++c) qv[c] = qn[c];
+      for (int e = 0; e < 3; ++e) raw[e] = rawn[e];
+      slot = slotn;
+    } else {
+#pragma unroll
+      for (int c = 0; c < QC; ++c) qv[c] = qn[c];
+    }
 #pragma unroll
     for (int m = 0; m < kKeysPerThread; ++m) held[m] = heldn[m];
     p0 = p0n;
@@ -621,6 +724,29 @@ bool encode_ring(CUtensorMap* map, const void* base, int64_t rows, int n) {
          CUDA_SUCCESS;
 }
 
+// Launches the persistent kernel over its one wave of CTAs (two per SM).
+template <bool FUSED>
+int launch_stream(const StreamArgs& sa, int t, int n, cudaStream_t st, const char* name) {
+  const size_t sh = stream_smem(t, n);
+  const size_t sh_max = stream_smem(kMaxQueries, kStreamMaxKeys);
+  const int64_t sms = sm_count();
+  const unsigned sgrid = static_cast<unsigned>(2 * sms < sa.items ? 2 * sms : sa.items);
+#define MOSS_HATTN_STREAM(T)                                                            \
+  case T: {                                                                             \
+    static bool attr_done[kMaxDevices] = {};                                            \
+    allow_dynamic_smem(history_attn_stream_kernel<T, FUSED>, sh_max, attr_done);        \
+    history_attn_stream_kernel<T, FUSED><<<sgrid, kThreads, sh, st>>>(sa);              \
+    break;                                                                              \
+  }
+  switch (t) {
+    MOSS_HATTN_STREAM(1) MOSS_HATTN_STREAM(2) MOSS_HATTN_STREAM(3) MOSS_HATTN_STREAM(4)
+    MOSS_HATTN_STREAM(5) MOSS_HATTN_STREAM(6) MOSS_HATTN_STREAM(7) MOSS_HATTN_STREAM(8)
+    default: break;
+  }
+#undef MOSS_HATTN_STREAM
+  return launch_status(name);
+}
+
 }  // namespace hattn
 }  // namespace moss
 
@@ -652,31 +778,12 @@ extern "C" int moss_history_attention(const void* q, const void* k_cache, const 
   const int64_t items = s * h;
   const int64_t sms = sm_count();
   if (n <= kStreamMaxKeys && items >= 2 * sms && items * n < 0x7fffffffLL) {
-    StreamArgs sa;
+    StreamArgs sa{};
     if (!encode_ring(&sa.k_map, k_cache, items * n, static_cast<int>(n)))
       return fail(MOSS_ERR_CUDA, "%s: tensor map encoding failed", name);
-    sa.a = Args{static_cast<const uint16_t*>(q), static_cast<const uint16_t*>(k_cache),
-                static_cast<const uint16_t*>(v_cache), slot_pos, pos,
-                static_cast<uint16_t*>(out), context, scale, static_cast<int>(h),
-                static_cast<int>(t), static_cast<int>(n)};
+    sa.a = a;
     sa.items = items;
-    const size_t sh = stream_smem(static_cast<int>(t), static_cast<int>(n));
-    const size_t sh_max = stream_smem(kMaxQueries, kStreamMaxKeys);
-    const unsigned sgrid = static_cast<unsigned>(2 * sms < items ? 2 * sms : items);
-#define MOSS_HATTN_STREAM(T)                                                            \
-  case T: {                                                                             \
-    static bool attr_done[kMaxDevices] = {};                                            \
-    allow_dynamic_smem(history_attn_stream_kernel<T>, sh_max, attr_done);               \
-    history_attn_stream_kernel<T><<<sgrid, kThreads, sh, st>>>(sa);                     \
-    break;                                                                              \
-  }
-    switch (t) {
-      MOSS_HATTN_STREAM(1) MOSS_HATTN_STREAM(2) MOSS_HATTN_STREAM(3) MOSS_HATTN_STREAM(4)
-      MOSS_HATTN_STREAM(5) MOSS_HATTN_STREAM(6) MOSS_HATTN_STREAM(7) MOSS_HATTN_STREAM(8)
-      default: break;
-    }
-#undef MOSS_HATTN_STREAM
-    return launch_status(name);
+    return launch_stream<false>(sa, static_cast<int>(t), static_cast<int>(n), st, name);
   }
   const size_t shmem = smem_bytes(static_cast<int>(t), static_cast<int>(n));
   const unsigned grid = static_cast<unsigned>(s * h);
@@ -695,4 +802,41 @@ extern "C" int moss_history_attention(const void* q, const void* k_cache, const 
   }
 #undef MOSS_HATTN
   return launch_status(name);
+}
+
+extern "C" int moss_history_attention_qkv(const void* qkv, const int64_t* slots, float freq_coef,
+                                          void* k_cache, void* v_cache, const int64_t* slot_pos,
+                                          const int64_t* pos, int64_t s, int64_t h, int64_t t,
+                                          int64_t n, int64_t d, int64_t context, float scale,
+                                          void* out, void* stream) {
+  using namespace hattn;
+  const char* name = "moss_history_attention_qkv";
+  if (s < 0 || h < 1 || t < 1 || n < 1 || context < 1)
+    return fail(MOSS_ERR_VALUE, "%s: need streams >= 0, heads, queries, slots and context >= 1", name);
+  if (d != kDim) return fail(MOSS_ERR_UNSUPPORTED, "%s: only heads of 64 are supported", name);
+  if (s == 0) return MOSS_OK;
+  if (!qkv || !slots || !k_cache || !v_cache || !slot_pos || !pos || !out)
+    return fail(MOSS_ERR_VALUE, "%s: null pointer", name);
+  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(MOSS_ERR_VALUE, "%s: qkv and the history rings must be 16-byte aligned", name);
+  // the persistent kernel's range only: many (stream, head) items, rings of
+  // at most 256 slots, at most 8 queries
+  const int64_t items = s * h;
+  const int64_t sms = sm_count();
+  if (t > kMaxQueries || n > kStreamMaxKeys || items < 2 * sms || items * n >= 0x7fffffffLL)
+    return fail(MOSS_ERR_UNSUPPORTED,
+                "%s: needs at most %d queries, at most %d slots and at least %lld (stream, head) "
+                "items; use moss_rope_kv and moss_history_attention",
+                name, kMaxQueries, kStreamMaxKeys, static_cast<long long>(2 * sms));
+  StreamArgs sa{};
+  if (!encode_ring(&sa.k_map, k_cache, items * n, static_cast<int>(n)))
+    return fail(MOSS_ERR_CUDA, "%s: tensor map encoding failed", name);
+  sa.a = Args{nullptr, static_cast<const uint16_t*>(k_cache), static_cast<const uint16_t*>(v_cache),
+              slot_pos, pos, static_cast<uint16_t*>(out), context, scale, static_cast<int>(h),
+              static_cast<int>(t), static_cast<int>(n)};
+  sa.items = items;
+  sa.qkv = static_cast<const uint16_t*>(qkv);
+  sa.slots = slots;
+  sa.coef = freq_coef;
+  return launch_stream<true>(sa, static_cast<int>(t), static_cast<int>(n), as_stream(stream), name);
 }

@@ -22,6 +22,7 @@ from .rvq import ResidualVectorQuantizer
 from .v2_pointwise import (
     gated_activation,
     history_attention,
+    history_attention_qkv,
     layer_norm,
     pack_qkv_weight,
     qkv_rope,
@@ -48,6 +49,7 @@ __all__ = [
     "residual_layer_norm",
     "gated_activation",
     "history_attention",
+    "history_attention_qkv",
     "select",
     "decode_latents",
     "prepare",

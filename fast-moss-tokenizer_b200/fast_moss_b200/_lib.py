@@ -62,6 +62,8 @@ _SIGNATURES = {
                            _i64, _vp]),
     "moss_history_attention": (_i, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,
                                     _f, _vp, _vp]),
+    "moss_history_attention_qkv": (_i, [_vp, _vp, _f, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                        _i64, _i64, _f, _vp, _vp]),
     "moss_gated_act": (_i, [_vp, _vp, _vp, _i, _i64, _i64, _i, _i, _vp]),
     "moss_linear_pack_weight": (_i, [_vp, _i64, _i64, _vp, _vp]),
     "moss_linear": (_i, [_vp, _i64, _i64, _vp, _i64, _vp, _i, _i, _vp, _vp]),

@@ -58,6 +58,7 @@ from .linear import pack_weight
 from .v2_pointwise import (
     gated_activation,
     history_attention,
+    history_attention_qkv,
     layer_norm,
     pack_qkv_weight,
     qkv_rope,
@@ -259,9 +260,19 @@ class StreamingTransformer:
                                        or cfg.history_slots > 512):
             raise ValueError("the history attention kernel needs heads of 64, at most 8 "
                              "tokens per chunk and at most 512 history slots")
+        # with many (stream, head) items the rotary and the ring update run
+        # inside the attention kernel (moss_history_attention_qkv)
+        self._fused_attention_items = 2 * torch.cuda.get_device_properties(
+            device).multi_processor_count
 
     def history(self, streams):
         return StreamHistory(self.cfg, streams, self.device)
+
+    def _attention_takes_qkv(self, streams):
+        """True when the history attention also does the rotary and the ring
+        update (moss_history_attention_qkv): its persistent kernel's range."""
+        return (self.history_attention and streams * self.cfg.heads >= self._fused_attention_items
+                and self.cfg.history_slots <= 256)
 
     def _linear(self, x, p, name):
         if self.owned_linear:
@@ -275,6 +286,9 @@ class StreamingTransformer:
         residual + LayerNorm passes (the last layer's second is
         moss_scale_add) and the feed-forward activation."""
         per_layer = 4 + (1 if self.history_attention else 0)
+        if self._attention_takes_qkv(streams) and not (
+                self.fused_qkv and streams * self.cfg.chunk_tokens <= FUSED_QKV_MAX_ROWS):
+            per_layer -= 1  # the rotary runs inside the attention kernel
         if self.owned_linear:
             per_layer += 3  # four Linears, the activation in the first feed-forward one
         return 1 + self.cfg.layers * per_layer
@@ -297,24 +311,33 @@ class StreamingTransformer:
         bf16 = torch.bfloat16
         # LayerNorm outputs go straight to the next GEMM as its bf16 input
         normed = layer_norm(x, first["norm1_w"], first["norm1_b"], cfg.eps, out_dtype=bf16)
+        fused_qkv = self.fused_qkv and s * t <= FUSED_QKV_MAX_ROWS and not self.owned_linear
+        fused_attention = self._attention_takes_qkv(s) and not fused_qkv
         for i, p in enumerate(self.layers):
-            if self.fused_qkv and s * t <= FUSED_QKV_MAX_ROWS and not self.owned_linear:
-                q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
-                             slots, hist.keys[i], hist.values[i])
-            else:
+            if fused_attention:
+                # rotary, ring update and attention in one kernel
                 qkv = self._linear(normed, p, "qkv")
-                qkv = qkv.view(s, t, 3, h, dh)
-                q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
-                            qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
-                            hist.keys[i], hist.values[i])
-            if self.history_attention:
-                a = history_attention(q, hist.keys[i], hist.values[i], hist.slot_pos, offset,
-                                      cfg.context).view(s, t, d)
+                a = history_attention_qkv(qkv.view(s, t, 3 * d), h, offset, cfg.max_period, slots,
+                                          hist.keys[i], hist.values[i], hist.slot_pos,
+                                          cfg.context).view(s, t, d)
             else:
-                with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
-                    a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
-                                                       attn_mask=mask)
-                a = a.transpose(1, 2).reshape(s, t, d)
+                if fused_qkv:
+                    q = qkv_rope(normed, p["qkv_image"], p["qkv_b16"], h, offset, cfg.max_period,
+                                 slots, hist.keys[i], hist.values[i])
+                else:
+                    qkv = self._linear(normed, p, "qkv")
+                    qkv = qkv.view(s, t, 3, h, dh)
+                    q = rope_kv(qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2),
+                                qkv[:, :, 2].transpose(1, 2), offset, cfg.max_period, slots,
+                                hist.keys[i], hist.values[i])
+                if self.history_attention:
+                    a = history_attention(q, hist.keys[i], hist.values[i], hist.slot_pos, offset,
+                                          cfg.context).view(s, t, d)
+                else:
+                    with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION]):
+                        a = F.scaled_dot_product_attention(q, hist.keys[i], hist.values[i],
+                                                           attn_mask=mask)
+                    a = a.transpose(1, 2).reshape(s, t, d)
             u = self._linear(a, p, "out")
             x, normed = residual_layer_norm(x, u, p["ls1"], p["norm2_w"], p["norm2_b"], cfg.eps,
                                             out_dtype=bf16)
@@ -417,6 +440,72 @@ class BatchedStreams:
             sl = slice(g * self.span, (g + 1) * self.span)
             out[:, sl].copy_(self.push(features[:, sl]))
         return out[:, :n]
+
+    @torch.inference_mode()
+    def run_host(self, host_in, host_out, *, reset=True, depth=2):
+        """Advances every stream through chunks held in pinned host memory.
+
+        host_in, host_out: chunk-major pinned host tensors [chunks, streams,
+        span, dim] FP32 (each chunk's block contiguous).  Chunk c's features
+        are copied to the device on one copy stream and chunk c's output back
+        on another while the neighbouring chunks replay (`depth` staging
+        buffers each way); the replay stream only moves them between the
+        staging buffers and the graph's static buffers (device to device).
+        On return the current stream waits for the last copy out
+        (synchronize before reading host_out)."""
+        shape = (self.streams, self.span, self.stack.cfg.dim)
+        if host_in.ndim != 4 or tuple(host_in.shape[1:]) != shape or host_in.is_cuda or \
+                host_in.dtype != torch.float32:
+            raise ValueError(f"host_in must be FP32 host features [chunks, {shape[0]}, "
+                             f"{shape[1]}, {shape[2]}]")
+        if host_out.shape != host_in.shape or host_out.is_cuda or host_out.dtype != torch.float32:
+            raise ValueError("host_out must be an FP32 host tensor shaped like host_in")
+        if depth < 1:
+            raise ValueError("depth must be >= 1")
+        dev = self.stack.device
+        main = torch.cuda.current_stream(dev)
+        h2d = torch.cuda.Stream(device=dev)
+        d2h = torch.cuda.Stream(device=dev)
+        stage_in = [torch.empty(shape, device=dev) for _ in range(depth)]
+        stage_out = [torch.empty(shape, device=dev) for _ in range(depth)]
+        # the staging buffers are used on the copy streams too: the caching
+        # allocator must not hand their memory out again before those uses
+        # end, and the copy streams start after the work already queued
+        for buf in stage_in:
+            buf.record_stream(h2d)
+        for buf in stage_out:
+            buf.record_stream(d2h)
+        h2d.wait_stream(main)
+        d2h.wait_stream(main)
+        in_free = [None] * depth   # main has copied stage_in[b] into the graph input
+        out_free = [None] * depth  # d2h has copied stage_out[b] to the host
+        if reset:
+            self.reset()
+        for c in range(host_in.shape[0]):
+            b = c % depth
+            if in_free[b] is not None:
+                h2d.wait_event(in_free[b])
+            with torch.cuda.stream(h2d):
+                stage_in[b].copy_(host_in[c], non_blocking=True)
+                loaded = torch.cuda.Event()
+                loaded.record(h2d)
+            main.wait_event(loaded)
+            self.input.copy_(stage_in[b])
+            in_free[b] = torch.cuda.Event()
+            in_free[b].record(main)
+            out = self.advance()
+            if out_free[b] is not None:
+                main.wait_event(out_free[b])
+            stage_out[b].copy_(out)
+            done = torch.cuda.Event()
+            done.record(main)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                host_out[c].copy_(stage_out[b], non_blocking=True)
+                out_free[b] = torch.cuda.Event()
+                out_free[b].record(d2h)
+        main.wait_stream(d2h)
+        main.wait_stream(h2d)
 
     def release(self):
         """Drops the captured graph and its static buffers."""

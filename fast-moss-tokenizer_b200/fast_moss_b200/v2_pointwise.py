@@ -202,6 +202,62 @@ def history_attention(q, k_cache, v_cache, slot_pos, pos, context, scale=None, o
     return out
 
 
+def history_attention_qkv(qkv, heads, pos, max_period, slots, k_cache, v_cache, slot_pos,
+                          context, scale=None, out=None):
+    """`rope_kv` followed by `history_attention` in one kernel.
+
+    qkv: bf16 [S, T, 3 * heads * 64] (the qkv projection's output: q, k, v of
+    every head); pos: int64 [S], the chunk's first position (the rotary
+    offset and the queries' position); slots: int64 [S, T]; k_cache,
+    v_cache, slot_pos, context, scale as for `history_attention`.  Rotates q
+    and k as `rope_kv` does, writes the rotated keys and the values into the
+    rings and returns the attention [S, T, heads, 64]: the same bits as the
+    two calls.  Covers many (stream, head) items (at least twice the SM
+    count), rings of at most 256 slots and at most 8 queries; other inputs
+    raise UnsupportedError (call `rope_kv` and `history_attention` then)."""
+    if qkv.ndim != 3 or k_cache.ndim != 4:
+        raise ValueError("Expected qkv [S, T, 3*H*D] and caches [S, H, N, D]")
+    s, t, width = qkv.shape
+    h, n, d = k_cache.shape[1], k_cache.shape[2], k_cache.shape[3]
+    if (
+        qkv.dtype != torch.bfloat16
+        or k_cache.dtype != torch.bfloat16
+        or v_cache.dtype != torch.bfloat16
+        or not qkv.is_cuda
+        or any(x.device != qkv.device for x in (k_cache, v_cache, slot_pos, pos, slots))
+        or h != heads
+        or width != 3 * h * d
+        or k_cache.shape[0] != s
+        or v_cache.shape != k_cache.shape
+        or not k_cache.is_contiguous()
+        or not v_cache.is_contiguous()
+        or slot_pos.shape != (s, n)
+        or slot_pos.dtype != torch.int64
+        or pos.shape != (s,)
+        or pos.dtype != torch.int64
+        or slots.shape != (s, t)
+        or slots.dtype != torch.int64
+    ):
+        raise ValueError("Expected same-device bf16 qkv [S,T,3*H*D] and contiguous [S,H,N,D] bf16 "
+                         "caches, int64 [S,N] slot positions, [S] positions and [S,T] slots")
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    if out is None:
+        out = torch.empty((s, t, h, d), device=qkv.device, dtype=torch.bfloat16)
+    elif out.shape != (s, t, h, d) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bf16 [S, T, H, D] tensor")
+    qkv = qkv.contiguous()
+    slots = slots.contiguous()
+    slot_pos = slot_pos.contiguous()
+    pos = pos.contiguous()
+    coef = -math.log(max_period) * 2 / d
+    with torch.cuda.device(qkv.device):
+        _lib.call("moss_history_attention_qkv", qkv.data_ptr(), slots.data_ptr(), coef,
+                  k_cache.data_ptr(), v_cache.data_ptr(), slot_pos.data_ptr(), pos.data_ptr(),
+                  s, h, t, n, d, int(context), float(scale), out.data_ptr(), _stream(qkv.device))
+    return out
+
+
 def pack_qkv_weight(weight):
     """Packs a bf16 qkv Linear weight [3*H*64, K] (K a multiple of 64) for
     `qkv_rope`: blocks of 32 rows x 64 columns in the tensor cores'

@@ -238,6 +238,29 @@ MOSS_API int moss_history_attention(const void* q, const void* k_cache, const vo
               void* stream);
 
 /* ---------------------------------------------------------------------------
+ * moss_rope_kv followed by moss_history_attention in one kernel: the
+ * streaming layer's rotary forward (fast_moss/v2_runtime.py:186-224), the
+ * history's key/value update (fast_moss/streaming.py:68-79) and the
+ * attention over the history (fast_moss/v2_runtime.py:40-41, :254-262).
+ *   qkv [s * t, 3 * h * 64] bf16, 16-byte aligned: the qkv projection's
+ *     output (row s_i * t + t_i; q, k, v of every head of 64)
+ *   slots int64 [s, t]: each token's ring slot; freq_coef: as moss_rope_kv
+ *   pos int64 [s]: the chunk's first position, both the rotary offset and
+ *     the queries' position
+ * q and k are rotated exactly as moss_rope_kv does; the rotated keys and
+ * the values are written into k_cache / v_cache at their slots (a slot out
+ * of range is skipped and reported in the device error word) and the
+ * attention is that of moss_history_attention on the rotated q: the same
+ * bits as the two calls.  Covers the persistent kernel's range only (at
+ * most 8 queries, rings of at most 256 slots, at least two (stream, head)
+ * items per resident CTA: 2 x the SM count); MOSS_ERR_UNSUPPORTED otherwise.
+ * ------------------------------------------------------------------------- */
+MOSS_API int moss_history_attention_qkv(const void* qkv, const int64_t* slots, float freq_coef,
+              void* k_cache, void* v_cache, const int64_t* slot_pos,
+              const int64_t* pos, int64_t s, int64_t h, int64_t t, int64_t n,
+              int64_t d, int64_t context, float scale, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Linear layer on cached bf16 weights, tcgen05 tensor cores, bias or bias +
  * activation in the epilogue.
  * Replaces the cached bf16 Linear of the patched model

@@ -151,3 +151,65 @@ def test_stack_with_history_attention(moss, cuda_device, fused_qkv):
     assert rel < 2e-2, rel
     sp.release()
     so.release()
+
+
+@pytest.mark.parametrize("streams,heads,tokens,slots,context", [
+    (64, 20, 4, 253, 250),   # the 64-stream stack
+    (16, 20, 1, 253, 250), (40, 8, 2, 100, 60), (16, 20, 8, 256, 250),
+])
+def test_history_attention_qkv_matches_rope_kv_then_attention(moss, cuda_device, streams, heads,
+                                                              tokens, slots, context):
+    """The fused entry (rotary + ring update + attention) against moss_rope_kv
+    followed by moss_history_attention on the same inputs: the same bits in
+    the output and in both rings."""
+    _, k, v, slot_pos, pos = _ring(streams, heads, slots, tokens, context, 11, cuda_device)
+    g = torch.Generator().manual_seed(12)
+    qkv = torch.randn(streams, tokens, 3 * heads * 64, generator=g).to(cuda_device, torch.bfloat16)
+    slot_of = torch.remainder(pos[:, None] + torch.arange(tokens, device=cuda_device), slots)
+    k1, v1 = k.clone(), v.clone()
+    view = qkv.view(streams, tokens, 3, heads, 64)
+    q = moss.rope_kv(view[:, :, 0].transpose(1, 2), view[:, :, 1].transpose(1, 2),
+                     view[:, :, 2].transpose(1, 2), pos, 10000.0, slot_of, k1, v1)
+    want = moss.history_attention(q, k1, v1, slot_pos, pos, context)
+    k2, v2 = k.clone(), v.clone()
+    got = moss.history_attention_qkv(qkv, heads, pos, 10000.0, slot_of, k2, v2, slot_pos, context)
+    torch.cuda.synchronize()
+    assert torch.equal(k2.view(torch.int16), k1.view(torch.int16))
+    assert torch.equal(v2.view(torch.int16), v1.view(torch.int16))
+    assert torch.equal(torch.isnan(got), torch.isnan(want))
+    ok = ~torch.isnan(want)
+    assert torch.equal(got[ok].view(torch.int16), want[ok].view(torch.int16))
+    from fast_moss_b200 import _lib
+    _lib.check(_lib.load().moss_check_device_error(None), "device error word")
+
+
+def test_history_attention_qkv_rejects_the_per_item_range(moss, cuda_device):
+    from fast_moss_b200._lib import UnsupportedError
+
+    _, k, v, slot_pos, pos = _ring(2, 4, 16, 2, 9, 5, cuda_device)
+    qkv = torch.zeros(2, 2, 3 * 4 * 64, device=cuda_device, dtype=torch.bfloat16)
+    slot_of = torch.zeros(2, 2, device=cuda_device, dtype=torch.int64)
+    with pytest.raises(UnsupportedError):  # too few (stream, head) items
+        moss.history_attention_qkv(qkv, 4, pos, 10000.0, slot_of, k, v, slot_pos, 9)
+
+
+def test_stack_fused_attention_equals_the_two_kernels(moss, cuda_device):
+    """64 streams (the headline's batch): the stack whose attention also
+    rotates and writes the ring gives the same bits as the stack that calls
+    moss_rope_kv and moss_history_attention, under graph replay."""
+    from fast_moss_b200.transformer import (BatchedStreams, StackConfig, StreamingTransformer,
+                                            init_weights)
+
+    cfg = StackConfig()
+    weights = init_weights(cfg, seed=2)
+    fused = StreamingTransformer(cfg, weights, cuda_device, history_attention=True)
+    split = StreamingTransformer(cfg, weights, cuda_device, history_attention=True)
+    split._fused_attention_items = 1 << 30  # never fused
+    assert fused._attention_takes_qkv(64) and not split._attention_takes_qkv(64)
+    g = torch.Generator().manual_seed(8)
+    feats = torch.randn(64, 4 * 3, cfg.dim, generator=g).to(cuda_device)
+    sf = BatchedStreams(fused, streams=64)
+    ss = BatchedStreams(split, streams=64)
+    assert torch.equal(sf(feats), ss(feats))
+    sf.release()
+    ss.release()

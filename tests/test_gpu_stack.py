@@ -156,3 +156,27 @@ def test_owned_linear_stack(moss, cuda_device):
         rel = float((a - b).norm() / a.norm())
         assert rel < 2e-2, (opts, rel)
         so.release()
+
+
+def test_batched_streams_run_host_matches_the_device_path(moss, cuda_device):
+    """run_host (copies in and out overlapped with the replays) gives the
+    same bits as pushing the same chunks from device memory."""
+    from fast_moss_b200.transformer import BatchedStreams, StackConfig, StreamingTransformer
+    from fast_moss_b200.transformer import init_weights
+
+    cfg = StackConfig(layers=2)
+    stack = StreamingTransformer(cfg, init_weights(cfg, seed=2), cuda_device,
+                                 history_attention=True)
+    sched = BatchedStreams(stack, streams=3)
+    g = torch.Generator().manual_seed(9)
+    feats = torch.randn(7, 3, cfg.chunk_tokens, cfg.dim, generator=g)
+    host_in = feats.pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    sched.run_host(host_in, host_out)
+    torch.cuda.synchronize()
+    sched.reset()
+    want = torch.stack([sched.push(feats[c].to(cuda_device)).cpu() for c in range(7)])
+    assert torch.equal(host_out, want)
+    with pytest.raises(ValueError):
+        sched.run_host(host_in[:, :2], host_out[:, :2])
+    sched.release()
