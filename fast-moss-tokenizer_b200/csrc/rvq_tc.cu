@@ -34,9 +34,11 @@
 //              and 64 + i), so four threads screen its 256 columns per tile
 //              (two lane copies x two column halves); with 128 rows per CTA
 //              each row has one lane and two threads.  The part-0 thread of
-//              a row owns it: residual in registers, the exact resolve of
-//              its warp's candidate queue, the residual update, and the next
-//              stage's A operand (2r, K-major 128B-swizzled) in shared memory;
+//              a row owns its norm, window and slow-path flag; the lanes of
+//              each warp share the exact resolve of its candidate queue; the
+//              residual itself is spread over all 256 threads in 16-byte
+//              units (16 adjacent lanes per row), which update it and write
+//              the next stage's A operand (2r, K-major 128B-swizzled);
 //   warp 8     producer: cp.async.bulk of pre-built 256-code codebook tile
 //              images (64 KB swizzled dims + 8 KB norm column) into 2 slots;
 //   warp 9     TMEM allocator + MMA issuer: per tile 9 x tcgen05.mma
@@ -78,6 +80,9 @@ struct __align__(1024) Smem {
 // The dynamic allocation adds 1024 bytes of alignment slack.
 static_assert(sizeof(Smem) + 1024 <= 232448, "shared memory above the sm_100 per-block limit");
 
+// kCopies = 2: at most 64 rows per CTA, every row in two TMEM lanes; 1: up to
+// 128 rows, one lane each.
+template <int kCopies>
 __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment for the swizzled operand images, by pointer
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
   const int rpc = a.rows_per_cta;
   // rows_per_cta <= 64: every row sits in two TMEM lanes, copy c of local
   // row i in lane c * 64 + i (lanes i >= rpc of each copy hold no row)
-  const int copies = rpc <= kRows / 2 ? 2 : 1;
+  constexpr int copies = kCopies;
   const int span = kRows / copies;  // lanes per copy
   const int64_t row0 = static_cast<int64_t>(blockIdx.x) * rpc;
 
@@ -107,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       mbar_init(&sm.t_full[i], 1);
       mbar_init(&sm.t_empty[i], kEpiThreads);
     }
-    mbar_init(&sm.a_full, span);  // every owner thread writes its lane
+    mbar_init(&sm.a_full, kEpiThreads);  // every epilogue thread writes its units
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     sm.slow_count = 0;
   }
@@ -197,17 +202,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     const bool owner = part == 0;
     const int64_t grow = row0 + lr;
     const bool valid = lr < rpc && grow < a.rows;
-    float r[kDim];
-    if (owner && valid) {
-      const float4* src = reinterpret_cast<const float4*>(a.x + grow * kDim);
+    // The residual is spread over all epilogue threads in 16-byte units: unit
+    // i of thread `tid` is dims [4 uchunk, 4 uchunk + 4) of local row
+    // unit_row(i), so the 16 units of a row sit in 16 adjacent lanes and each
+    // codeword read, A-image write and output store of a row is one
+    // contiguous 256-byte span.
+    constexpr int kUnits = kRows / kCopies * (kDim / 4) / kEpiThreads;
+    const int uchunk = tid & 15;
+    auto unit_row = [&](int i) { return (tid >> 4) + 16 * i; };
+    auto unit_valid = [&](int i) { return unit_row(i) < rpc && row0 + unit_row(i) < a.rows; };
+    float4 r4[kUnits];
 #pragma unroll
-      for (int i = 0; i < kDim / 4; ++i) {
-        const float4 v = src[i];
-        r[4 * i] = v.x; r[4 * i + 1] = v.y; r[4 * i + 2] = v.z; r[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int d = 0; d < kDim; ++d) r[d] = 0.0f;
+    for (int i = 0; i < kUnits; ++i) {
+      r4[i] = unit_valid(i)
+                  ? reinterpret_cast<const float4*>(a.x + (row0 + unit_row(i)) * kDim)[uchunk]
+                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     unsigned char* a_bytes = reinterpret_cast<unsigned char*>(sm.a);
     if (owner) {
@@ -221,29 +230,24 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     // The A operand (2r, in every copy) of the next stage is written as soon
     // as the residual is known, so that its MMA starts before the bookkeeping
-    // of the stage boundary.
+    // of the stage boundary.  Every epilogue thread writes its units (rows
+    // past the CTA's rows hold zeros) and arrives.
+    const uint32_t a_base = smem_u32(sm.a);
     auto write_a = [&]() {
-      const uint32_t a_base = smem_u32(sm.a);
-      if (copies == 2) {
 #pragma unroll
-        for (int c = 0; c < kDim / 4; ++c) {
-          const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
-          const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
-          st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
-          st_shared_v4(a_base + sw128_offset(lr + span, 4 * c, kRows * 128u), x0, x1, x2, x3);
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < kDim / 4; ++c) {
-          const float x0 = __fmul_rn(2.0f, r[4 * c]), x1 = __fmul_rn(2.0f, r[4 * c + 1]);
-          const float x2 = __fmul_rn(2.0f, r[4 * c + 2]), x3 = __fmul_rn(2.0f, r[4 * c + 3]);
-          st_shared_v4(a_base + sw128_offset(lr, 4 * c, kRows * 128u), x0, x1, x2, x3);
-        }
+      for (int i = 0; i < kUnits; ++i) {
+        const float x0 = __fmul_rn(2.0f, r4[i].x), x1 = __fmul_rn(2.0f, r4[i].y);
+        const float x2 = __fmul_rn(2.0f, r4[i].z), x3 = __fmul_rn(2.0f, r4[i].w);
+        st_shared_v4(a_base + sw128_offset(unit_row(i), 4 * uchunk, kRows * 128u), x0, x1, x2, x3);
+        if (kCopies == 2)
+          st_shared_v4(a_base + sw128_offset(unit_row(i) + span, 4 * uchunk, kRows * 128u), x0, x1,
+                       x2, x3);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       mbar_arrive(&sm.a_full);
     };
-    if (owner) write_a();
+    write_a();
+    epi_bar();  // the first A image is complete before the owners read it
 
     int q = 0;
     bool aborted = false;
@@ -260,9 +264,21 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       }
       float norm = 0.0f;
       if (owner) {
+        // r_d = (2 r_d) / 2 exactly from the A image; where 2 r_d overflowed,
+        // r_d^2 overflows as well, so the sum is the same
 #pragma unroll
-        for (int d = 0; d < kDim; ++d) norm = __fmaf_rn(r[d], r[d], norm);
+        for (int c = 0; c < kDim / 4; ++c) {
+          const float4 tw =
+              *reinterpret_cast<const float4*>(a_bytes + sw128_offset(lr, 4 * c, kRows * 128u));
+          const float r0 = __fmul_rn(0.5f, tw.x), r1 = __fmul_rn(0.5f, tw.y);
+          const float r2 = __fmul_rn(0.5f, tw.z), r3 = __fmul_rn(0.5f, tw.w);
+          norm = __fmaf_rn(r0, r0, norm);
+          norm = __fmaf_rn(r1, r1, norm);
+          norm = __fmaf_rn(r2, r2, norm);
+          norm = __fmaf_rn(r3, r3, norm);
+        }
         sm.norms[lr] = norm;
+        sm.sel[lr] = -1;  // set by the exact scan for the rows that take it
         // screening window and preconditions
         const float sc = __fmul_rn(2.0f, sqrtf(norm)) * sqrtf(cn_max);
         const bool slow = !(isfinite(norm) && book_ok && sc < 1.0e36f);
@@ -479,63 +495,69 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         epi_bar();
         if (warp == 0 && lane == 0) sm.slow_count = 0;
       }
-      if (owner && valid && winner < 0) {
-        // Unreachable: on the fast path the screening maximum is a real code
-        // (padding codes screen at -inf, real ones are finite), so every
-        // unflagged row has a resolved candidate.  Kept in bounds, reported.
-        record_device_error(MOSS_ERR_UNSUPPORTED);
-        winner = 0;
-      }
-      if (owner && valid) {
-        // ---- update the residual (the reconstruction is summed at the end)
-        const float4* cw =
-            reinterpret_cast<const float4*>(book + static_cast<int64_t>(winner) * kDim);
+      // ---- update the residual (the reconstruction is summed at the end).
+      // A row's code is the exact scan's where it took one, else the key
+      // minimum; both are final here, so every thread updates its own units.
 #pragma unroll
-        for (int i = 0; i < kDim / 4; ++i) {
-          const float4 v = cw[i];
-          r[4 * i] = __fsub_rn(r[4 * i], v.x);
-          r[4 * i + 1] = __fsub_rn(r[4 * i + 1], v.y);
-          r[4 * i + 2] = __fsub_rn(r[4 * i + 2], v.z);
-          r[4 * i + 3] = __fsub_rn(r[4 * i + 3], v.w);
+      for (int i = 0; i < kUnits; ++i) {
+        if (!unit_valid(i)) continue;
+        const int row = unit_row(i);
+        int w = sm.sel[row];
+        if (w < 0) {
+          const unsigned long long key = sm.best[row];
+          if (key != ~0ull) {
+            w = static_cast<int>(key & 0xffffffffu);
+          } else {
+            // Unreachable: on the fast path the screening maximum is a real
+            // code (padding codes screen at -inf, real ones are finite), so
+            // every row outside the exact scan has a resolved candidate.
+            // Kept in bounds, reported.
+            if (uchunk == 0) record_device_error(MOSS_ERR_UNSUPPORTED);
+            w = 0;
+          }
         }
-        a.codes[static_cast<int64_t>(s) * a.rows + grow] = winner;
+        const float4 v =
+            reinterpret_cast<const float4*>(book + static_cast<int64_t>(w) * kDim)[uchunk];
+        r4[i].x = __fsub_rn(r4[i].x, v.x);
+        r4[i].y = __fsub_rn(r4[i].y, v.y);
+        r4[i].z = __fsub_rn(r4[i].z, v.z);
+        r4[i].w = __fsub_rn(r4[i].w, v.w);
+        if (uchunk == 0) a.codes[static_cast<int64_t>(s) * a.rows + row0 + row] = w;
       }
       // every reader of this stage's A image (MMA, exact distances, slow
       // scan) is done: the next stage's operand can go in
-      if (owner && s + 1 < a.stages) write_a();
+      if (s + 1 < a.stages) write_a();
       // the slow scan read the A image and the resolve read the other parts'
       // records: both must be finished before the next stage rewrites them
       epi_bar();
     }
-    if (owner && !aborted && valid) {
+    if (!aborted) {
       // recon = sum of the chosen codewords in stage order from +0 (the same
-      // float32 additions as an incremental sum)
-      float acc[kDim];
+      // float32 additions as an incremental sum), unit by unit.  The codes
+      // were stored by the rows' first-unit threads before the stage
+      // barriers; they are read past L1.
+      float4 acc[kUnits];
 #pragma unroll
-      for (int d = 0; d < kDim; ++d) acc[d] = 0.0f;
-#pragma unroll 4
+      for (int i = 0; i < kUnits; ++i) acc[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       for (int s = 0; s < a.stages; ++s) {
-        const int c = a.codes[static_cast<int64_t>(s) * a.rows + grow];
-        const float4* cw = reinterpret_cast<const float4*>(
-            a.books + (static_cast<int64_t>(s) * a.k + c) * kDim);
 #pragma unroll
-        for (int i = 0; i < kDim / 4; ++i) {
-          const float4 v = cw[i];
-          acc[4 * i] = __fadd_rn(acc[4 * i], v.x);
-          acc[4 * i + 1] = __fadd_rn(acc[4 * i + 1], v.y);
-          acc[4 * i + 2] = __fadd_rn(acc[4 * i + 2], v.z);
-          acc[4 * i + 3] = __fadd_rn(acc[4 * i + 3], v.w);
+        for (int i = 0; i < kUnits; ++i) {
+          if (!unit_valid(i)) continue;
+          const int c = __ldcg(a.codes + static_cast<int64_t>(s) * a.rows + row0 + unit_row(i));
+          const float4 v = reinterpret_cast<const float4*>(
+              a.books + (static_cast<int64_t>(s) * a.k + c) * kDim)[uchunk];
+          acc[i].x = __fadd_rn(acc[i].x, v.x);
+          acc[i].y = __fadd_rn(acc[i].y, v.y);
+          acc[i].z = __fadd_rn(acc[i].z, v.z);
+          acc[i].w = __fadd_rn(acc[i].w, v.w);
         }
       }
-      float4* dst = reinterpret_cast<float4*>(a.recon + grow * kDim);
 #pragma unroll
-      for (int i = 0; i < kDim / 4; ++i)
-        dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
-      if (a.residual_out) {
-        float4* res = reinterpret_cast<float4*>(a.residual_out + grow * kDim);
-#pragma unroll
-        for (int i = 0; i < kDim / 4; ++i)
-          res[i] = make_float4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+      for (int i = 0; i < kUnits; ++i) {
+        if (!unit_valid(i)) continue;
+        const int64_t g = row0 + unit_row(i);
+        reinterpret_cast<float4*>(a.recon + g * kDim)[uchunk] = acc[i];
+        if (a.residual_out) reinterpret_cast<float4*>(a.residual_out + g * kDim)[uchunk] = r4[i];
       }
     }
   }
@@ -621,13 +643,18 @@ extern "C" int moss_rvq_encode_kernel(const float* x, int64_t rows, int64_t d, c
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= kMaxDevices || !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(rvqtc::rvq_tc_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return fail(MOSS_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    for (auto fn : {rvqtc::rvq_tc_kernel<1>, rvqtc::rvq_tc_kernel<2>}) {
+      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return fail(MOSS_ERR_CUDA, "%s: %s", name, cudaGetErrorString(e));
+    }
     if (dev >= 0 && dev < kMaxDevices) configured[dev] = true;
   }
-  rvqtc::rvq_tc_kernel<<<static_cast<unsigned>(grid), rvqtc::kThreads, smem, as_stream(stream)>>>(args);
+  const dim3 blocks(static_cast<unsigned>(grid));
+  if (rows_per_cta <= rvqtc::kRows / 2)
+    rvqtc::rvq_tc_kernel<2><<<blocks, rvqtc::kThreads, smem, as_stream(stream)>>>(args);
+  else
+    rvqtc::rvq_tc_kernel<1><<<blocks, rvqtc::kThreads, smem, as_stream(stream)>>>(args);
   return launch_status(name);
 }
 
