@@ -382,8 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       // candidates overflow the queue; the flag rides on the next barrier.
       int slow_flag = (owner && valid && !fast) ? 1 : 0;
       // Count the surviving candidates, keeping the first four in registers
-      // for the queue fill and sending their codewords on their way into L1
-      // (the lane that resolves a candidate reads it from there).
+      // for the queue fill.
       int cnt = 0;
       int c0 = 0, c1 = 0, c2 = 0, c3 = 0;
       if (fast) {
@@ -402,9 +401,6 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           for (uint32_t m = rmask[e]; m; m &= m - 1) {
             const int j = base + (__ffs(m) - 1);
             if (cnt < 4) {
-              const int jc = j < a.k ? j : 0;
-              prefetch_l1(book + static_cast<int64_t>(jc) * kDim);
-              prefetch_l1(book + static_cast<int64_t>(jc) * kDim + 32);
               c3 = cnt == 3 ? j : c3;
               c2 = cnt == 2 ? j : c2;
               c1 = cnt == 1 ? j : c1;
@@ -451,7 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
         float4 w[kDim / 4];
 #pragma unroll
         for (int i4 = 0; i4 < kDim / 4; ++i4) w[i4] = cw[i4];
-        const float nj = cnorm[j];
+        // the code norm in the prepared order (sequential FMAs from +0), from
+        // the codeword in registers instead of one more dependent load
+        float nj = 0.0f;
         float dot = 0.0f;
 #pragma unroll
         for (int i4 = 0; i4 < kDim / 4; ++i4) {
@@ -461,6 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
           dot = __fmaf_rn(tw.y, w[i4].y, dot);
           dot = __fmaf_rn(tw.z, w[i4].z, dot);
           dot = __fmaf_rn(tw.w, w[i4].w, dot);
+          nj = __fmaf_rn(w[i4].x, w[i4].x, nj);
+          nj = __fmaf_rn(w[i4].y, w[i4].y, nj);
+          nj = __fmaf_rn(w[i4].z, w[i4].z, nj);
+          nj = __fmaf_rn(w[i4].w, w[i4].w, nj);
         }
         const float dist = __fadd_rn(__fadd_rn(__fsub_rn(sm.norms[rr], dot), nj), 0.0f);
         atomicMin(&sm.best[rr],
