@@ -381,34 +381,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       // A row needs the exact scan when its preconditions failed or its
       // candidates overflow the queue; the flag rides on the next barrier.
       int slow_flag = (owner && valid && !fast) ? 1 : 0;
-      // Count the surviving candidates, keeping the first four in registers
-      // for the queue fill.
+      // The records' fields are loaded together and filtered without
+      // branches; each record keeps its mask if its chunk maximum is still
+      // inside the final window.
       int cnt = 0;
-      int c0 = 0, c1 = 0, c2 = 0, c3 = 0;
-      if (fast) {
-        // the records' fields are loaded together, then walked
-        float rmax[kRec];
-        uint32_t rmask[kRec];
+      uint32_t keep[kRec];
+      int base[kRec];
 #pragma unroll
-        for (int e = 0; e < kRec; ++e) {
-          rmax[e] = e < nrec ? sm.rec_max[e][slot] : -CUDART_INF_F;
-          rmask[e] = e < nrec ? sm.rec_mask[e][slot] : 0u;
-        }
-#pragma unroll
-        for (int e = 0; e < kRec; ++e) {
-          if (rmax[e] < athr || rmask[e] == 0u) continue;
-          const int base = sm.rec_chunk[e][slot] * 32;
-          for (uint32_t m = rmask[e]; m; m &= m - 1) {
-            const int j = base + (__ffs(m) - 1);
-            if (cnt < 4) {
-              c3 = cnt == 3 ? j : c3;
-              c2 = cnt == 2 ? j : c2;
-              c1 = cnt == 1 ? j : c1;
-              c0 = cnt == 0 ? j : c0;
-            }
-            ++cnt;
-          }
-        }
+      for (int e = 0; e < kRec; ++e) {
+        const bool live = fast && e < nrec;
+        const float mx = live ? sm.rec_max[e][slot] : -CUDART_INF_F;
+        const uint32_t mask = live ? sm.rec_mask[e][slot] : 0u;
+        base[e] = live ? sm.rec_chunk[e][slot] * 32 : 0;
+        keep[e] = mx >= athr ? mask : 0u;
+        cnt += __popc(keep[e]);
       }
       int incl = cnt;
 #pragma unroll
@@ -421,20 +407,13 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       if (incl > kQueue) {
         sm.row_bad[lr] = 1;  // does not fit: exact scan
         slow_flag = 1;
-      } else if (cnt > 4) {  // rare: walk the records again
-        int pos = incl - cnt;
-        for (int e = 0; e < nrec; ++e) {
-          if (sm.rec_max[e][slot] < athr) continue;
-          const int base = sm.rec_chunk[e][slot] * 32;
-          for (uint32_t m = sm.rec_mask[e][slot]; m; m &= m - 1)
-            queue[pos++] = (lr << 16) | (base + (__ffs(m) - 1));
-        }
       } else if (cnt > 0) {
-        const int pos = incl - cnt;
-        queue[pos] = (lr << 16) | c0;
-        if (cnt > 1) queue[pos + 1] = (lr << 16) | c1;
-        if (cnt > 2) queue[pos + 2] = (lr << 16) | c2;
-        if (cnt > 3) queue[pos + 3] = (lr << 16) | c3;
+        int pos = incl - cnt;
+#pragma unroll
+        for (int e = 0; e < kRec; ++e) {
+          for (uint32_t m = keep[e]; m; m &= m - 1u)
+            queue[pos++] = (lr << 16) | (base[e] + (__ffs(m) - 1));
+        }
       }
       // entries [0, nq) are written: the rows whose candidates all fit
       const int nq = total <= kQueue ? total : __reduce_max_sync(0xffffffffu, incl <= kQueue ? incl : 0);
