@@ -716,7 +716,7 @@ def _attention_kernel_line(torch, dev, cfg):
     the output."""
     from torch.nn.attention import SDPBackend, sdpa_kernel
     from fast_moss_b200.transformer import StreamHistory, additive_mask
-    from fast_moss_b200.v2_pointwise import history_attention, history_attention_qkv
+    from fast_moss_b200.v2_pointwise import history_attention, history_attention_qkv, rope_kv
 
     h, t, dh = cfg.heads, cfg.chunk_tokens, cfg.head_dim
     res = {}
@@ -759,12 +759,23 @@ def _attention_kernel_line(torch, dev, cfg):
                 history_attention_qkv(qkv, h, offset, cfg.max_period, slots, layer[0], layer[1],
                                       hist.slot_pos, cfg.context)
 
+            # the same step unfused: moss_rope_kv (q rotated in place, k and v
+            # rotated into the rings) and then moss_history_attention
+            qkv_u = qkv.clone().view(streams, t, 3, h, dh)
+            qu, ku, vu = (qkv_u[:, :, i].transpose(1, 2) for i in range(3))
+
+            def unfused(layer, _handle):
+                rope_kv(qu, ku, vu, offset, cfg.max_period, slots, layer[0], layer[1])
+                history_attention(qu, layer[0], layer[1], hist.slot_pos, offset, cfg.context)
+
             tf = time_launches(torch, fused, layers, launches=48, replays=5)
+            tu = time_launches(torch, unfused, layers, launches=48, replays=5)
             # rings read, qkv read, the chunk's keys and values written, out
             fbytes = streams * (h * n * dh * 2 * 2 + 3 * h * t * dh * 2 + 2 * h * t * dh * 2 +
                                 h * t * dh * 2 + n * 8 + 8 + t * 8)
             line["fused_rotary"] = {"us": tf * 1e6, "gbs": fbytes / tf / 1e9, "bytes": fbytes,
-                                    "us_rope_kv_then_attention_kernel_only": to * 1e6}
+                                    "us_rope_kv_plus_attention": tu * 1e6,
+                                    "us_attention_kernel_alone": to * 1e6}
         res[f"streams_{streams}"] = line
         del hist, layers
     return res
@@ -1015,6 +1026,7 @@ def step_roofline(torch, dev, cfg, peaks, ms_per_chunk):
         "traffic": profile_traffic("history_attn_qkv_stream_kernel"),
         "bytes_per_launch": fused["bytes"], "us_per_launch": fused["us"],
         "us_per_launch_attention_alone": att["us_owned"], "us_per_launch_sdpa": att["us_sdpa"],
+        "us_rope_kv_plus_attention": fused["us_rope_kv_plus_attention"],
         "step": {"what": "one chunk of all 64 streams: bf16 weights of 24 layers + every layer's "
                          "key/value ring read once",
                  "bytes_per_chunk": chunk_bytes, "weight_bytes": weight_bytes,
