@@ -38,6 +38,7 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxDim = 2048;
 constexpr int kMaxCodes = 65536;
+constexpr int kGroup = 4;  // codes (dims) per thread held in registers at a time
 
 struct Args {
   const float* x;       // [B, D, T]
@@ -139,24 +140,42 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
       }
       const float* book = a.book + static_cast<int64_t>(s) * a.k * 8;
       const float* cn = a.cnorm + static_cast<int64_t>(s) * a.k;
-      for (int j = tid; j < a.k; j += kThreads) {
-        const float4 c0 = __ldg(reinterpret_cast<const float4*>(book + static_cast<int64_t>(j) * 8));
-        const float4 c1 =
-            __ldg(reinterpret_cast<const float4*>(book + static_cast<int64_t>(j) * 8 + 4));
-        const float cnj = __ldg(cn + j);
+      // kGroup codes of this thread (tid, tid + 256, ...) in registers, then
+      // every frame's 2e read once per group; each frame still sees its
+      // codes in ascending order
+      for (int j0 = tid; j0 < a.k; j0 += kGroup * kThreads) {
+        float4 c0[kGroup], c1[kGroup];
+        float cnj[kGroup];
+#pragma unroll
+        for (int m = 0; m < kGroup; ++m) {
+          const int j = j0 + m * kThreads;
+          const int jj = j < a.k ? j : j0;
+          c0[m] = __ldg(reinterpret_cast<const float4*>(book + static_cast<int64_t>(jj) * 8));
+          c1[m] = __ldg(reinterpret_cast<const float4*>(book + static_cast<int64_t>(jj) * 8 + 4));
+          cnj[m] = __ldg(cn + jj);
+        }
 #pragma unroll
         for (int f = 0; f < F; ++f) {
           if (f < nf) {
-            const float* t8 = tw + f * 8;
-            float dot = __fmul_rn(t8[0], c0.x);
-            dot = __fmaf_rn(t8[1], c0.y, dot);
-            dot = __fmaf_rn(t8[2], c0.z, dot);
-            dot = __fmaf_rn(t8[3], c0.w, dot);
-            dot = __fmaf_rn(t8[4], c1.x, dot);
-            dot = __fmaf_rn(t8[5], c1.y, dot);
-            dot = __fmaf_rn(t8[6], c1.z, dot);
-            dot = __fmaf_rn(t8[7], c1.w, dot);
-            pick32_push(pk[f], __fadd_rn(__fsub_rn(nrm[f], dot), cnj), j);
+            float t8[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) t8[q] = tw[f * 8 + q];
+            const float nf_ = nrm[f];
+#pragma unroll
+            for (int m = 0; m < kGroup; ++m) {
+              const int j = j0 + m * kThreads;
+              if (j < a.k) {
+                float dot = __fmul_rn(t8[0], c0[m].x);
+                dot = __fmaf_rn(t8[1], c0[m].y, dot);
+                dot = __fmaf_rn(t8[2], c0[m].z, dot);
+                dot = __fmaf_rn(t8[3], c0[m].w, dot);
+                dot = __fmaf_rn(t8[4], c1[m].x, dot);
+                dot = __fmaf_rn(t8[5], c1[m].y, dot);
+                dot = __fmaf_rn(t8[6], c1[m].z, dot);
+                dot = __fmaf_rn(t8[7], c1[m].w, dot);
+                pick32_push(pk[f], __fadd_rn(__fsub_rn(nf_, dot), cnj[m]), j);
+              }
+            }
           }
         }
       }
@@ -203,24 +222,41 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
     }
     __syncthreads();
     // ---- output projection and residual update: thread -> dims tid, tid + 256, ...
-    for (int dd = tid; dd < D; dd += kThreads) {
-      const float* wo = a.w_out + (static_cast<int64_t>(s) * D + dd) * 8;
-      const float4 w0 = __ldg(reinterpret_cast<const float4*>(wo));
-      const float4 w1 = __ldg(reinterpret_cast<const float4*>(wo + 4));
-      const float bo = __ldg(a.b_out + static_cast<int64_t>(s) * D + dd);
+    // kGroup dims of this thread (tid, tid + 256, ...) with their weights in
+    // registers, then every frame's codeword read once per group
+    for (int d0 = tid; d0 < D; d0 += kGroup * kThreads) {
+      float4 w0[kGroup], w1[kGroup];
+      float bo[kGroup];
+#pragma unroll
+      for (int m = 0; m < kGroup; ++m) {
+        const int dd = d0 + m * kThreads;
+        const int de = dd < D ? dd : d0;
+        const float* wo = a.w_out + (static_cast<int64_t>(s) * D + de) * 8;
+        w0[m] = __ldg(reinterpret_cast<const float4*>(wo));
+        w1[m] = __ldg(reinterpret_cast<const float4*>(wo + 4));
+        bo[m] = __ldg(a.b_out + static_cast<int64_t>(s) * D + de);
+      }
 #pragma unroll
       for (int f = 0; f < F; ++f) {
         if (f < nf) {
-          const float* c = cw + f * 8;
-          float o = __fmaf_rn(w0.x, c[0], 0.0f);
-          o = __fmaf_rn(w0.y, c[1], o);
-          o = __fmaf_rn(w0.z, c[2], o);
-          o = __fmaf_rn(w0.w, c[3], o);
-          o = __fmaf_rn(w1.x, c[4], o);
-          o = __fmaf_rn(w1.y, c[5], o);
-          o = __fmaf_rn(w1.z, c[6], o);
-          o = __fmaf_rn(w1.w, c[7], o);
-          r[f * D + dd] = __fsub_rn(r[f * D + dd], __fadd_rn(o, bo));
+          float c[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) c[q] = cw[f * 8 + q];
+#pragma unroll
+          for (int m = 0; m < kGroup; ++m) {
+            const int dd = d0 + m * kThreads;
+            if (dd < D) {
+              float o = __fmaf_rn(w0[m].x, c[0], 0.0f);
+              o = __fmaf_rn(w0[m].y, c[1], o);
+              o = __fmaf_rn(w0[m].z, c[2], o);
+              o = __fmaf_rn(w0[m].w, c[3], o);
+              o = __fmaf_rn(w1[m].x, c[4], o);
+              o = __fmaf_rn(w1[m].y, c[5], o);
+              o = __fmaf_rn(w1[m].z, c[6], o);
+              o = __fmaf_rn(w1[m].w, c[7], o);
+              r[f * D + dd] = __fsub_rn(r[f * D + dd], __fadd_rn(o, bo[m]));
+            }
+          }
         }
       }
     }
