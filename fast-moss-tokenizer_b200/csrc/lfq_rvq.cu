@@ -22,8 +22,9 @@
 //     o_d  = (FMA chain over j = 0..7 of w_out[s, d, j] c_j from +0) + b_out[s, d]
 //     r_d  = r_d - o_d ;  codes[s, b * T + t] = index
 // A CTA takes F frames (F = 1, 4 or 16 by the number of frames) for all
-// stages, 256 threads: warp j forms z_j for every frame (each weight read
-// serves F frames), each thread scores codes tid, tid + 256, ... for every
+// stages, 256 threads: each warp forms a block of the z_j x frames (4 x 4
+// at 16 frames, so each residual read serves four outputs and each weight
+// read four frames), each thread scores codes tid, tid + 256, ... for every
 // frame (a block reduction picks the winner), each thread updates dims
 // tid, tid + 256, ... of every frame.  The stage weights are read through
 // L1/L2 (about 120 KB per stage at D = 1280, K = 1024).
@@ -38,7 +39,9 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxDim = 2048;
 constexpr int kMaxCodes = 65536;
-constexpr int kGroup = 4;  // codes (dims) per thread held in registers at a time
+constexpr int kGroup = 4;  // codes per thread held in registers at a time
+constexpr int kOutGroup = 8;  // output dims per thread held in registers at a time
+constexpr int kInBlock = 10;  // input-projection dims per lane loaded ahead
 
 struct Args {
   const float* x;       // [B, D, T]
@@ -89,27 +92,61 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
   }
   __syncthreads();
   for (int s = 0; s < a.stages; ++s) {
-    // ---- input projection: warp j -> z_j of every frame
+    // ---- input projection: warp -> JW outputs z_j of FW frames (16 frames:
+    // a 4 x 4 block, so each residual value read from shared memory serves
+    // four outputs and each weight four frames); per output the order is
+    // the same for every blocking: lane partial sums over dims lane,
+    // lane + 32, ... from +0, then added pairwise across the lanes
     {
-      const float* wrow = a.w_in + (static_cast<int64_t>(s) * 8 + warp) * D;
-      float acc[F];
+      constexpr int JW = F == 16 ? 4 : 1;
+      constexpr int FW = F == 16 ? 4 : F;
+      static_assert((8 / JW) * (F / FW) == kWarps, "one block per warp");
+      const int j0 = (warp % (8 / JW)) * JW, f0 = (warp / (8 / JW)) * FW;
+      const float* wrow = a.w_in + (static_cast<int64_t>(s) * 8 + j0) * D;
+      float acc[JW][FW];
 #pragma unroll
-      for (int f = 0; f < F; ++f) acc[f] = 0.0f;
-      for (int dd = lane; dd < D; dd += 32) {
-        const float wv = __ldg(wrow + dd);
+      for (int jj = 0; jj < JW; ++jj)
 #pragma unroll
-        for (int f = 0; f < F; ++f) acc[f] = __fmaf_rn(wv, r[f * D + dd], acc[f]);
+        for (int ff = 0; ff < FW; ++ff) acc[jj][ff] = 0.0f;
+      // blocks of kInBlock dims per lane: the block's weight loads are all
+      // issued before its multiply-adds, one round trip per block
+      for (int db = 0; db < D; db += 32 * kInBlock) {
+        float wv[kInBlock][JW];
+#pragma unroll
+        for (int u = 0; u < kInBlock; ++u) {
+          const int dd = db + lane + 32 * u;
+#pragma unroll
+          for (int jj = 0; jj < JW; ++jj) wv[u][jj] = dd < D ? __ldg(wrow + jj * D + dd) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kInBlock; ++u) {
+          const int dd = db + lane + 32 * u;
+          if (dd < D) {
+#pragma unroll
+            for (int ff = 0; ff < FW; ++ff) {
+              const float rv = r[(f0 + ff) * D + dd];
+#pragma unroll
+              for (int jj = 0; jj < JW; ++jj) acc[jj][ff] = __fmaf_rn(wv[u][jj], rv, acc[jj][ff]);
+            }
+          }
+        }
       }
 #pragma unroll
-      for (int f = 0; f < F; ++f) {
+      for (int jj = 0; jj < JW; ++jj) {
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-          acc[f] = __fadd_rn(acc[f], __shfl_xor_sync(0xffffffffu, acc[f], off));
+        for (int ff = 0; ff < FW; ++ff) {
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+            acc[jj][ff] = __fadd_rn(acc[jj][ff], __shfl_xor_sync(0xffffffffu, acc[jj][ff], off));
+        }
       }
       if (lane == 0) {
-        const float bj = a.b_in[s * 8 + warp];
 #pragma unroll
-        for (int f = 0; f < F; ++f) z[f * 8 + warp] = __fadd_rn(acc[f], bj);
+        for (int jj = 0; jj < JW; ++jj) {
+          const float bj = a.b_in[s * 8 + j0 + jj];
+#pragma unroll
+          for (int ff = 0; ff < FW; ++ff) z[(f0 + ff) * 8 + j0 + jj] = __fadd_rn(acc[jj][ff], bj);
+        }
       }
     }
     __syncthreads();
@@ -222,13 +259,13 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
     }
     __syncthreads();
     // ---- output projection and residual update: thread -> dims tid, tid + 256, ...
-    // kGroup dims of this thread (tid, tid + 256, ...) with their weights in
+    // kOutGroup dims of this thread (tid, tid + 256, ...) with their weights in
     // registers, then every frame's codeword read once per group
-    for (int d0 = tid; d0 < D; d0 += kGroup * kThreads) {
-      float4 w0[kGroup], w1[kGroup];
-      float bo[kGroup];
+    for (int d0 = tid; d0 < D; d0 += kOutGroup * kThreads) {
+      float4 w0[kOutGroup], w1[kOutGroup];
+      float bo[kOutGroup];
 #pragma unroll
-      for (int m = 0; m < kGroup; ++m) {
+      for (int m = 0; m < kOutGroup; ++m) {
         const int dd = d0 + m * kThreads;
         const int de = dd < D ? dd : d0;
         const float* wo = a.w_out + (static_cast<int64_t>(s) * D + de) * 8;
@@ -243,7 +280,7 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
 #pragma unroll
           for (int q = 0; q < 8; ++q) c[q] = cw[f * 8 + q];
 #pragma unroll
-          for (int m = 0; m < kGroup; ++m) {
+          for (int m = 0; m < kOutGroup; ++m) {
             const int dd = d0 + m * kThreads;
             if (dd < D) {
               float o = __fmaf_rn(w0[m].x, c[0], 0.0f);
