@@ -65,6 +65,30 @@ __host__ __device__ inline size_t smem_bytes(int f, int d) {
   return static_cast<size_t>(f) * (d + 8 + 1 + 8 + 8 + 3 * kWarps + 1) * 4;
 }
 
+__device__ __forceinline__ Pick32 pick_shfl(const Pick32& p, int o) {
+  return Pick32{__shfl_xor_sync(0xffffffffu, p.best, o), __shfl_xor_sync(0xffffffffu, p.best_i, o),
+                __shfl_xor_sync(0xffffffffu, p.nan_i, o)};
+}
+__device__ __forceinline__ void pick_merge(Pick32& p, const Pick32& o) {
+  if (o.best < p.best || (o.best == p.best && o.best_i < p.best_i)) {
+    p.best = o.best;
+    p.best_i = o.best_i;
+  }
+  if (o.nan_i < p.nan_i) p.nan_i = o.nan_i;
+}
+// picks [0, M) -> [0, M / 2): the lanes with bit O set keep the upper half.
+template <int M, int O, int N>
+__device__ __forceinline__ void pick_halve(Pick32 (&pk)[N], int lane) {
+  const bool up = (lane & O) != 0;
+#pragma unroll
+  for (int i = 0; i < M / 2; ++i) {
+    const Pick32 lo = pk[i], hi = pk[i + M / 2];
+    Pick32 keep = up ? hi : lo;
+    pick_merge(keep, pick_shfl(up ? lo : hi, O));
+    pk[i] = keep;
+  }
+}
+
 template <int F>
 __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
   extern __shared__ float sm[];
@@ -216,25 +240,37 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
           }
         }
       }
+      // Warp reduction of the F frames' picks, scattered over the lanes:
+      // each halving step keeps half of the frames and merges in the other
+      // lane's copy of them, until every lane holds one frame (16 frames:
+      // lanes differing in bit 0 share one; 4 frames: bits 0-2), then a
+      // plain butterfly over the remaining lane bits.  The merge (lexicographic
+      // minimum of (best, index), minimum NaN index) is associative and
+      // commutative, so the winner is the same as over any other tree.
+      int frame = 0;
+      if constexpr (F == 16) {
+        pick_halve<16, 16>(pk, lane);
+        pick_halve<8, 8>(pk, lane);
+        pick_halve<4, 4>(pk, lane);
+        pick_halve<2, 2>(pk, lane);
+        pick_merge(pk[0], pick_shfl(pk[0], 1));
+        frame = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                ((lane >> 1) & 1);
+      } else if constexpr (F == 4) {
+        pick_halve<4, 16>(pk, lane);
+        pick_halve<2, 8>(pk, lane);
 #pragma unroll
-      for (int f = 0; f < F; ++f) {
-        Pick32 p = pk[f];
+        for (int o = 4; o > 0; o >>= 1) pick_merge(pk[0], pick_shfl(pk[0], o));
+        frame = ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+      } else {
 #pragma unroll
-        for (int m = 16; m > 0; m >>= 1) {
-          const float ob = __shfl_xor_sync(0xffffffffu, p.best, m);
-          const int oi = __shfl_xor_sync(0xffffffffu, p.best_i, m);
-          const int on = __shfl_xor_sync(0xffffffffu, p.nan_i, m);
-          if (ob < p.best || (ob == p.best && oi < p.best_i)) {
-            p.best = ob;
-            p.best_i = oi;
-          }
-          if (on < p.nan_i) p.nan_i = on;
-        }
-        if (lane == 0) {
-          pbest[f * kWarps + warp] = p.best;
-          pidx[f * kWarps + warp] = p.best_i;
-          pnan[f * kWarps + warp] = p.nan_i;
-        }
+        for (int o = 16; o > 0; o >>= 1) pick_merge(pk[0], pick_shfl(pk[0], o));
+      }
+      constexpr int kShare = F == 16 ? 1 : (F == 4 ? 7 : 31);  // lanes holding one frame
+      if ((lane & kShare) == 0) {
+        pbest[frame * kWarps + warp] = pk[0].best;
+        pidx[frame * kWarps + warp] = pk[0].best_i;
+        pnan[frame * kWarps + warp] = pk[0].nan_i;
       }
     }
     __syncthreads();
