@@ -90,7 +90,7 @@ __device__ __forceinline__ void pick_halve(Pick32 (&pk)[N], int lane) {
 }
 
 template <int F>
-__global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, 2) lfq_rvq_kernel(const Args a) {
   extern __shared__ float sm[];
   const int D = a.d;
   float* r = sm;                        // [F][D]
@@ -114,6 +114,10 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
     }
     r[i] = v;
   }
+  // 2e, norms and codewords of frames past the CTA's rows stay zero: the
+  // distance and output phases run over all F frames without a guard, and
+  // those frames' results are never used
+  for (int i = tid; i < F * 25; i += kThreads) tw[i] = 0.0f;  // tw, nrm, z, cw
   __syncthreads();
   for (int s = 0; s < a.stages; ++s) {
     // ---- input projection: warp -> JW outputs z_j of FW frames (16 frames:
@@ -217,7 +221,7 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
         }
 #pragma unroll
         for (int f = 0; f < F; ++f) {
-          if (f < nf) {
+          {
             float t8[8];
 #pragma unroll
             for (int q = 0; q < 8; ++q) t8[q] = tw[f * 8 + q];
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kThreads) lfq_rvq_kernel(const Args a) {
       }
 #pragma unroll
       for (int f = 0; f < F; ++f) {
-        if (f < nf) {
+        {
           float c[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q) c[q] = cw[f * 8 + q];
