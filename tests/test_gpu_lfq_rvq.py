@@ -45,7 +45,9 @@ def _run(moss, cuda_device, x, params):
     (1, 256, 50, 8, 300),      # one clip: the transposed prepare order
     (5, 96, 1, 3, 64),         # streaming: one frame per clip
     (2, 256, 300, 4, 512),     # 4 frames per CTA
-    (3, 128, 800, 3, 256),     # 16 frames per CTA, a ragged last CTA
+    (2, 256, 301, 4, 512),     # 4 frames per CTA, the last CTA holds 2
+    (3, 128, 800, 3, 256),     # 16 frames per CTA, every CTA full
+    (3, 128, 801, 3, 256),     # 16 frames per CTA, the last CTA holds 3
     (2, 200, 5, 2, 1000),      # a width that is not a multiple of 32
 ])
 def test_lfq_rvq_matches_the_oracle_loop(moss, cuda_device, b, d, t, stages, k):
