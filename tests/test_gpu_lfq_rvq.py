@@ -70,3 +70,21 @@ def test_lfq_rvq_non_finite_frames(moss, cuda_device):
     codes, res, oc, ores = _run(moss, cuda_device, x, _params(d, stages, k, 3))
     assert np.array_equal(codes.reshape(stages, -1), oc)
     assert same_bits(res, ores)
+
+
+@pytest.mark.parametrize("t", [6, 2400])  # 1 and 16 frames per CTA
+def test_lfq_rvq_non_finite_code(moss, cuda_device, t):
+    """A NaN in one code of one stage makes that code's distance NaN for
+    every frame, so every frame takes it at that stage (first NaN wins);
+    the stages before it run on finite data.  Same codes and residual as
+    the oracle."""
+    b, d, stages, k = 1, 64, 3, 300
+    rng = np.random.default_rng(10)
+    x = rng.standard_normal((b, d, t)).astype(np.float32)
+    params = list(_params(d, stages, k, 4))
+    params[2] = params[2].copy()
+    params[2][1, 7, 3] = np.nan
+    codes, res, oc, ores = _run(moss, cuda_device, x, tuple(params))
+    assert np.array_equal(codes.reshape(stages, -1), oc)
+    assert (oc[1] == 7).all()
+    assert same_bits(res, ores)
