@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_tc_kernel(Args a) {
       int timed_out = 0;
       for (int t = 0; t < ntiles; ++t, ++q) {
         const int abuf = q & 1;
-        if (!timed_out && !mbar_wait(&sm.t_full[abuf], (q >> 1) & 1)) timed_out = 1;
+        if (!timed_out && !mbar_wait_spin(&sm.t_full[abuf], (q >> 1) & 1)) timed_out = 1;
         tc_fence_after();
         const uint32_t tcol =
             tmem + lane_base + static_cast<uint32_t>(abuf * 256 + part * cpp * 32);

@@ -61,6 +61,23 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, uint32_t pari
                                           uint64_t limit_ns = kWaitLimitNs) {
   return bounded_wait([&] { return mbar_try_wait(bar, parity); }, limit_ns);
 }
+// The same without the suspend hint: for waits on the critical path whose
+// waiters have nothing else to do (the epilogue waiting for an accumulator).
+__device__ __forceinline__ bool mbar_try_wait_spin(unsigned long long* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(unsigned long long* bar, uint32_t parity,
+                                               uint64_t limit_ns = kWaitLimitNs) {
+  return bounded_wait([&] { return mbar_try_wait_spin(bar, parity); }, limit_ns);
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
                                          unsigned long long* bar) {
   asm volatile(
